@@ -1,0 +1,420 @@
+"""Benchmark of the paged-attention hot path (libnvattn) on B200.
+
+Workload (one step = one decode layer-step): 256 sequences, Qwen3-8B
+attention shape (32 q heads, 8 kv heads, head_dim 128, 256-token blocks,
+BF16 KV), context lengths log-uniform in [1k, 32k] (seeded), block tables
+from a seeded permutation of a pool 10% larger than needed, Q/K/V N(0,1).
+A step stores the new token's K/V through the fused q/k RMSNorm + RoPE +
+slot_mapping kernel and then runs paged split-KV decode over all cached
+tokens.  With --gpus N the 8 kv heads are sharded N ways (rank r owns kv
+heads [r*8/N, (r+1)*8/N) and their q heads) -- strong scaling, no collective
+on the data path (--allgather adds the optional all-gather of head outputs).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  `value` is whole-job decode tokens/s with
+inputs resident in HBM; `e2e` is the same metric through the C ABI with the
+step's inputs copied from pinned host memory and the output copied back
+inside the timed region.  `--impl reference` times the CPU restatement of the
+reference's attention (its ggml dtype chain, paged form) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nano-vllm.cpp_b200", "python"))
+
+METRIC = "paged decode-attn tokens/s + HBM GB/s vs 8 TB/s; prefill-attn TFLOPS vs peak"
+WORKLOAD = "decode_qwen3_8b_attn_256seq_ctx1k-32k"
+N_SEQS, HQ, HKV, D, BS = 256, 32, 8, 128, 256
+SEED = 0
+
+# DRAM traffic per decode launch of this workload (dram__bytes_read.sum +
+# dram__bytes_write.sum), from the ncu capture summarised in
+# profiles/paged_decode_qwen3_8b_256seq.md; None until that capture exists.
+NCU_TRAFFIC_BYTES_N1 = None
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def workload(rng_seed=SEED):
+    rng = np.random.default_rng(rng_seed)
+    lens = np.exp(rng.uniform(math.log(1024), math.log(32768), N_SEQS)).astype(np.int64)
+    need = (lens + BS - 1) // BS
+    num_blocks = int(need.sum() * 1.1) + 1
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    max_blocks = int(need.max())
+    bt = np.full((N_SEQS, max_blocks), -1, np.int32)
+    off = 0
+    for s in range(N_SEQS):
+        bt[s, :need[s]] = perm[off:off + need[s]]
+        off += int(need[s])
+    return lens, bt, num_blocks
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def mark(self):
+        return len(self.rows)
+
+    def stop(self, since=0):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except Exception:
+                self.proc.kill()
+        rows = self.rows[since:] or self.rows[-3:]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_sample(lens, bt, k_host_fn, n_target_s=12.0):
+    """Times the oracle's GGML-mode paged decode (the reference's dtype chain)
+    on all host cores over the first sequences of the workload; returns
+    (tokens/s, n_seqs, seconds, cores)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    results = []
+    n = 2
+    while True:
+        kc, vc, btc, lc, q = k_host_fn(n)
+        p = O.params(n_q_heads=HQ, n_kv_heads=HKV, n_slots=kc.shape[1], n_threads=cores)
+        t0 = time.perf_counter()
+        O.paged_decode(p, O.MODE_GGML, 0, q, kc, vc, btc, lc)
+        dt = time.perf_counter() - t0
+        results.append((n, dt))
+        if dt >= n_target_s or n >= N_SEQS:
+            break
+        n = min(N_SEQS, max(n + 1, int(n * min(8.0, n_target_s / max(dt, 1e-3)))))
+    n, dt = results[-1]
+    return n / dt, n, dt, cores
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    lens, bt, _ = workload()
+    rng = np.random.default_rng(SEED + 1)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    # A pool of 128 physical blocks of N(0,1) bf16 K/V; the sample's block
+    # tables walk it cyclically (physical blocks may be shared, as prefix
+    # caching does), which keeps host set-up time independent of the sample.
+    POOL = 128
+    kpool = O.f32_to_bf16(rng.standard_normal((1, POOL * BS, HKV, D), dtype=np.float32))
+    vpool = O.f32_to_bf16(rng.standard_normal((1, POOL * BS, HKV, D), dtype=np.float32))
+
+    def host_case(n):
+        need = (lens[:n] + BS - 1) // BS
+        btc = np.full((n, bt.shape[1]), -1, np.int32)
+        o = 0
+        for s in range(n):
+            btc[s, :need[s]] = np.arange(o, o + need[s]) % POOL
+            o += int(need[s])
+        q = rng.standard_normal((n, HQ, D), dtype=np.float32)
+        return kpool, vpool, btc, lens[:n].astype(np.int32), q
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cores = os.cpu_count() or 1
+    # size one step so that warmup + steps take about two minutes in all
+    per_step = min(2.0, 120.0 / max(1, args.steps + args.warmup))
+    tps, n, dt, cores = cpu_sample(lens, bt, host_case, n_target_s=per_step)
+    kc, vc, btc, lc, q = host_case(n)
+    p = O.params(n_q_heads=HQ, n_kv_heads=HKV, n_slots=kc.shape[1], n_threads=cores)
+    for _ in range(args.warmup):
+        O.paged_decode(p, O.MODE_GGML, 0, q, kc, vc, btc, lc)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.paged_decode(p, O.MODE_GGML, 0, q, kc, vc, btc, lc)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = n * args.steps / total
+    sample = (f"first {n} of the {N_SEQS} sequences (sum L = {int(lc.sum())} tokens) per step; "
+              "oracle GGML mode: f16 Q/K/V, f32 online softmax, f16 V accumulator, paged form "
+              "(the reference's concat-all form is O(B*sum L))")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16/f32 (ggml chain)",
+            "data": "synthetic", "config": {"workload": WORKLOAD, "n_seqs": N_SEQS,
+                                            "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
+                                            "block_size": BS},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--allgather", action="store_true",
+                    help="all-gather the head-sharded outputs every step (NCCL)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    import nvattn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"note: WORLD_SIZE={world} but --gpus={args.gpus}; using WORLD_SIZE")
+    assert HKV % world == 0, "kv heads must divide across ranks"
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
+
+    hkv, hq = HKV // world, HQ // world
+    lens, bt_np, num_blocks = workload()
+    max_ctx = int(lens.max())
+    cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
+                              max_seqs=N_SEQS, max_context=max_ctx, max_position=max_ctx,
+                              device=local_rank)
+    h = nvattn.Handle(cfg)
+
+    # KV cache shard, generated on the device (N(0,1) -> bf16) in chunks.
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    n_slots = num_blocks * BS
+    kc = torch.empty((n_slots, hkv, D), dtype=torch.bfloat16, device=device)
+    vc = torch.empty_like(kc)
+    chunk = 1 << 16
+    for t in (kc, vc):
+        for i in range(0, n_slots, chunk):
+            t[i:i + chunk].copy_(torch.randn((min(chunk, n_slots - i), hkv, D), generator=gen,
+                                             device=device))
+    bt = torch.from_numpy(bt_np).to(device)
+    cl, pos_np, slot_np = nvattn.plan_decode(lens, bt_np)
+    ctx = torch.from_numpy(cl).to(device)
+    pos = torch.from_numpy(pos_np).to(device)
+    slots = torch.from_numpy(slot_np).to(device)
+    q0 = torch.randn((N_SEQS, hq, D), generator=gen, device=device)
+    k_new = torch.randn((N_SEQS, hkv, D), generator=gen, device=device)
+    v_new = torch.randn((N_SEQS, hkv, D), generator=gen, device=device)
+    w = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16)
+    q = torch.empty_like(q0)
+    out = torch.empty((N_SEQS, hq, D), device=device)
+    gathered = torch.empty((world, N_SEQS, hq, D), device=device) if args.allgather else None
+    stream = torch.cuda.current_stream(device)
+    kc16, vc16, w16 = kc.view(torch.int16), vc.view(torch.int16), w.view(torch.int16)
+
+    def step():
+        q.copy_(q0)  # the fused kernel writes q in place; keep every step identical
+        h.kv_store(0, q, k_new, v_new, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
+        ev_a.record(stream)
+        h.decode(0, q, kc16, vc16, bt, ctx, max_ctx, out, stream=stream)
+        ev_b.record(stream)
+        if gathered is not None:
+            dist.all_gather_into_tensor(gathered, out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(device)
+
+    ev_a = torch.cuda.Event(enable_timing=True)
+    ev_b = torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    h.check_device("warmup")
+    barrier()
+    mark = clocks.mark()
+
+    # ---- timed region: device-resident inputs ----
+    dec_ms = 0.0
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    pairs = []
+    t0.record(stream)
+    for _ in range(args.steps):
+        ev_a = torch.cuda.Event(enable_timing=True)
+        ev_b = torch.cuda.Event(enable_timing=True)
+        step()
+        pairs.append((ev_a, ev_b))
+    t1.record(stream)
+    barrier()
+    clk = clocks.stop(mark)
+    elapsed = t0.elapsed_time(t1) / 1e3
+    dec_ms = sum(a.elapsed_time(b) for a, b in pairs) / len(pairs)
+    h.check_device("timed region")
+
+    # ---- e2e: the same step through the C ABI with pinned host buffers ----
+    hq0 = q0.cpu().pin_memory()
+    hk = k_new.cpu().pin_memory()
+    hv = v_new.cpu().pin_memory()
+    hbt = bt.cpu().pin_memory()
+    hctx = ctx.cpu().pin_memory()
+    hpos = pos.cpu().pin_memory()
+    hslot = slots.cpu().pin_memory()
+    hout = torch.empty((N_SEQS, hq, D), dtype=torch.float32).pin_memory()
+    dk, dv = torch.empty_like(k_new), torch.empty_like(v_new)
+    dbt, dctx, dpos, dslot = (torch.empty_like(x) for x in (bt, ctx, pos, slots))
+    h2d = sum(x.numel() * x.element_size() for x in (hq0, hk, hv, hbt, hctx, hpos, hslot))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step():
+        q.copy_(hq0, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dbt.copy_(hbt, non_blocking=True)
+        dctx.copy_(hctx, non_blocking=True)
+        dpos.copy_(hpos, non_blocking=True)
+        dslot.copy_(hslot, non_blocking=True)
+        h.kv_store(0, q, dk, dv, w16, w16, dpos, dslot, q, kc16, vc16, stream=stream)
+        h.decode(0, q, kc16, vc16, dbt, dctx, max_ctx, out, stream=stream)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    e2e_elapsed = e0.elapsed_time(e1) / 1e3
+    h.check_device("e2e region")
+
+    times = torch.tensor([elapsed, e2e_elapsed, dec_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    elapsed, e2e_elapsed, dec_ms = times.tolist()
+
+    if rank == 0:
+        hbm_peak, _, peak_kind = peaks()
+        n_tok = N_SEQS * args.steps
+        kv_bytes = int(lens.sum()) * hkv * D * 2 * 2
+        alg_bytes = (kv_bytes + N_SEQS * hq * D * 4 * 2 + int(((lens + BS - 1) // BS).sum()) * 4
+                     + N_SEQS * 4)
+        achieved = alg_bytes / (dec_ms / 1e3) / 1e9
+        splits = 1
+        line = {
+            "metric": METRIC, "value": n_tok / elapsed, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16 KV, fp32 accumulate",
+            "data": "synthetic (seeded N(0,1) Q/K/V, log-uniform context lengths)",
+            "config": {"workload": WORKLOAD, "n_seqs": N_SEQS, "q_heads": HQ, "kv_heads": HKV,
+                       "head_dim": D, "block_size": BS, "sum_context": int(lens.sum()),
+                       "kv_gb_per_gpu": round(kv_bytes / 1e9, 3),
+                       "parallelism": f"kv-head shard x{world}",
+                       "l2": "inputs larger than L2 (KV cache >> 126 MB), no flush",
+                       "allgather": bool(args.allgather)},
+            "roofline": {"bound": "hbm", "kernel": "paged_decode (main + split combine)",
+                         "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_source": peak_kind,
+                         "traffic": NCU_TRAFFIC_BYTES_N1 if world == 1 else None,
+                         "algorithmic_bytes": alg_bytes, "decode_ms": dec_ms,
+                         "frac_of_8tbs": achieved / 8000.0},
+            "e2e": {"value": n_tok / e2e_elapsed, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * (2 + splits),
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            def host_case(n):
+                need = (lens[:n] + BS - 1) // BS
+                ids = np.concatenate([bt_np[s, :need[s]] for s in range(n)])
+                idx = torch.from_numpy(ids.astype(np.int64)).to(device)
+                rows = (idx[:, None] * BS + torch.arange(BS, device=device)[None]).reshape(-1)
+                kh = kc.index_select(0, rows).view(torch.int16).cpu().numpy().view(np.uint16)
+                vh = vc.index_select(0, rows).view(torch.int16).cpu().numpy().view(np.uint16)
+                btc = np.full((n, bt_np.shape[1]), -1, np.int32)
+                o = 0
+                for s in range(n):
+                    btc[s, :need[s]] = np.arange(o, o + need[s])
+                    o += int(need[s])
+                return (kh[None], vh[None], btc, lens[:n].astype(np.int32),
+                        q.cpu().numpy()[:n].copy())
+            tps, n, dt, cores = cpu_sample(lens, bt_np, host_case)
+            line["cpu_baseline"] = {
+                "value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                "sample": f"oracle GGML-mode paged decode of the first {n} sequences "
+                          f"({dt:.1f} s on {cores} threads)"}
+        print(json.dumps(line), flush=True)
+    h.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

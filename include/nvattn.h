@@ -1,0 +1,200 @@
+/*
+ * nvattn.h -- C ABI of libnvattn, the B200 (sm_100a) paged-attention hot path
+ * for nano-vllm.cpp.
+ *
+ * The library replaces, inside ModelRunner::Run (src/engine/model_runner.cpp:25),
+ * the host-side KV gather / store loops and the ggml attention node:
+ *
+ *   reference (nano-vllm.cpp)                              -> libnvattn
+ *   ---------------------------------------------------------------------------
+ *   Qwen3Model::Qwen3Model KV alloc (qwen3.cpp:186-213)   -> caller allocates the
+ *       [n_layer][num_blocks*block_size][n_kv_heads][head_dim] BF16 K and V
+ *       buffers (same layout); nvattn_create sizes only the workspace.
+ *   BuildNorm + ggml_rope_ext on q/k (qwen3.cpp:497-514, 627-641) and
+ *   StorePrefillKV / AppendDecodeKV + WriteKVToCache
+ *       (model_runner.cpp:248-296, 380-415; qwen3.cpp:411-422)
+ *                                                          -> nvattn_kv_store_qk_norm_rope
+ *   LoadHistoryKV + ReadKVFromCache + FillVarlenMask + decode concat +
+ *   BuildAttention (model_runner.cpp:219-243, 300-376; qwen3.cpp:424-435,
+ *   648-662, 377-405)                                      -> nvattn_paged_decode
+ *   FillCausalMask + prefill pad/permute + BuildAttention
+ *       (model_runner.cpp:188-217; qwen3.cpp:515-533, 377-405)
+ *                                                          -> nvattn_paged_prefill
+ *   PrepareInputs position/slot derivation (model_runner.cpp:138-186,
+ *   286-288, 332-333, 402-405)                              -> nvattn_plan_prefill /
+ *                                                             nvattn_plan_decode
+ *
+ * Conventions:
+ *   - Every pointer argument named *_dev is device memory on the handle's
+ *     device; every other pointer is host memory.  No pointer is retained
+ *     after a call returns.
+ *   - All device work is ordered on the stream argument (NULL = legacy
+ *     default stream).  Calls return after launching; they do not
+ *     synchronise.  Errors detected by the kernels (a block id or slot out of
+ *     range, a bounded wait that ran out) are recorded in a device status word
+ *     and reported by nvattn_get_error.
+ *   - No C++ exception crosses this interface.  A handle is not thread-safe;
+ *     distinct handles are independent.
+ *   - bf16 values are passed as uint16_t bit patterns.
+ */
+#ifndef NVATTN_H
+#define NVATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define NVATTN_API __attribute__((visibility("default")))
+#else
+#define NVATTN_API
+#endif
+
+#define NVATTN_VERSION_MAJOR 0
+#define NVATTN_VERSION_MINOR 1
+
+typedef enum nvattn_status {
+  NVATTN_OK = 0,
+  NVATTN_ERR_INVALID_ARG = 1,  /* bad pointer, size or shape */
+  NVATTN_ERR_OUT_OF_RANGE = 2, /* a block id / slot outside the cache */
+  NVATTN_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed */
+  NVATTN_ERR_TIMEOUT = 4,      /* a bounded device wait ran out */
+  NVATTN_ERR_UNSUPPORTED = 5,  /* shape not built (head_dim != 128, ...) */
+  NVATTN_ERR_NO_MEMORY = 6     /* workspace allocation failed */
+} nvattn_status;
+
+typedef enum nvattn_dtype {
+  NVATTN_DTYPE_F32 = 0,
+  NVATTN_DTYPE_BF16 = 1
+} nvattn_dtype;
+
+/* Same type as cudaStream_t, without pulling in CUDA headers. */
+typedef struct CUstream_st* nvattn_stream_t;
+
+typedef struct nvattn_config {
+  int n_layer;          /* Qwen3Hparams::n_layer (qwen3.h:32) */
+  int n_q_heads;        /* query heads served by this handle */
+  int n_kv_heads;       /* KV heads held in this handle's cache */
+  int head_dim;         /* 128 (only value built) */
+  int block_size;       /* Config::kvcache_block_size, 256 (only value built) */
+  int64_t num_blocks;   /* physical blocks per layer */
+  float rms_eps;        /* 1e-6 */
+  float rope_theta;     /* rope_freq_base, 1e6 */
+  float rope_freq_scale;  /* 1 */
+  float rope_ext_factor;  /* 1 */
+  float rope_attn_factor; /* 1 */
+  float rope_beta_fast;   /* 32 */
+  float rope_beta_slow;   /* 1 */
+  int rope_n_ctx_orig;  /* n_ctx passed to ggml_rope_ext (40960 for Qwen3) */
+  float scale;          /* softmax scale, 1/sqrt(head_dim) */
+  int max_position;     /* RoPE table covers positions [0, max_position) */
+  int max_seqs;         /* largest n_seqs of any call */
+  int max_context;      /* largest context length of any call */
+  int device;           /* CUDA device ordinal */
+} nvattn_config;
+
+typedef struct nvattn_handle nvattn_handle;
+
+/* ---- lifetime --------------------------------------------------------- */
+
+/* Qwen3-0.6B defaults (Qwen3Hparams, qwen3.h:30-56; Config, config.h:5-15). */
+NVATTN_API void nvattn_config_init_qwen3(nvattn_config* cfg);
+
+/* Validates cfg, builds the RoPE cos/sin table (ggml's float recurrence,
+ * computed on the host once and copied to the device) and allocates the
+ * split-KV workspace and status word.  Replaces the KV/backend set-up of
+ * Qwen3Model::Qwen3Model (qwen3.cpp:99-108, 186-213), whose failures throw;
+ * here they return a status. */
+NVATTN_API nvattn_status nvattn_create(const nvattn_config* cfg, nvattn_handle** out);
+NVATTN_API nvattn_status nvattn_destroy(nvattn_handle* h);
+
+NVATTN_API const char* nvattn_status_string(nvattn_status s);
+NVATTN_API void nvattn_version(int* major, int* minor);
+
+/* Synchronises the handle's device, returns the first error recorded by a
+ * kernel since the last call (NVATTN_OK if none) and clears it.  *detail
+ * (nullable) receives the offending value (block id, slot or wait site). */
+NVATTN_API nvattn_status nvattn_get_error(nvattn_handle* h, int64_t* detail);
+
+/* ---- host-side planning (no device work) ------------------------------- */
+
+/* ModelRunner::PrepareInputs for a prefill batch (model_runner.cpp:138-186)
+ * plus the slot derivation of StorePrefillKV (:286-288).
+ * Inputs per sequence s: seq_lens[s] (Sequence::SequenceLen),
+ * num_cached[s] (Sequence::GetNumCachedTokens), block_tables [n_seqs][max_blocks]
+ * (Sequence::block_table_).  Outputs: cu_q_lens[n_seqs+1], q_starts[n_seqs],
+ * context_lens[n_seqs], and for each of the cu_q_lens[n_seqs] new tokens
+ * positions[] and slot_mapping[] (capacity max_tokens).
+ * Returns INVALID_ARG if a sequence has no new token or too few blocks. */
+NVATTN_API nvattn_status nvattn_plan_prefill(int n_seqs, const int64_t* seq_lens,
+                                  const int64_t* num_cached,
+                                  const int32_t* block_tables, int max_blocks,
+                                  int block_size, int max_tokens,
+                                  int32_t* cu_q_lens, int32_t* q_starts,
+                                  int32_t* context_lens, int32_t* positions,
+                                  int32_t* slot_mapping);
+
+/* Decode batch: one new token per sequence at position seq_lens[s]-1
+ * (model_runner.cpp:161-165, 402-405). */
+NVATTN_API nvattn_status nvattn_plan_decode(int n_seqs, const int64_t* seq_lens,
+                                 const int32_t* block_tables, int max_blocks,
+                                 int block_size, int32_t* context_lens,
+                                 int32_t* positions, int32_t* slot_mapping);
+
+/* ---- device kernels ----------------------------------------------------- */
+
+/* Fused per-head q/k RMSNorm (weight = q_norm / k_norm), NEOX RoPE at
+ * positions[t], and the BF16 store of K (normed, rotated) and V (raw) into
+ * layer `layer` of the paged cache at slot_mapping[t] (slot < 0: not stored).
+ *   q_dev   [n_tokens][n_q_heads][head_dim]  f32
+ *   k_dev, v_dev [n_tokens][n_kv_heads][head_dim] f32
+ *   q_norm_w_dev, k_norm_w_dev [head_dim] bf16
+ *   q_out_dev [n_tokens][n_q_heads][head_dim] in q_out_dtype (may alias q_dev
+ *            when f32)
+ *   k_cache_dev, v_cache_dev: cache base (all layers).
+ * The stored K/V bytes equal ggml_fp32_to_bf16_row of the reference's f32
+ * graph outputs (round to nearest even). */
+NVATTN_API nvattn_status nvattn_kv_store_qk_norm_rope(
+    nvattn_handle* h, int layer, int n_tokens, const float* q_dev,
+    const float* k_dev, const float* v_dev, const uint16_t* q_norm_w_dev,
+    const uint16_t* k_norm_w_dev, const int32_t* positions_dev,
+    const int32_t* slot_mapping_dev, void* q_out_dev, nvattn_dtype q_out_dtype,
+    uint16_t* k_cache_dev, uint16_t* v_cache_dev, nvattn_stream_t stream);
+
+/* Paged GQA decode: for each sequence s, one query row per q head attends
+ * keys [0, context_lens[s]) of layer `layer`, read through
+ * block_tables[s][t / block_size].  The new token's K/V must already be in
+ * the cache (nvattn_kv_store_qk_norm_rope first).
+ *   q_dev   [n_seqs][n_q_heads][head_dim] f32
+ *   out_dev [n_seqs][n_q_heads][head_dim] f32
+ * max_context_len: host-side upper bound of context_lens (sizes the grid).
+ * Split-KV partial results go to the handle's workspace. */
+NVATTN_API nvattn_status nvattn_paged_decode(
+    nvattn_handle* h, int layer, int n_seqs, const float* q_dev,
+    const uint16_t* k_cache_dev, const uint16_t* v_cache_dev,
+    const int32_t* block_tables_dev, int max_blocks,
+    const int32_t* context_lens_dev, int max_context_len, float* out_dev,
+    nvattn_stream_t stream);
+
+/* Causal paged prefill, prefix aware (also serves chunked prefill): sequence
+ * s owns query rows [cu_q_lens[s], cu_q_lens[s+1]) at positions
+ * q_starts[s] + i; a row at position P attends keys [0, P] of layer `layer`
+ * through the block table.  The rows' own K/V must already be stored.
+ *   q_dev   [n_tokens][n_q_heads][head_dim] bf16
+ *   out_dev [n_tokens][n_q_heads][head_dim] f32
+ * max_q_len: host-side upper bound of the per-sequence query count. */
+NVATTN_API nvattn_status nvattn_paged_prefill(
+    nvattn_handle* h, int layer, int n_seqs, int n_tokens,
+    const uint16_t* q_dev, const int32_t* cu_q_lens_dev,
+    const int32_t* q_starts_dev, const int32_t* context_lens_dev,
+    const int32_t* block_tables_dev, int max_blocks, int max_q_len,
+    const uint16_t* k_cache_dev, const uint16_t* v_cache_dev, float* out_dev,
+    nvattn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NVATTN_H */

@@ -1,0 +1,81 @@
+// internal.h -- host-side state shared by the libnvattn translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "nvattn.h"
+#ifdef __CUDACC__
+#include "common.cuh"
+#else
+namespace nvattn {
+struct DeviceStatus;
+}
+#endif
+
+// One cached TMA descriptor for a cache buffer (keyed by its base pointer and
+// the box it was encoded with).
+struct NvattnTensorMapEntry {
+  const void* base;
+  int box_d;     // inner box extent (elements)
+  int box_rows;  // tokens per box
+  int swizzle;   // CUtensorMapSwizzle value
+  CUtensorMap map;
+};
+
+struct nvattn_handle {
+  nvattn_config cfg;
+  int64_t n_slots;  // num_blocks * block_size (slots per layer)
+  int sm_count;
+
+  float* rope_table_dev = nullptr;  // [max_position][head_dim/2][2] (cos, sin)
+  nvattn::DeviceStatus* status_dev = nullptr;
+
+  // split-KV workspace for decode
+  float* ws_o = nullptr;   // [max_seqs][n_kv_heads][max_splits][G][head_dim]
+  float* ws_ml = nullptr;  // [max_seqs][n_kv_heads][max_splits][G][2]
+  int max_splits = 0;
+
+  std::vector<NvattnTensorMapEntry> maps;
+};
+
+namespace nvattn {
+
+// Returns a TMA descriptor over a whole K or V cache (all layers):
+// dims {head_dim, n_kv_heads, n_layer*n_slots}, bf16, box {box_d, 1, box_rows}.
+nvattn_status get_cache_tensor_map(nvattn_handle* h, const void* base, int box_d,
+                                   int box_rows, int swizzle, const CUtensorMap** out);
+
+// Generic 3-D bf16 tensor map (used for Q in prefill).
+nvattn_status encode_tensor_map_3d(CUtensorMap* map, const void* base, uint64_t d0,
+                                   uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                                   uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
+                                   uint32_t box2, int swizzle);
+
+nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const float* q,
+                              const float* k, const float* v, const uint16_t* qw,
+                              const uint16_t* kw, const int32_t* positions,
+                              const int32_t* slots, void* q_out, nvattn_dtype q_out_dtype,
+                              uint16_t* k_cache, uint16_t* v_cache, cudaStream_t stream);
+
+nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const float* q,
+                                  const uint16_t* k_cache, const uint16_t* v_cache,
+                                  const int32_t* block_tables, int max_blocks,
+                                  const int32_t* context_lens, int max_context_len,
+                                  float* out, cudaStream_t stream);
+
+nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int n_tokens,
+                                   const uint16_t* q, const int32_t* cu_q,
+                                   const int32_t* q_starts, const int32_t* context_lens,
+                                   const int32_t* block_tables, int max_blocks,
+                                   int max_q_len, const uint16_t* k_cache,
+                                   const uint16_t* v_cache, float* out,
+                                   cudaStream_t stream);
+
+// Host RoPE table: ggml's rope cache recurrence for positions [0, n_pos).
+void build_rope_table(const nvattn_config& cfg, int n_pos, float* table);
+
+}  // namespace nvattn

@@ -1,0 +1,89 @@
+// attention_runner.h -- C++ host layer above the libnvattn C ABI, shaped like
+// the part of nano-vllm.cpp's engine::ModelRunner that the attention hot path
+// replaces (src/include/engine/model_runner.h:14-72).
+//
+// The reference's ModelRunner::Run (model_runner.cpp:25-136) builds inputs,
+// runs the ggml graph, and moves K/V between the graph and the BF16 cache on
+// the host (StorePrefillKV / LoadHistoryKV / AppendDecodeKV).  With the graph
+// cut around the attention node, the runner instead:
+//   1. PrepareInputs: derives positions, slot mapping, block tables and
+//      context lengths from the scheduled sequences (model_runner.cpp:138-186)
+//      and uploads them once per step;
+//   2. per layer, RunAttentionLayer: fused q/k norm + RoPE + KV store, then
+//      paged decode or prefill attention, all on the device.
+// Error behaviour follows the reference: the constructor throws
+// std::runtime_error (as Qwen3Model's does, qwen3.cpp:33-35, 106-108);
+// per-step calls return false where ModelRunner::Run returns {}
+// (model_runner.cpp:46-49, 67).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "nvattn.h"
+
+namespace nvattn_host {
+
+// The fields of engine::Sequence the attention path reads
+// (src/include/engine/sequence.h:19-88).
+struct SequenceView {
+  std::vector<size_t> block_table;  // Sequence::GetBlockTable()
+  size_t seq_len = 0;               // Sequence::SequenceLen()
+  size_t num_cached_tokens = 0;     // Sequence::GetNumCachedTokens()
+};
+
+class AttentionRunner {
+ public:
+  explicit AttentionRunner(const nvattn_config& cfg);
+  ~AttentionRunner();
+  AttentionRunner(const AttentionRunner&) = delete;
+  AttentionRunner& operator=(const AttentionRunner&) = delete;
+
+  // Builds and uploads this step's attention metadata.  Returns false on
+  // invalid input (no block for a position, too many tokens) or CUDA failure.
+  bool PrepareInputs(const std::vector<SequenceView*>& seqs, bool is_prefill,
+                     cudaStream_t stream);
+
+  // One layer of the cut graph: q [n_tokens][Hq][d] f32 (overwritten with the
+  // normed, rotated q), k/v [n_tokens][Hkv][d] f32 (graph projections), the
+  // layer's q/k norm weights (bf16 [d]), and the BF16 caches (all layers).
+  // Writes attention output [n_tokens][Hq][d] f32.
+  bool RunAttentionLayer(int layer, float* q, const float* k, const float* v,
+                         const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                         uint16_t* k_cache, uint16_t* v_cache, float* out,
+                         cudaStream_t stream);
+
+  int NumTokens() const { return n_tokens_; }
+  int NumSeqs() const { return n_seqs_; }
+  bool IsPrefill() const { return is_prefill_; }
+  nvattn_handle* Handle() const { return handle_; }
+  // Host copies of the last plan (for inspection and tests).
+  const std::vector<int32_t>& Positions() const { return positions_; }
+  const std::vector<int32_t>& SlotMapping() const { return slots_; }
+
+ private:
+  bool Reserve(size_t n_tokens, size_t n_seqs, size_t max_blocks);
+
+  nvattn_config cfg_;
+  nvattn_handle* handle_ = nullptr;
+  bool is_prefill_ = false;
+  int n_tokens_ = 0, n_seqs_ = 0, max_blocks_ = 0, max_q_len_ = 0, max_context_ = 0;
+
+  std::vector<int32_t> positions_, slots_, block_tables_, context_lens_, cu_q_, q_starts_;
+
+  // device buffers (owned)
+  size_t cap_tokens_ = 0, cap_seqs_ = 0, cap_blocks_ = 0;
+  int32_t* d_positions_ = nullptr;
+  int32_t* d_slots_ = nullptr;
+  int32_t* d_block_tables_ = nullptr;
+  int32_t* d_context_lens_ = nullptr;
+  int32_t* d_cu_q_ = nullptr;
+  int32_t* d_q_starts_ = nullptr;
+  uint16_t* d_q_bf16_ = nullptr;
+};
+
+}  // namespace nvattn_host

@@ -1,0 +1,237 @@
+"""Python binding of libnvattn through its C ABI (include/nvattn.h), via ctypes.
+
+This is the ctypes stub a Python caller (tests, benchmarks) uses; tensors are
+passed as raw device pointers, so no framework type crosses the ABI.  The
+library is loaded from nano-vllm.cpp_b200/lib/libnvattn.so and there is no
+fallback: a missing library raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.dirname(_HERE)
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libnvattn.so")
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_OUT_OF_RANGE = 2
+ERR_CUDA = 3
+ERR_TIMEOUT = 4
+ERR_UNSUPPORTED = 5
+ERR_NO_MEMORY = 6
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+
+EXPORTED = [
+    "nvattn_config_init_qwen3", "nvattn_create", "nvattn_destroy", "nvattn_status_string",
+    "nvattn_version", "nvattn_get_error", "nvattn_plan_prefill", "nvattn_plan_decode",
+    "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
+]
+
+
+class NvattnError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {status_string(status)} ({status})")
+
+
+class Config(ctypes.Structure):
+    _fields_ = [
+        ("n_layer", ctypes.c_int),
+        ("n_q_heads", ctypes.c_int),
+        ("n_kv_heads", ctypes.c_int),
+        ("head_dim", ctypes.c_int),
+        ("block_size", ctypes.c_int),
+        ("num_blocks", ctypes.c_int64),
+        ("rms_eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float),
+        ("rope_freq_scale", ctypes.c_float),
+        ("rope_ext_factor", ctypes.c_float),
+        ("rope_attn_factor", ctypes.c_float),
+        ("rope_beta_fast", ctypes.c_float),
+        ("rope_beta_slow", ctypes.c_float),
+        ("rope_n_ctx_orig", ctypes.c_int),
+        ("scale", ctypes.c_float),
+        ("max_position", ctypes.c_int),
+        ("max_seqs", ctypes.c_int),
+        ("max_context", ctypes.c_int),
+        ("device", ctypes.c_int),
+    ]
+
+
+_lib = None
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+
+
+def lib():
+    """Loads libnvattn.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"libnvattn not built: {LIB_PATH} (run __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        L.nvattn_config_init_qwen3.argtypes = [ctypes.POINTER(Config)]
+        L.nvattn_config_init_qwen3.restype = None
+        L.nvattn_create.argtypes = [ctypes.POINTER(Config), ctypes.POINTER(_vp)]
+        L.nvattn_destroy.argtypes = [_vp]
+        L.nvattn_status_string.argtypes = [_i32]
+        L.nvattn_status_string.restype = ctypes.c_char_p
+        L.nvattn_version.argtypes = [ctypes.POINTER(_i32), ctypes.POINTER(_i32)]
+        L.nvattn_version.restype = None
+        L.nvattn_get_error.argtypes = [_vp, ctypes.POINTER(_i64)]
+        L.nvattn_plan_prefill.argtypes = [_i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp,
+                                          _vp, _vp]
+        L.nvattn_plan_decode.argtypes = [_i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp]
+        L.nvattn_kv_store_qk_norm_rope.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
+                                                   _vp, _vp, _i32, _vp, _vp, _vp]
+        L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
+                                          _vp, _vp]
+        L.nvattn_paged_prefill.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32,
+                                           _i32, _vp, _vp, _vp, _vp]
+        # every other entry point returns nvattn_status (ctypes' default c_int)
+        _lib = L
+    return _lib
+
+
+def status_string(s: int) -> str:
+    return lib().nvattn_status_string(int(s)).decode()
+
+
+def version():
+    a, b = _i32(), _i32()
+    lib().nvattn_version(ctypes.byref(a), ctypes.byref(b))
+    return a.value, b.value
+
+
+def qwen3_config(**overrides) -> Config:
+    c = Config()
+    lib().nvattn_config_init_qwen3(ctypes.byref(c))
+    for k, v in overrides.items():
+        setattr(c, k, v)
+    return c
+
+
+def _check(st: int, what: str):
+    if st != OK:
+        raise NvattnError(st, what)
+
+
+def _ptr(t):
+    """Raw address of a tensor-like (anything with data_ptr()) or None."""
+    if t is None:
+        return None
+    return _vp(t.data_ptr())
+
+
+def _np_ptr(a):
+    return a.ctypes.data_as(_vp)
+
+
+def _stream_ptr(stream):
+    if stream is None:
+        return None
+    return _vp(int(stream.cuda_stream) if hasattr(stream, "cuda_stream") else int(stream))
+
+
+class Handle:
+    """One libnvattn handle (one device)."""
+
+    def __init__(self, cfg: Config):
+        self.cfg = cfg
+        h = _vp()
+        _check(lib().nvattn_create(ctypes.byref(cfg), ctypes.byref(h)), "nvattn_create")
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().nvattn_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def get_error(self):
+        """Returns (status, detail) recorded by kernels since the last call (syncs)."""
+        d = _i64()
+        st = lib().nvattn_get_error(self._h, ctypes.byref(d))
+        return st, d.value
+
+    def check_device(self, what="kernel"):
+        st, d = self.get_error()
+        if st != OK:
+            raise NvattnError(st, f"{what} (detail {d})")
+
+    def kv_store(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, q_out, k_cache,
+                 v_cache, stream=None, check=True):
+        import torch
+        dt = DTYPE_BF16 if q_out.dtype == torch.bfloat16 else DTYPE_F32
+        st = lib().nvattn_kv_store_qk_norm_rope(
+            self._h, layer, positions.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm_w),
+            _ptr(k_norm_w), _ptr(positions), _ptr(slots), _ptr(q_out), dt, _ptr(k_cache),
+            _ptr(v_cache), _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_kv_store_qk_norm_rope")
+        return st
+
+    def decode(self, layer, q, k_cache, v_cache, block_tables, context_lens, max_context_len,
+               out, stream=None, check=True):
+        st = lib().nvattn_paged_decode(
+            self._h, layer, context_lens.shape[0], _ptr(q), _ptr(k_cache), _ptr(v_cache),
+            _ptr(block_tables), block_tables.shape[1], _ptr(context_lens), int(max_context_len),
+            _ptr(out), _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_paged_decode")
+        return st
+
+    def prefill(self, layer, q, cu_q, q_starts, context_lens, block_tables, max_q_len, k_cache,
+                v_cache, out, stream=None, check=True):
+        st = lib().nvattn_paged_prefill(
+            self._h, layer, context_lens.shape[0], q.shape[0], _ptr(q), _ptr(cu_q),
+            _ptr(q_starts), _ptr(context_lens), _ptr(block_tables), block_tables.shape[1],
+            int(max_q_len), _ptr(k_cache), _ptr(v_cache), _ptr(out), _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_paged_prefill")
+        return st
+
+
+def plan_prefill(seq_lens, num_cached, block_tables, block_size=256):
+    """Host planner (no device work): numpy in, numpy out."""
+    import numpy as np
+    seq_lens = np.ascontiguousarray(seq_lens, dtype=np.int64)
+    num_cached = np.ascontiguousarray(num_cached, dtype=np.int64)
+    bt = np.ascontiguousarray(block_tables, dtype=np.int32)
+    n = seq_lens.shape[0]
+    cap = int(np.maximum(seq_lens - num_cached, 1).sum())
+    cu = np.zeros(n + 1, np.int32)
+    qs = np.zeros(n, np.int32)
+    cl = np.zeros(n, np.int32)
+    pos = np.zeros(cap, np.int32)
+    slot = np.zeros(cap, np.int32)
+    st = lib().nvattn_plan_prefill(n, _np_ptr(seq_lens), _np_ptr(num_cached), _np_ptr(bt),
+                                   bt.shape[1], block_size, cap, _np_ptr(cu), _np_ptr(qs),
+                                   _np_ptr(cl), _np_ptr(pos), _np_ptr(slot))
+    _check(st, "nvattn_plan_prefill")
+    T = int(cu[-1])
+    return cu, qs, cl, pos[:T], slot[:T]
+
+
+def plan_decode(seq_lens, block_tables, block_size=256):
+    import numpy as np
+    seq_lens = np.ascontiguousarray(seq_lens, dtype=np.int64)
+    bt = np.ascontiguousarray(block_tables, dtype=np.int32)
+    n = seq_lens.shape[0]
+    cl = np.zeros(n, np.int32)
+    pos = np.zeros(n, np.int32)
+    slot = np.zeros(n, np.int32)
+    st = lib().nvattn_plan_decode(n, _np_ptr(seq_lens), _np_ptr(bt), bt.shape[1], block_size,
+                                  _np_ptr(cl), _np_ptr(pos), _np_ptr(slot))
+    _check(st, "nvattn_plan_decode")
+    return cl, pos, slot

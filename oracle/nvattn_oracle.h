@@ -1,0 +1,133 @@
+/*
+ * nvattn_oracle.h -- CPU oracle for the paged-attention hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the shipped library links, loads or
+ * calls this code; only the test-suite, the smoke check and the CPU-baseline
+ * leg of the benchmark use it, as the checker.
+ *
+ * It restates, in plain C, what nano-vllm.cpp computes on this path:
+ *   - src/models/qwen3.cpp:326-353   BuildNorm (ggml_rms_norm + ggml_mul)
+ *   - src/models/qwen3.cpp:497-514   q/k norm + NEOX RoPE (ggml_rope_ext)
+ *   - src/models/qwen3.cpp:377-405   BuildAttention (ggml_flash_attn_ext,
+ *                                    K/V cast F32->F16, scale 1/sqrt(128))
+ *   - src/models/qwen3.cpp:407-435   KV cache layout / slot addressing
+ *   - src/engine/model_runner.cpp:248-415  StorePrefillKV / LoadHistoryKV /
+ *                                    AppendDecodeKV (fp32<->bf16 rows)
+ *   - src/engine/model_runner.cpp:219-243  FillVarlenMask (decode concat)
+ * The arithmetic itself lives in ggml (github.com/ggml-org/ggml), a git
+ * submodule that the reference does not vendor; its pinned commit is not
+ * recoverable.  The ggml CPU algorithms used here (rms_norm, rope cache with
+ * the YaRN ramp, flash_attn_ext with an F16 V accumulator, fp32<->bf16/f16
+ * conversions) are restated from ggml's published source, scalar paths.
+ *
+ * PARITY AGAINST THE REFERENCE IS UNPINNED: the reference ships no tests,
+ * fixtures or golden vectors and cannot be built here (ggml absent).  The
+ * oracle is pinned instead by known-answer tests (IEEE conversion edge cases,
+ * single-key / constant-key attention, RoPE at position 0) and by the
+ * bit-identity of the reference's own concat-all decode algorithm
+ * (orc_concat_decode_ggml) with the paged restatement.
+ *
+ * Two attention modes:
+ *   ORC_MODE_TRUTH  fp64 scores/softmax/accumulation on the exact inputs.
+ *   ORC_MODE_GGML   the reference's dtype chain: Q f32->f16, K/V bf16->f32->f16,
+ *                   f32 scores, f32 online softmax, f16 V accumulator.
+ *
+ * Build with -ffp-contract=off: every product and sum is rounded separately,
+ * as in ggml's scalar code.
+ */
+#ifndef NVATTN_ORACLE_H
+#define NVATTN_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { ORC_MODE_TRUTH = 0, ORC_MODE_GGML = 1 };
+
+typedef struct orc_params {
+  int n_q_heads;      /* Hq */
+  int n_kv_heads;     /* Hkv */
+  int head_dim;       /* d (128 for Qwen3) */
+  int block_size;     /* tokens per KV block (256) */
+  int64_t n_slots;    /* num_blocks * block_size, slots per layer */
+  float rms_eps;      /* 1e-6 */
+  float rope_theta;   /* 1e6 */
+  float rope_freq_scale;
+  float rope_ext_factor;
+  float rope_attn_factor;
+  float rope_beta_fast;
+  float rope_beta_slow;
+  int rope_n_ctx_orig; /* Qwen3Hparams::n_ctx, passed as n_ctx_orig */
+  float scale;         /* softmax scale, 1/sqrt(d) */
+  int n_threads;       /* 0 = all online cores */
+} orc_params;
+
+/* ---- scalar conversions (ggml semantics) ---- */
+uint16_t orc_f32_to_bf16(float f);
+float orc_bf16_to_f32(uint16_t h);
+uint16_t orc_f32_to_f16(float f);
+float orc_f16_to_f32(uint16_t h);
+void orc_f32_to_bf16_row(const float* x, uint16_t* y, int64_t n);
+void orc_bf16_to_f32_row(const uint16_t* x, float* y, int64_t n);
+
+/* ---- RoPE ---- */
+void orc_rope_corr_dims(int n_dims, int n_ctx_orig, float freq_base,
+                        float beta_fast, float beta_slow, float dims[2]);
+/* cos/sin for one position: cache[2*i] = cos(theta_i), cache[2*i+1] = sin. */
+void orc_rope_cache(int pos, const orc_params* p, float* cache);
+/* Whole table [n_pos][d/2][2] (the library builds the same table itself). */
+void orc_rope_table(int n_pos, const orc_params* p, float* table);
+
+/* ---- fused q/k RMSNorm + NEOX RoPE + paged KV store ---- */
+/* q [T][Hq][d], k/v [T][Hkv][d] f32; weights bf16 [d]; positions/slots [T].
+ * q_out [T][Hq][d] f32 (post norm+rope); k_out nullable [T][Hkv][d] f32.
+ * Rows with slot < 0 are not stored. */
+void orc_qk_norm_rope_store(const orc_params* p, int layer, int n_tokens,
+                            const float* q, const float* k, const float* v,
+                            const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                            const int32_t* positions, const int32_t* slots,
+                            float* q_out, float* k_out,
+                            uint16_t* k_cache, uint16_t* v_cache);
+
+/* ---- paged decode: one query token per sequence, keys [0, context_len) ----
+ * q [B][Hq][d] f32, out [B][Hq][d] f32.  block_tables [B][max_blocks].
+ * new_k/new_v (nullable, [B][Hkv][d] f32): in GGML mode the newest key
+ * (index context_len-1) is taken from these f32 rows (cast to f16) instead of
+ * the bf16 cache, as in the reference's decode graph concat. */
+void orc_paged_decode(const orc_params* p, int mode, int layer, int n_seqs,
+                      const float* q, const uint16_t* k_cache,
+                      const uint16_t* v_cache, const int32_t* block_tables,
+                      int max_blocks, const int32_t* context_lens,
+                      const float* new_k, const float* new_v, float* out);
+
+/* ---- paged prefill: causal, prefix aware ----
+ * Sequence s owns query rows [cu_q[s], cu_q[s+1]) at positions
+ * q_start[s] + i; a row at position P attends keys [0, P].  Keys come from the
+ * cache through the block table.  new_k/new_v (nullable, [T][Hkv][d] f32):
+ * in GGML mode keys at positions >= q_start[s] use these f32 rows. */
+void orc_paged_prefill(const orc_params* p, int mode, int layer, int n_seqs,
+                       const float* q, const int32_t* cu_q,
+                       const int32_t* q_start, const int32_t* context_lens,
+                       const int32_t* block_tables, int max_blocks,
+                       const uint16_t* k_cache, const uint16_t* v_cache,
+                       const float* new_k, const float* new_v, float* out);
+
+/* ---- the reference's own decode algorithm (GGML mode only) ----
+ * Gathers every sequence's history (context_len-1 rows) into one
+ * concatenated K/V, appends the new rows after all histories, pads to 256 and
+ * runs masked attention over the whole buffer for each query row
+ * (model_runner.cpp:85-124,219-243,298-376; qwen3.cpp:573-662).
+ * O(B * sum(L)); small cases only. */
+void orc_concat_decode_ggml(const orc_params* p, int layer, int n_seqs,
+                            const float* q, const uint16_t* k_cache,
+                            const uint16_t* v_cache,
+                            const int32_t* block_tables, int max_blocks,
+                            const int32_t* context_lens, const float* new_k,
+                            const float* new_v, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NVATTN_ORACLE_H */

@@ -1,0 +1,110 @@
+"""GPU parity of nvattn_kv_store_qk_norm_rope against the oracle: the normed,
+rotated q (f32 and bf16) and the bf16 K/V cache rows must match bit for bit
+(StorePrefillKV / AppendDecodeKV semantics, model_runner.cpp:248-415)."""
+import numpy as np
+import pytest
+
+import make_golden
+import nvattn
+import oracle as O
+from gpu_util import dev, handle, host_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def run_store(h, layer, q, k, v, qw, kw, pos, slots, n_slots, Hkv, n_layer=1, q_bf16=False,
+              cache_fill=0):
+    import torch
+    kc = torch.full((n_layer, n_slots, Hkv, 128), cache_fill, dtype=torch.int16, device="cuda")
+    vc = torch.full_like(kc, cache_fill)
+    dq = dev(q)
+    qo = torch.empty(q.shape, dtype=torch.bfloat16 if q_bf16 else torch.float32, device="cuda")
+    h.kv_store(layer, dq, dev(k), dev(v), dev(qw), dev(kw), dev(pos), dev(slots), qo, kc, vc)
+    torch.cuda.synchronize()
+    return qo, kc, vc
+
+
+def test_golden_fixture_bit_exact(cuda):
+    fx = np.load(make_golden.__file__.replace("make_golden.py", "kv_store_qwen3_0p6b.npz"))
+    q, k, v, qw, kw, pos, slots = make_golden.store_inputs()
+    assert np.array_equal(make_golden._digest(q, k, v, qw, kw, pos, slots), fx["inputs_sha256"])
+    h = handle(16, 8, 2)
+    qo, kc, vc = run_store(h, 0, q, k, v, qw, kw, pos, slots, 512, 8)
+    h.check_device()
+    assert np.array_equal(qo.cpu().numpy().view(np.uint32), fx["q_out"].view(np.uint32))
+    assert np.array_equal(host_bits(kc)[0, slots], fx["k_rows"])
+    assert np.array_equal(host_bits(vc)[0, slots], fx["v_rows"])
+
+
+@pytest.mark.parametrize("Hq,Hkv,T", [(16, 8, 3000), (32, 8, 777), (8, 1, 513), (64, 8, 129)])
+@pytest.mark.parametrize("q_bf16", [False, True])
+def test_random_tokens_bit_exact(cuda, Hq, Hkv, T, q_bf16):
+    rng = np.random.default_rng(Hq * 1000 + T)
+    n_layer, layer, num_blocks = 3, 1, (T + 255) // 256 + 2
+    n_slots = num_blocks * 256
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = (rng.standard_normal((T, Hkv, 128)) * rng.uniform(0.01, 30, (T, Hkv, 1))).astype(np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    qw = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(128)).astype(np.float32))
+    kw = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(128)).astype(np.float32))
+    pos = rng.integers(0, 40960, T).astype(np.int32)
+    slots = rng.permutation(n_slots)[:T].astype(np.int32)
+    h = handle(Hq, Hkv, num_blocks, n_layer=n_layer)
+    qo, kc, vc = run_store(h, layer, q, k, v, qw, kw, pos, slots, n_slots, Hkv, n_layer, q_bf16)
+    h.check_device()
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=n_slots)
+    okc = np.zeros((n_layer, n_slots, Hkv, 128), np.uint16)
+    ovc = np.zeros_like(okc)
+    oq = O.qk_norm_rope_store(p, layer, q, k, v, qw, kw, pos, slots, okc, ovc)
+    if q_bf16:
+        import torch
+        assert np.array_equal(host_bits(qo.view(torch.int16)), O.f32_to_bf16(oq))
+    else:
+        assert np.array_equal(qo.cpu().numpy().view(np.uint32), oq.view(np.uint32))
+    got_k, got_v = host_bits(kc), host_bits(vc)
+    assert np.array_equal(got_k, okc)  # other layers and unused slots untouched (zero)
+    assert np.array_equal(got_v, ovc)
+
+
+def test_negative_slot_is_skipped_and_bad_slot_is_reported(cuda):
+    rng = np.random.default_rng(5)
+    T, Hq, Hkv = 4, 16, 8
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    w = O.f32_to_bf16(np.ones(128, np.float32))
+    pos = np.array([1, 2, 3, 4], np.int32)
+    h = handle(Hq, Hkv, 1)
+    _, kc, _ = run_store(h, 0, q, k, v, w, w, pos, np.array([0, -1, 2, 3], np.int32), 256, Hkv)
+    assert h.get_error()[0] == nvattn.OK
+    kb = host_bits(kc)
+    assert not kb[0, 1].any() and kb[0, 0].any()
+    _, kc, _ = run_store(h, 0, q, k, v, w, w, pos, np.array([0, 1, 256, 3], np.int32), 256, Hkv)
+    st, detail = h.get_error()
+    assert st == nvattn.ERR_OUT_OF_RANGE and detail == 256
+    _, kc, _ = run_store(h, 0, q, k, v, w, w, np.array([0, 1, 40960, 3], np.int32),
+                         np.array([0, 1, 2, 3], np.int32), 256, Hkv)
+    st, detail = h.get_error()
+    assert st == nvattn.ERR_OUT_OF_RANGE and detail == 40960
+    assert h.get_error()[0] == nvattn.OK  # cleared after reading
+
+
+def test_in_place_f32_q(cuda):
+    import torch
+    rng = np.random.default_rng(6)
+    T, Hq, Hkv = 300, 16, 8
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    w = O.f32_to_bf16(np.ones(128, np.float32))
+    pos = np.arange(T, dtype=np.int32)
+    slots = np.arange(T, dtype=np.int32)
+    h = handle(Hq, Hkv, 2)
+    dq = dev(q)
+    kc = torch.zeros((1, 512, Hkv, 128), dtype=torch.int16, device="cuda")
+    vc = torch.zeros_like(kc)
+    h.kv_store(0, dq, dev(k), dev(v), dev(w), dev(w), dev(pos), dev(slots), dq, kc, vc)
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=512)
+    oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos, slots, np.zeros((1, 512, Hkv, 128), np.uint16),
+                              np.zeros((1, 512, Hkv, 128), np.uint16))
+    assert np.array_equal(dq.cpu().numpy().view(np.uint32), oq.view(np.uint32))
