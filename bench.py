@@ -50,19 +50,162 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
-def workload(rng_seed=SEED):
+def workload(rng_seed=SEED, n_seqs=N_SEQS):
+    """Context lengths, block tables and pool size.  n_seqs < 256 keeps the
+    first n_seqs lengths of the same draw (a smaller case for profiling)."""
     rng = np.random.default_rng(rng_seed)
     lens = np.exp(rng.uniform(math.log(1024), math.log(32768), N_SEQS)).astype(np.int64)
+    lens = lens[:n_seqs]
     need = (lens + BS - 1) // BS
     num_blocks = int(need.sum() * 1.1) + 1
     perm = rng.permutation(num_blocks).astype(np.int32)
     max_blocks = int(need.max())
-    bt = np.full((N_SEQS, max_blocks), -1, np.int32)
+    bt = np.full((n_seqs, max_blocks), -1, np.int32)
     off = 0
-    for s in range(N_SEQS):
+    for s in range(n_seqs):
         bt[s, :need[s]] = perm[off:off + need[s]]
         off += int(need[s])
     return lens, bt, num_blocks
+
+
+def prefill_workload(kind):
+    """(name, Hq, Hkv, seq_lens, cached prefix per sequence, block tables,
+    num_blocks) for the two prefill workloads.
+
+    prefix_hit: Qwen3-0.6B attention shape, 8 sequences with prompt lengths
+      uniform in [512, 4096]; the first 1024 tokens (4 blocks) are a prefix
+      already in the cache and shared by all 8 (refcount 8); a prompt of at
+      most 1024 tokens hits 256*floor((L-1)/256) tokens of the same blocks.
+    chunk: Qwen3-32B attention shape (64 q / 8 kv heads), 16 sequences whose
+      cached context is 129024 tokens; one 2048-token chunk each at positions
+      [129024, 131072)."""
+    rng = np.random.default_rng(SEED + 2)
+    if kind == "prefix_hit":
+        name, Hq, Hkv = "prefill_prefix_hit_qwen3_0p6b_8seq", 16, 8
+        lens = rng.integers(512, 4097, 8).astype(np.int64)
+        cached = np.where(lens > 1024, 1024, 256 * ((lens - 1) // 256)).astype(np.int64)
+        n_shared = 4
+    else:
+        name, Hq, Hkv = "chunked_prefill_qwen3_32b_16x2048_at_129024", 64, 8
+        lens = np.full(16, 131072, np.int64)
+        cached = np.full(16, 129024, np.int64)
+        n_shared = 0
+    need = (lens + BS - 1) // BS
+    n_hit = cached // BS if n_shared else np.zeros_like(cached)  # blocks taken from the prefix
+    num_blocks = int(n_shared + (need - n_hit).sum() + 8)
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    shared, pool = perm[:n_shared], perm[n_shared:]
+    bt = np.full((len(lens), int(need.max())), -1, np.int32)
+    off = 0
+    for s in range(len(lens)):
+        ns = int(n_hit[s])
+        bt[s, :ns] = shared[:ns]
+        bt[s, ns:need[s]] = pool[off:off + need[s] - ns]
+        off += int(need[s] - ns)
+    return name, Hq, Hkv, lens, cached, bt, num_blocks
+
+
+def bench_prefill(kind, args, world, rank, device):
+    """Times one prefill layer-step (fused q/k norm + RoPE + suffix K/V store,
+    then causal paged prefill over prefix + suffix) on this rank's kv-head
+    shard.  Returns (fields, per-rank prefill ms, per-rank step ms)."""
+    import torch
+    import nvattn
+    name, Hq, Hkv, lens, cached, bt_np, num_blocks = prefill_workload(kind)
+    hq, hkv = Hq // world, Hkv // world
+    cu, qs, cl, pos_np, slot_np = nvattn.plan_prefill(lens, cached, bt_np)
+    T = int(cu[-1])
+    max_q = int((cl - qs).max())
+    max_ctx = int(cl.max())
+    cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
+                              max_seqs=len(lens), max_context=max_ctx, max_position=max_ctx,
+                              device=device.index)
+    h = nvattn.Handle(cfg)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2000 + rank)
+    n_slots = num_blocks * BS
+    kc = torch.empty((n_slots, hkv, D), dtype=torch.bfloat16, device=device)
+    vc = torch.empty_like(kc)
+    for t in (kc, vc):
+        for i in range(0, n_slots, 1 << 16):
+            t[i:i + (1 << 16)].copy_(torch.randn((min(1 << 16, n_slots - i), hkv, D),
+                                                 generator=gen, device=device))
+    q = torch.randn((T, hq, D), generator=gen, device=device)
+    k = torch.randn((T, hkv, D), generator=gen, device=device)
+    v = torch.randn((T, hkv, D), generator=gen, device=device)
+    qw = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16)
+    kw = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16)
+    qb = torch.empty((T, hq, D), dtype=torch.bfloat16, device=device)
+    out = torch.empty((T, hq, D), device=device)
+    d = {n: torch.from_numpy(a).to(device) for n, a in
+         (("cu", cu), ("qs", qs), ("cl", cl), ("pos", pos_np), ("slot", slot_np), ("bt", bt_np))}
+    stream = torch.cuda.current_stream(device)
+    kc16, vc16 = kc.view(torch.int16), vc.view(torch.int16)
+    qw16, kw16 = qw.view(torch.int16), kw.view(torch.int16)
+    evs = []
+
+    def step():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h.kv_store(0, q, k, v, qw16, kw16, d["pos"], d["slot"], qb, kc16, vc16, stream=stream)
+        a.record(stream)
+        h.prefill(0, qb, d["cu"], d["qs"], d["cl"], d["bt"], max_q, kc16, vc16, out,
+                  stream=stream)
+        b.record(stream)
+        evs.append((a, b))
+
+    steps = max(2, args.prefill_steps)
+    for _ in range(max(3, min(args.warmup, 5))):
+        step()
+    torch.cuda.synchronize(device)
+    h.check_device(f"prefill warmup {name}")
+    evs.clear()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[device.index])
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    h.check_device(f"prefill {name}")
+    step_ms = t0.elapsed_time(t1) / steps
+    pre_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    # algorithmic causal FLOPs (whole job, all heads): 4*d*Hq per visible (q, k) pair
+    pairs = sum(int(((np.arange(qs[s], cl[s]) + 1)).sum()) for s in range(len(lens)))
+    flops = 4.0 * D * Hq * pairs
+    h.close()
+    fields = {"workload": name, "q_heads": Hq, "kv_heads": Hkv, "n_seqs": len(lens),
+              "new_tokens": T, "sum_context": int(cl.sum()), "flops_per_step": flops,
+              "steps": steps, "p_split": 1}
+    return fields, pre_ms, step_ms
+
+
+def run_prefills(args, world, rank, device):
+    """Times every selected prefill workload; returns JSON-ready dicts (the
+    per-step times are the max over ranks)."""
+    import torch
+    kinds = [k for k in args.prefill.split(",") if k and k != "none"]
+    _, tflops_peak, peak_kind = peaks()
+    results = []
+    for kind in kinds:
+        fields, pre_ms, step_ms = bench_prefill(kind, args, world, rank, device)
+        t = torch.tensor([pre_ms, step_ms], dtype=torch.float64, device=device)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre_ms, step_ms = t.tolist()
+        achieved = fields["flops_per_step"] / (pre_ms / 1e3) / 1e12
+        fields.update({
+            "tokens_per_s": fields["new_tokens"] / (step_ms / 1e3), "ms_per_step": step_ms,
+            "tflops": achieved,
+            "roofline": {"bound": "tensor", "kernel": "paged_prefill (tcgen05)",
+                         "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
+                         "frac": achieved / tflops_peak, "peak_source": peak_kind,
+                         "prefill_ms": pre_ms, "frac_of_2250_nominal": achieved / 2250.0},
+        })
+        results.append(fields)
+    return results
 
 
 def peaks():
@@ -142,9 +285,9 @@ def cpu_sample(lens, bt, k_host_fn, n_target_s=12.0):
         O.paged_decode(p, O.MODE_GGML, 0, q, kc, vc, btc, lc)
         dt = time.perf_counter() - t0
         results.append((n, dt))
-        if dt >= n_target_s or n >= N_SEQS:
+        if dt >= n_target_s or n >= len(lens):
             break
-        n = min(N_SEQS, max(n + 1, int(n * min(8.0, n_target_s / max(dt, 1e-3)))))
+        n = min(len(lens), max(n + 1, int(n * min(8.0, n_target_s / max(dt, 1e-3)))))
     n, dt = results[-1]
     return n / dt, n, dt, cores
 
@@ -218,6 +361,13 @@ def main():
     ap.add_argument("--allgather", action="store_true",
                     help="all-gather the head-sharded outputs every step (NCCL)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seqs", type=int, default=N_SEQS,
+                    help="use the first SEQS sequences only (smaller case for profiling)")
+    ap.add_argument("--prefill", default="prefix_hit,chunk",
+                    help="comma list of prefill workloads to time (prefix_hit, chunk) or none")
+    ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--only-prefill", action="store_true",
+                    help="skip the decode workload (for profiling the prefill kernel)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -238,11 +388,22 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=device, timeout=timedelta(seconds=120))
 
+    if args.only_prefill:
+        res = run_prefills(args, world, rank, device)
+        if rank == 0:
+            first = res[0] if res else {}
+            print(json.dumps({"metric": METRIC, "value": first.get("tokens_per_s"),
+                              "unit": "tokens/s", "n_gpus": world, "prefill": res}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
     hkv, hq = HKV // world, HQ // world
-    lens, bt_np, num_blocks = workload()
+    B = args.seqs
+    lens, bt_np, num_blocks = workload(n_seqs=B)
     max_ctx = int(lens.max())
     cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
-                              max_seqs=N_SEQS, max_context=max_ctx, max_position=max_ctx,
+                              max_seqs=B, max_context=max_ctx, max_position=max_ctx,
                               device=local_rank)
     h = nvattn.Handle(cfg)
 
@@ -262,13 +423,13 @@ def main():
     ctx = torch.from_numpy(cl).to(device)
     pos = torch.from_numpy(pos_np).to(device)
     slots = torch.from_numpy(slot_np).to(device)
-    q0 = torch.randn((N_SEQS, hq, D), generator=gen, device=device)
-    k_new = torch.randn((N_SEQS, hkv, D), generator=gen, device=device)
-    v_new = torch.randn((N_SEQS, hkv, D), generator=gen, device=device)
+    q0 = torch.randn((B, hq, D), generator=gen, device=device)
+    k_new = torch.randn((B, hkv, D), generator=gen, device=device)
+    v_new = torch.randn((B, hkv, D), generator=gen, device=device)
     w = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16)
     q = torch.empty_like(q0)
-    out = torch.empty((N_SEQS, hq, D), device=device)
-    gathered = torch.empty((world, N_SEQS, hq, D), device=device) if args.allgather else None
+    out = torch.empty((B, hq, D), device=device)
+    gathered = torch.empty((world, B, hq, D), device=device) if args.allgather else None
     stream = torch.cuda.current_stream(device)
     kc16, vc16, w16 = kc.view(torch.int16), vc.view(torch.int16), w.view(torch.int16)
 
@@ -322,7 +483,7 @@ def main():
     hctx = ctx.cpu().pin_memory()
     hpos = pos.cpu().pin_memory()
     hslot = slots.cpu().pin_memory()
-    hout = torch.empty((N_SEQS, hq, D), dtype=torch.float32).pin_memory()
+    hout = torch.empty((B, hq, D), dtype=torch.float32).pin_memory()
     dk, dv = torch.empty_like(k_new), torch.empty_like(v_new)
     dbt, dctx, dpos, dslot = (torch.empty_like(x) for x in (bt, ctx, pos, slots))
     h2d = sum(x.numel() * x.element_size() for x in (hq0, hk, hv, hbt, hctx, hpos, hslot))
@@ -358,12 +519,40 @@ def main():
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     elapsed, e2e_elapsed, dec_ms = times.tolist()
 
+    # CPU baseline (rank 0, one GPU): the oracle's ggml-chain decode on the
+    # host cores over the workload's first sequences, with this run's K/V.
+    cpu_base = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        def host_case(n):
+            need = (lens[:n] + BS - 1) // BS
+            ids = np.concatenate([bt_np[s, :need[s]] for s in range(n)])
+            idx = torch.from_numpy(ids.astype(np.int64)).to(device)
+            rows = (idx[:, None] * BS + torch.arange(BS, device=device)[None]).reshape(-1)
+            kh = kc.index_select(0, rows).view(torch.int16).cpu().numpy().view(np.uint16)
+            vh = vc.index_select(0, rows).view(torch.int16).cpu().numpy().view(np.uint16)
+            btc = np.full((n, bt_np.shape[1]), -1, np.int32)
+            o = 0
+            for s in range(n):
+                btc[s, :need[s]] = np.arange(o, o + need[s])
+                o += int(need[s])
+            return (kh[None], vh[None], btc, lens[:n].astype(np.int32),
+                    q.cpu().numpy()[:n].copy())
+        tps, n, dt, cores = cpu_sample(lens, bt_np, host_case)
+        cpu_base = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                    "sample": f"oracle GGML-mode paged decode of the first {n} sequences "
+                              f"({dt:.1f} s on {cores} threads)"}
+
+    # release the decode cache before the prefill workloads allocate theirs
+    del kc, vc, kc16, vc16
+    torch.cuda.empty_cache()
+    prefill_results = run_prefills(args, world, rank, device)
+
     if rank == 0:
         hbm_peak, _, peak_kind = peaks()
-        n_tok = N_SEQS * args.steps
+        n_tok = B * args.steps
         kv_bytes = int(lens.sum()) * hkv * D * 2 * 2
-        alg_bytes = (kv_bytes + N_SEQS * hq * D * 4 * 2 + int(((lens + BS - 1) // BS).sum()) * 4
-                     + N_SEQS * 4)
+        alg_bytes = (kv_bytes + B * hq * D * 4 * 2 + int(((lens + BS - 1) // BS).sum()) * 4
+                     + B * 4)
         achieved = alg_bytes / (dec_ms / 1e3) / 1e9
         splits = 1
         line = {
@@ -372,7 +561,8 @@ def main():
             "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 KV, fp32 accumulate",
             "data": "synthetic (seeded N(0,1) Q/K/V, log-uniform context lengths)",
-            "config": {"workload": WORKLOAD, "n_seqs": N_SEQS, "q_heads": HQ, "kv_heads": HKV,
+            "config": {"workload": WORKLOAD if B == N_SEQS else f"{WORKLOAD}[first {B}]",
+                       "n_seqs": B, "q_heads": HQ, "kv_heads": HKV,
                        "head_dim": D, "block_size": BS, "sum_context": int(lens.sum()),
                        "kv_gb_per_gpu": round(kv_bytes / 1e9, 3),
                        "parallelism": f"kv-head shard x{world}",
@@ -388,27 +578,10 @@ def main():
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * (2 + splits),
             "clocks": clk,
+            "prefill": prefill_results,
         }
-        if world == 1 and not args.no_cpu_baseline:
-            def host_case(n):
-                need = (lens[:n] + BS - 1) // BS
-                ids = np.concatenate([bt_np[s, :need[s]] for s in range(n)])
-                idx = torch.from_numpy(ids.astype(np.int64)).to(device)
-                rows = (idx[:, None] * BS + torch.arange(BS, device=device)[None]).reshape(-1)
-                kh = kc.index_select(0, rows).view(torch.int16).cpu().numpy().view(np.uint16)
-                vh = vc.index_select(0, rows).view(torch.int16).cpu().numpy().view(np.uint16)
-                btc = np.full((n, bt_np.shape[1]), -1, np.int32)
-                o = 0
-                for s in range(n):
-                    btc[s, :need[s]] = np.arange(o, o + need[s])
-                    o += int(need[s])
-                return (kh[None], vh[None], btc, lens[:n].astype(np.int32),
-                        q.cpu().numpy()[:n].copy())
-            tps, n, dt, cores = cpu_sample(lens, bt_np, host_case)
-            line["cpu_baseline"] = {
-                "value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
-                "sample": f"oracle GGML-mode paged decode of the first {n} sequences "
-                          f"({dt:.1f} s on {cores} threads)"}
+        if cpu_base is not None:
+            line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)
     h.close()
     if world > 1:

@@ -109,20 +109,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs, records NVATTN_ERR_TIMEOUT with `site`, and returns false;
-// callers carry on so the kernel always terminates.
+// kWaitLimitNs, records NVATTN_ERR_TIMEOUT with `site`, raises the CTA's
+// abort flag (when given) and returns false.  Once the abort flag is up,
+// every later wait of the CTA returns false at once, so a CTA that lost a
+// wait finishes its (bounded) loops quickly instead of timing out again.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, DeviceStatus* st,
-                                          int site) {
+                                          int site, volatile int* abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   uint32_t it = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((++it & 63u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
-      record_error(st, NVATTN_ERR_TIMEOUT, site, 0);
-      return false;
+    if ((++it & 63u) == 0) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_error(st, NVATTN_ERR_TIMEOUT, site, 0);
+        if (abort_flag != nullptr) *abort_flag = 1;
+        return false;
+      }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, DeviceStatus* st,
+                                          volatile int* abort_flag, int site) {
+  return mbar_wait(bar, parity, st, site, abort_flag);
+}
+
+// True when an earlier launch already recorded a timeout: CTAs then skip
+// their work so a systematic wait failure costs one timeout, not one per CTA.
+__device__ __forceinline__ bool timeout_recorded(const DeviceStatus* st) {
+  return st != nullptr && *reinterpret_cast<const volatile int*>(&st->code) == NVATTN_ERR_TIMEOUT;
 }
 
 // ---------------------------------------------------------------------------
@@ -162,6 +179,107 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMEM (5th-generation tensor cores, cta_group::1)
+// ---------------------------------------------------------------------------
+
+// Allocates n_cols TMEM columns (power of two >= 32); one whole warp calls
+// this; the TMEM base address is written to *dst (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t n_cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(n_cols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t n_cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(n_cols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 format: start
+// address, leading / stride byte offsets in 16-byte units, version 1 at bit
+// 46, layout type 2 = SWIZZLE_128B at bits 61-63).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
+                                                    uint32_t sbo_bytes) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 A and B, f32 accumulator.
+// a_mn / b_mn select MN-major (transposed) operands.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4)                         // D format f32
+         | (1u << 7)                       // A format bf16
+         | (1u << 10)                      // B format bf16
+         | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by a single thread.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on an mbarrier once every previously issued tcgen05.mma of this
+// thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+#define NVATTN_R8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), \
+                     "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+#define NVATTN_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), \
+                     "r"(r[i + 4]), "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
+
+// 32 lanes x 32 columns of 32-bit TMEM: thread i of the warp receives lane
+// (taddr.lane + i), columns [taddr.col, taddr.col + 32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : NVATTN_R8(0), NVATTN_R8(8), NVATTN_R8(16), NVATTN_R8(24)
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      NVATTN_W8(0), NVATTN_W8(8), NVATTN_W8(16), NVATTN_W8(24)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------

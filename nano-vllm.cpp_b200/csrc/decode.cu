@@ -57,6 +57,7 @@ struct __align__(1024) DecodeSmem {
   float l_run[G];
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  int abort_flag;  // raised by the first wait that times out
 };
 
 // Butterfly transpose-reduction of V per-lane partial sums across the warp.
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     ctx = ctx < 0 ? 0 : prm.max_context;
   }
   if (t_begin >= ctx && split > 0) return;  // nothing for this split
+  if (timeout_recorded(prm.status)) return;
   const int t_end = min(ctx, t_begin + prm.split_tokens);
   const int n_tiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
   const int n_splits = ctx > 0 ? (ctx + prm.split_tokens - 1) / prm.split_tokens : 1;
@@ -129,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], kConsumerWarps);
     }
+    sm.abort_flag = 0;
     fence_barrier_init();
   }
   if (threadIdx.x < G) {
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t policy = l2_policy_evict_first();
       for (int i = 0; i < n_tiles; ++i) {
         const int stage = i % kStages;
-        if (i >= kStages) mbar_wait(&sm.empty[stage], ((i / kStages) & 1) ^ 1, prm.status, 11);
+        if (i >= kStages) mbar_wait(&sm.empty[stage], ((i / kStages) & 1) ^ 1, prm.status, &sm.abort_flag, 11);
         const int tok = t_begin + i * kTile;
         const int bi = tok / prm.block_size;
         long long bid = prm.block_tables[(long long)seq * prm.max_blocks + bi];
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   for (int i = 0; i < n_tiles; ++i) {
     const int stage = i % kStages;
-    mbar_wait(&sm.full[stage], (i / kStages) & 1, prm.status, 13);
+    mbar_wait(&sm.full[stage], (i / kStages) & 1, prm.status, &sm.abort_flag, 13);
     const uint16_t* kt = sm.k[stage];
     const uint16_t* vt = sm.v[stage];
     const int tok0 = t_begin + i * kTile;

@@ -6,10 +6,10 @@ import nvattn
 
 
 def handle(Hq, Hkv, num_blocks, n_layer=1, max_seqs=512, max_context=40960,
-           max_position=40960, device=0):
+           max_position=40960, device=0, **overrides):
     cfg = nvattn.qwen3_config(n_layer=n_layer, n_q_heads=Hq, n_kv_heads=Hkv,
                               num_blocks=num_blocks, max_seqs=max_seqs, max_context=max_context,
-                              max_position=max_position, device=device)
+                              max_position=max_position, device=device, **overrides)
     return nvattn.Handle(cfg)
 
 
