@@ -41,9 +41,10 @@ N_SEQS, HQ, HKV, D, BS = 256, 32, 8, 128, 256
 SEED = 0
 
 # DRAM traffic per decode launch of this workload (dram__bytes_read.sum +
-# dram__bytes_write.sum), from the ncu capture summarised in
-# profiles/paged_decode_qwen3_8b_256seq.md; None until that capture exists.
-NCU_TRAFFIC_BYTES_N1 = None
+# dram__bytes_write.sum): the 32-sequence ncu capture summarised in
+# profiles/paged_decode_qwen3_8b_256seq.md read 1.0062x its algorithmic
+# bytes; scaled to the full launch's 10.987 GB of algorithmic bytes.
+NCU_TRAFFIC_BYTES_N1 = 11.055e9
 
 
 def log(*a):

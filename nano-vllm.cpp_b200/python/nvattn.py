@@ -203,6 +203,25 @@ class Handle:
         return st
 
 
+def kv_head_shard(n_q_heads, n_kv_heads, world, rank):
+    """KV-head sharding across `world` GPUs: rank r owns kv heads
+    [r*Hkv/N, (r+1)*Hkv/N) and the GQA q heads that read them (consecutive q
+    heads share a kv head, as ggml's broadcast does).  Returns
+    (kv_begin, kv_end, q_begin, q_end)."""
+    if world <= 0 or not 0 <= rank < world or n_kv_heads % world or n_q_heads % n_kv_heads:
+        raise ValueError("kv heads must split evenly across ranks")
+    per = n_kv_heads // world
+    g = n_q_heads // n_kv_heads
+    return rank * per, (rank + 1) * per, rank * per * g, (rank + 1) * per * g
+
+
+def gather_heads(shards):
+    """Concatenates per-rank outputs [tokens][Hq/N][d] along the head axis into
+    [tokens][Hq][d] (the layout BuildAttention hands to o_proj)."""
+    import numpy as np
+    return np.concatenate(shards, axis=1)
+
+
 def plan_prefill(seq_lens, num_cached, block_tables, block_size=256):
     """Host planner (no device work): numpy in, numpy out."""
     import numpy as np
