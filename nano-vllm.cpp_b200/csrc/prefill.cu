@@ -9,20 +9,29 @@
 // position P attends keys [0, P] of its sequence through the block table,
 // which covers prefix-cache hits and chunked prefill alike.
 //
-// One CTA = (sequence, q head, tile of 128 query rows); 128-key KV tiles.
-//   warp 0      TMA producer: Q once, then K and V tiles (two 64-column
-//               boxes each, 128-byte swizzle) into a 2-stage ring.
-//   warp 1      TMEM allocation; one lane issues the MMAs:
-//                 S[b] = Q K^T   (M=128, N=128, K=128; A, B K-major)
-//                 O   += P V     (M=128, N=128, K=128; P K-major, V MN-major)
-//               S is double-buffered in TMEM so S(j+1) runs while the
-//               softmax warps work on S(j).
-//   warps 2-5   softmax: thread = query row = TMEM lane.  Causal mask,
-//               online softmax in the log2 domain, P written to shared
-//               memory as bf16 in the UMMA operand layout, lazy O rescaling
-//               (only when a row max grows by more than 2^8), epilogue
-//               O / l -> f32 output.
-// TMEM: columns [0,256) two S buffers, [256,384) O.
+// One CTA owns two 128-row query tiles that read the same keys: the two GQA
+// heads of a pair (same rows, same kv head), or, when a kv head serves one q
+// head, two consecutive row tiles.  Keys come in 128-key tiles.
+//   warp 0       TMA producer: both Q tiles once, then K(j), V(j), K(j+1) ...
+//                through a ring of 5 x 32 KiB slots (two 64-column boxes per
+//                tile, 128-byte swizzle).
+//   warp 1       TMEM allocation; one lane issues the MMAs, interleaving the
+//                two tiles so the tensor core works on one tile while the
+//                other tile's softmax runs:
+//                  PV0(j), S0(j+1), PV1(j), S1(j+1), ...
+//                S_t = Q_t K^T (M=128, N=128, K=128; A and B K-major, smem)
+//                O_t += P_t V  (A = P from TMEM, B = V MN-major from smem)
+//   warps 4-7    softmax of tile 0; warps 8-11 softmax of tile 1: thread =
+//                query row = TMEM lane.  Causal mask, online softmax in the
+//                log2 domain, P written as bf16 into the TMEM columns of its
+//                own S (S was read to registers), lazy O rescaling (only when
+//                a row max grows by more than 2^8), epilogue O / l.
+// MMAs issued by one thread execute in order, so S(j+1) may overwrite the
+// columns of P(j) right after PV(j) is issued, and the completion of S(j+1)
+// implies PV(j) is done (its O may then be rescaled).
+// TMEM columns: tile t uses [256t, 256t+128) for S/P and [256t+128, 256t+256)
+// for O.  Split-P mode keeps bf16(P) in the first 64 columns of S and the
+// bf16 remainder P - bf16(P) in the next 64, and runs P.V twice.
 #include "common.cuh"
 #include "internal.h"
 
@@ -30,16 +39,17 @@ namespace nvattn {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kBM = 128;  // query rows per CTA
-constexpr int kBN = 128;  // keys per KV tile
-constexpr int kThreads = 192;
+constexpr int kBM = 128;  // query rows per tile
+constexpr int kBN = 128;  // keys per tile
+constexpr int kSlots = 5;
+constexpr int kThreads = 12 * 32;
 constexpr int kHalfBytes = 128 * 64 * 2;  // one 128-row x 64-column bf16 box: 16 KiB
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
-  int Hq, Hkv, G, layer, block_size, max_blocks, n_mtiles;
+  int Hq, Hkv, G, layer, block_size, max_blocks, n_mtiles, pair_heads;
   long long n_slots, num_blocks;
   float scale_log2;
   const int32_t* cu_q;
@@ -50,20 +60,263 @@ struct PrefillParams {
   DeviceStatus* status;
 };
 
-template <bool kSplitP>
 struct __align__(1024) PrefillSmem {
-  uint16_t q[2][kBM * 64];     // [d half][row][64]
-  uint16_t k[2][2][kBN * 64];  // [stage][d half][key][64]
-  uint16_t v[2][2][kBN * 64];  // [stage][d half][key][64]
-  uint16_t p[2][kBM * 64];     // [key half][row][64]
-  uint16_t p_lo[kSplitP ? 2 : 1][kSplitP ? kBM * 64 : 512];  // bf16 remainder of P
+  uint16_t q[2][2][kBM * 64];       // [tile][d half][row][64]
+  uint16_t kv[kSlots][2][kBN * 64];  // [slot][d half][key][64]
   uint64_t q_full;
-  uint64_t k_full[2], v_full[2], kv_empty[2];
-  uint64_t s_full[2], s_free[2];
-  uint64_t p_full, o_done;
+  uint64_t full[kSlots], empty[kSlots];
+  uint64_t s_full[2], p_full[2];
+  uint64_t o_final;
   uint32_t tmem_base;
   int abort_flag;  // raised by the first wait that times out
 };
+
+// What one CTA works on (computed identically by every thread).
+struct Work {
+  int seq, kvh, q0, q_start, ctx, n_kv, p_last0;
+  int head[2], row0[2], rows[2];
+};
+
+__device__ __forceinline__ int ring_slot(int idx) { return idx % kSlots; }
+__device__ __forceinline__ uint32_t ring_parity(int idx) { return (uint32_t)(idx / kSlots) & 1u; }
+
+// ---------------------------------------------------------------- producer
+__device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap* tm_q,
+                                              const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                                              const PrefillParams& prm, const Work& w) {
+  volatile int* abort_flag = &sm.abort_flag;
+  tma_prefetch_desc(tm_q);
+  tma_prefetch_desc(tm_k);
+  tma_prefetch_desc(tm_v);
+  mbar_arrive_expect_tx(&sm.q_full, 4 * kHalfBytes);
+  for (int t = 0; t < 2; ++t) {
+    tma_load_3d(sm.q[t][0], tm_q, &sm.q_full, 0, w.head[t], w.q0 + w.row0[t]);
+    tma_load_3d(sm.q[t][1], tm_q, &sm.q_full, 64, w.head[t], w.q0 + w.row0[t]);
+  }
+  const int n_loads = 2 * w.n_kv;
+  long long bid = 0;
+  for (int idx = 0; idx < n_loads; ++idx) {
+    const int slot = ring_slot(idx);
+    if (idx >= kSlots)
+      mbar_wait(&sm.empty[slot], ring_parity(idx) ^ 1u, prm.status, abort_flag, 30);
+    const int key0 = (idx >> 1) * kBN;
+    if ((idx & 1) == 0) {
+      bid = prm.block_tables[(long long)w.seq * prm.max_blocks + key0 / prm.block_size];
+      if (bid < 0 || bid >= prm.num_blocks) {
+        record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 24, bid);
+        bid = 0;
+      }
+    }
+    const int row = (int)((long long)prm.layer * prm.n_slots + bid * prm.block_size +
+                          key0 % prm.block_size);
+    const CUtensorMap* map = (idx & 1) ? tm_v : tm_k;
+    mbar_arrive_expect_tx(&sm.full[slot], 2 * kHalfBytes);
+    tma_load_3d(sm.kv[slot][0], map, &sm.full[slot], 0, w.kvh, row);
+    tma_load_3d(sm.kv[slot][1], map, &sm.full[slot], 64, w.kvh, row);
+  }
+  // Drain: the last load of every slot has landed before the CTA can exit
+  // (immediate in normal operation; bounded after an abort).
+  for (int idx = max(0, n_loads - kSlots); idx < n_loads; ++idx)
+    mbar_wait(&sm.full[ring_slot(idx)], ring_parity(idx), prm.status, 40);
+}
+
+// ---------------------------------------------------------------- MMA issuer
+template <bool kSplitP>
+__device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
+                                         const PrefillParams& prm, const Work& w) {
+  volatile int* abort_flag = &sm.abort_flag;
+  constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kBM, kBN, 0, 0);
+  constexpr uint32_t idesc_o = umma_idesc_bf16_f32(kBM, kD, 0, 1);
+  const int n_kv = w.n_kv;
+  mbar_wait(&sm.q_full, 0, prm.status, abort_flag, 31);
+  auto issue_s = [&](int t, int j) {
+    const int slot = ring_slot(2 * j);
+#pragma unroll
+    for (int k = 0; k < kD / 16; ++k) {
+      const uint32_t koff = (uint32_t)(k & 3) * 32;
+      const uint64_t a = umma_desc_sw128(smem_u32(sm.q[t][k >> 2]) + koff, 16, 1024);
+      const uint64_t b = umma_desc_sw128(smem_u32(sm.kv[slot][k >> 2]) + koff, 16, 1024);
+      umma_bf16(tmem + t * 256, a, b, idesc_s, k > 0 ? 1u : 0u);
+    }
+  };
+  auto issue_pv = [&](int t, int j) {
+    const uint32_t vbase = smem_u32(sm.kv[ring_slot(2 * j + 1)][0]);
+#pragma unroll
+    for (int k = 0; k < kBN / 16; ++k) {
+      const uint64_t b = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kHalfBytes, 1024);
+      umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, b, idesc_o,
+                   (j > 0 || k > 0) ? 1u : 0u);
+    }
+    if constexpr (kSplitP) {
+#pragma unroll
+      for (int k = 0; k < kBN / 16; ++k) {
+        const uint64_t b = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kHalfBytes, 1024);
+        umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + 64 + k * 8, b, idesc_o, 1u);
+      }
+    }
+  };
+  mbar_wait(&sm.full[ring_slot(0)], ring_parity(0), prm.status, abort_flag, 32);
+  tc_fence_after();
+  issue_s(0, 0);
+  umma_commit(&sm.s_full[0]);
+  issue_s(1, 0);
+  umma_commit(&sm.s_full[1]);
+  umma_commit(&sm.empty[ring_slot(0)]);
+  for (int j = 0; j < n_kv; ++j) {
+    const int vidx = 2 * j + 1, kidx = 2 * j + 2;
+    mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 33);
+    mbar_wait(&sm.p_full[0], j & 1, prm.status, abort_flag, 34);
+    tc_fence_after();
+    issue_pv(0, j);
+    if (j + 1 < n_kv) {
+      mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 35);
+      tc_fence_after();
+      issue_s(0, j + 1);
+      umma_commit(&sm.s_full[0]);
+    }
+    mbar_wait(&sm.p_full[1], j & 1, prm.status, abort_flag, 36);
+    tc_fence_after();
+    issue_pv(1, j);
+    umma_commit(&sm.empty[ring_slot(vidx)]);
+    if (j + 1 < n_kv) {
+      issue_s(1, j + 1);
+      umma_commit(&sm.s_full[1]);
+      umma_commit(&sm.empty[ring_slot(kidx)]);
+    }
+  }
+  umma_commit(&sm.o_final);
+  // Drain: every MMA has completed before TMEM is released.
+  mbar_wait(&sm.o_final, 0, prm.status, 42);
+}
+
+// ---------------------------------------------------------------- softmax
+template <bool kSplitP>
+__device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
+                                             const PrefillParams& prm, const Work& w, int warp,
+                                             int lane) {
+  volatile int* abort_flag = &sm.abort_flag;
+  const int t = (warp - 4) >> 2;  // query tile
+  const int quad = warp & 3;      // TMEM lanes [32*quad, 32*quad+32)
+  const int row = quad * 32 + lane;
+  const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+  const uint32_t s_col = tmem + lane_off + t * 256;
+  const uint32_t o_col = s_col + 128;
+  const int my_rows = t ? w.rows[1] : w.rows[0];
+  const int my_row0 = t ? w.row0[1] : w.row0[0];
+  const int my_head = t ? w.head[1] : w.head[0];
+  // Rows past the end of the sequence mimic a real row (never stored).
+  const int pos_row = my_rows > 0 ? w.q_start + my_row0 + min(row, my_rows - 1) : w.p_last0;
+  const int vis_last = min(pos_row, w.ctx - 1);  // last visible key
+  const float sc = prm.scale_log2;
+  float m_used = -INFINITY;
+  float l = 0.0f;
+
+  for (int j = 0; j < w.n_kv; ++j) {
+    mbar_wait(&sm.s_full[t], j & 1, prm.status, abort_flag, 37);
+    tc_fence_after();
+    uint32_t sr[128];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+    tmem_wait_ld();
+
+    const int lim = vis_last - j * kBN;  // keys c <= lim are visible
+    if (lim < kBN - 1) {
+#pragma unroll
+      for (int c = 0; c < kBN; ++c)
+        if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+    }
+    float mx[8];
+#pragma unroll
+    for (int a = 0; a < 8; ++a) mx[a] = __uint_as_float(sr[a]);
+#pragma unroll
+    for (int c = 8; c < kBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sr[c]));
+    const float tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
+    const float m_new = fmaxf(m_used, tile_max);
+    float alpha = 1.0f;
+    bool rescale = false;
+    if (m_new > m_used + kRescaleThreshold) {
+      alpha = fast_exp2(m_used - m_new);
+      rescale = j > 0;
+      m_used = m_new;
+    }
+    const float neg_m = -m_used;
+    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // 32 keys per chunk -> 16 packed columns
+      uint32_t hi[16];
+      uint32_t lo[kSplitP ? 16 : 1];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), sc, neg_m));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), sc, neg_m));
+        sum[i & 3] += p0 + p1;
+        hi[i] = cvt_bf16x2(p0, p1);
+        if constexpr (kSplitP)
+          lo[i] = cvt_bf16x2(p0 - bf16lo_to_f32(hi[i]), p1 - bf16hi_to_f32(hi[i]));
+      }
+      tmem_st16(s_col + c * 16, hi);
+      if constexpr (kSplitP) tmem_st16(s_col + 64 + c * 16, lo);
+    }
+    l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+
+    // O_t: the completion of S_t(j) implies PV_t(j-1) has completed.
+    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(o_col + c * 32, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        tmem_st32(o_col + c * 32, o);
+      }
+    }
+    bool zeroed = false;
+    if (t == 0 && j * kBN + kBN > w.ctx) {
+      // Keys at or past the context end hold whatever the cache slot
+      // contains; zero their V rows so that P = 0 never meets a NaN.
+      const int vidx = 2 * j + 1;
+      mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 38);
+      if (j * kBN + row >= w.ctx) {
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        uint8_t* v0 = reinterpret_cast<uint8_t*>(sm.kv[ring_slot(vidx)][0]) + row * 128;
+        uint8_t* v1 = reinterpret_cast<uint8_t*>(sm.kv[ring_slot(vidx)][1]) + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          reinterpret_cast<uint4*>(v0)[c] = z;
+          reinterpret_cast<uint4*>(v1)[c] = z;
+        }
+      }
+      zeroed = true;
+    }
+    tmem_wait_st();
+    if (zeroed) fence_proxy_async_smem();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.p_full[t]);
+  }
+
+  // ---- epilogue ----
+  mbar_wait(&sm.o_final, 0, prm.status, abort_flag, 39);
+  tc_fence_after();
+  const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+  float* dst = prm.out + ((long long)(w.q0 + my_row0 + row) * prm.Hq + my_head) * kD;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t o[32];
+    tmem_ld32(o_col + c * 32, o);
+    tmem_wait_ld();
+    if (row < my_rows) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(dst + c * 32 + i) =
+            make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
+                        __uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
+    }
+  }
+}
 
 template <bool kSplitP>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -71,48 +324,62 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, PrefillParams prm) {
   extern __shared__ uint8_t smem_raw[];
-  PrefillSmem<kSplitP>& sm = *reinterpret_cast<PrefillSmem<kSplitP>*>(
+  PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-  const int G = prm.G;
-  const int g = blockIdx.x % G;
-  const int mt = prm.n_mtiles - 1 - (int)(blockIdx.x / G);  // longest tiles launch first
-  const int kvh = blockIdx.y, seq = blockIdx.z;
-  const int h = kvh * G + g;
-  const int q0 = prm.cu_q[seq];
-  const int n_q = prm.cu_q[seq + 1] - q0;
-  if (n_q > prm.n_mtiles * kBM) {
-    if (threadIdx.x == 0 && blockIdx.x == 0 && kvh == 0)
-      record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 21, n_q);
+  // ---- which rows and heads this CTA owns ----
+  Work w;
+  w.kvh = blockIdx.y;
+  w.seq = blockIdx.z;
+  if (prm.pair_heads) {
+    const int n_pairs = prm.G / 2;
+    const int mt = prm.n_mtiles - 1 - (int)(blockIdx.x / n_pairs);  // longest tiles first
+    const int gp = blockIdx.x % n_pairs;
+    w.head[0] = w.kvh * prm.G + 2 * gp;
+    w.head[1] = w.head[0] + 1;
+    w.row0[0] = w.row0[1] = mt * kBM;
+  } else {
+    const int n_units = (prm.n_mtiles + 1) / 2;
+    const int u = n_units - 1 - (int)blockIdx.x;
+    w.head[0] = w.head[1] = w.kvh * prm.G;
+    w.row0[0] = 2 * u * kBM;
+    w.row0[1] = w.row0[0] + kBM;
   }
-  if (mt * kBM >= n_q) return;  // whole CTA: nothing to do
+  w.q0 = prm.cu_q[w.seq];
+  const int n_q = prm.cu_q[w.seq + 1] - w.q0;
+  if (n_q > prm.n_mtiles * kBM && threadIdx.x == 0 && blockIdx.x == 0 && w.kvh == 0)
+    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 21, n_q);
+  if (w.row0[0] >= n_q) return;  // whole CTA: nothing to do
   if (timeout_recorded(prm.status)) return;
-  const int rows = min(kBM, n_q - mt * kBM);
-  const int p_first = prm.q_starts[seq] + mt * kBM;  // position of tile row 0
-  const int p_last = p_first + rows - 1;
-  int ctx = prm.context_lens[seq];
-  if (p_first < 0 || (long long)p_last >= (long long)prm.max_blocks * prm.block_size) {
+  w.q_start = prm.q_starts[w.seq];
+  w.rows[0] = min(kBM, n_q - w.row0[0]);
+  w.rows[1] = max(0, min(kBM, n_q - w.row0[1]));
+  w.p_last0 = w.q_start + w.row0[0] + w.rows[0] - 1;
+  const int p_last =
+      w.rows[1] > 0 ? max(w.p_last0, w.q_start + w.row0[1] + w.rows[1] - 1) : w.p_last0;
+  if (w.q_start < 0 || (long long)p_last >= (long long)prm.max_blocks * prm.block_size) {
     if (threadIdx.x == 0) record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 22, p_last);
     return;
   }
-  if (ctx <= p_last) {
-    if (threadIdx.x == 0) record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 23, ctx);
-    ctx = p_last + 1;
+  w.ctx = prm.context_lens[w.seq];
+  if (w.ctx <= p_last) {
+    if (threadIdx.x == 0) record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 23, w.ctx);
+    w.ctx = p_last + 1;
   }
-  const int n_kv = p_last / kBN + 1;
+  w.n_kv = p_last / kBN + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&sm.k_full[i], 1);
-      mbar_init(&sm.v_full[i], 1);
-      mbar_init(&sm.kv_empty[i], 1);
-      mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_free[i], 4);
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
     }
-    mbar_init(&sm.p_full, 4);
-    mbar_init(&sm.o_done, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], 4);
+    }
+    mbar_init(&sm.o_final, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
   }
@@ -124,225 +391,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tmem_o = tmem + 256;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&sm.q_full, 2 * kHalfBytes);
-      tma_load_3d(sm.q[0], &tm_q, &sm.q_full, 0, h, q0 + mt * kBM);
-      tma_load_3d(sm.q[1], &tm_q, &sm.q_full, 64, h, q0 + mt * kBM);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (j >= 2) mbar_wait(&sm.kv_empty[st], ((j >> 1) - 1) & 1, prm.status, &sm.abort_flag, 30);
-        const int key0 = j * kBN;
-        long long bid = prm.block_tables[(long long)seq * prm.max_blocks + key0 / prm.block_size];
-        if (bid < 0 || bid >= prm.num_blocks) {
-          record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 24, bid);
-          bid = 0;
-        }
-        const int row = (int)((long long)prm.layer * prm.n_slots + bid * prm.block_size +
-                              key0 % prm.block_size);
-        mbar_arrive_expect_tx(&sm.k_full[st], 2 * kHalfBytes);
-        tma_load_3d(sm.k[st][0], &tm_k, &sm.k_full[st], 0, kvh, row);
-        tma_load_3d(sm.k[st][1], &tm_k, &sm.k_full[st], 64, kvh, row);
-        mbar_arrive_expect_tx(&sm.v_full[st], 2 * kHalfBytes);
-        tma_load_3d(sm.v[st][0], &tm_v, &sm.v_full[st], 0, kvh, row);
-        tma_load_3d(sm.v[st][1], &tm_v, &sm.v_full[st], 64, kvh, row);
-      }
-      // Drain: the last loads of each stage have landed before the CTA
-      // can exit (immediate in normal operation; bounded after an abort).
-      for (int j = n_kv - 2 < 0 ? 0 : n_kv - 2; j < n_kv; ++j) {
-        mbar_wait(&sm.k_full[j & 1], (j >> 1) & 1, prm.status, 40);
-        mbar_wait(&sm.v_full[j & 1], (j >> 1) & 1, prm.status, 41);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kBM, kBN, 0, 0);
-      constexpr uint32_t idesc_o = umma_idesc_bf16_f32(kBM, kD, 0, 1);
-      mbar_wait(&sm.q_full, 0, prm.status, &sm.abort_flag, 31);
-      auto issue_s = [&](int j) {
-        const int st = j & 1;
-        mbar_wait(&sm.k_full[st], (j >> 1) & 1, prm.status, &sm.abort_flag, 32);
-        if (j >= 2) mbar_wait(&sm.s_free[st], ((j >> 1) - 1) & 1, prm.status, &sm.abort_flag, 33);
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          const uint32_t koff = (uint32_t)(k & 3) * 32;
-          const uint64_t a = umma_desc_sw128(smem_u32(sm.q[k >> 2]) + koff, 16, 1024);
-          const uint64_t b = umma_desc_sw128(smem_u32(sm.k[st][k >> 2]) + koff, 16, 1024);
-          umma_bf16(tmem + st * 128, a, b, idesc_s, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&sm.s_full[st]);
-      };
-      issue_s(0);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (j + 1 < n_kv) issue_s(j + 1);
-        mbar_wait(&sm.p_full, j & 1, prm.status, &sm.abort_flag, 34);
-        mbar_wait(&sm.v_full[st], (j >> 1) & 1, prm.status, &sm.abort_flag, 35);
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < kBN / 16; ++k) {
-          const uint64_t a =
-              umma_desc_sw128(smem_u32(sm.p[k >> 2]) + (uint32_t)(k & 3) * 32, 16, 1024);
-          const uint64_t b =
-              umma_desc_sw128(smem_u32(sm.v[st][0]) + (uint32_t)k * 16 * 128, kHalfBytes, 1024);
-          umma_bf16(tmem_o, a, b, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        if constexpr (kSplitP) {
-#pragma unroll
-          for (int k = 0; k < kBN / 16; ++k) {
-            const uint64_t a =
-                umma_desc_sw128(smem_u32(sm.p_lo[k >> 2]) + (uint32_t)(k & 3) * 32, 16, 1024);
-            const uint64_t b = umma_desc_sw128(smem_u32(sm.v[st][0]) + (uint32_t)k * 16 * 128,
-                                               kHalfBytes, 1024);
-            umma_bf16(tmem_o, a, b, idesc_o, 1u);
-          }
-        }
-        umma_commit(&sm.o_done);
-        umma_commit(&sm.kv_empty[st]);
-      }
-      // Drain: every MMA has completed before TMEM is released.
-      mbar_wait(&sm.o_done, (n_kv - 1) & 1, prm.status, 42);
-    }
+  // 384 threads x 168 registers at launch: warpgroup 0 (TMA, MMA, two idle
+  // warps) gives back down to 112, the two softmax warpgroups take 192 each
+  // (128*112 + 256*192 = 63488 <= 384*168 = 64512).
+  if (warp < 4) {
+    regs_dec<112>();
+    if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm, w);
+    if (warp == 1 && lane == 0) mma_role<kSplitP>(sm, tmem, prm, w);
   } else {
-    // ------------------------------------------------------------ softmax
-    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32)
-    const int row = quad * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    // Rows past the end of the sequence mimic its last row (never stored).
-    const int pos_row = p_first + min(row, rows - 1);
-    const float sc = prm.scale_log2;
-    float m_used = -INFINITY;
-    float l = 0.0f;
-
-    for (int j = 0; j < n_kv; ++j) {
-      const int st = j & 1;
-      mbar_wait(&sm.s_full[st], (j >> 1) & 1, prm.status, &sm.abort_flag, 36);
-      tc_fence_after();
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_off + st * 128 + c * 32, sr[c]);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.s_free[st]);
-
-      const int key0 = j * kBN;
-      const int lim = pos_row - key0;  // keys c <= lim are visible (causal)
-      float mt = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(sr[c][i]) * sc;
-          x = (c * 32 + i <= lim) ? x : -INFINITY;
-          sr[c][i] = __float_as_uint(x);
-          mt = fmaxf(mt, x);
-        }
-      }
-      const float m_new = fmaxf(m_used, mt);
-      float alpha = 1.0f;
-      bool rescale = false;
-      if (m_new > m_used + kRescaleThreshold) {
-        alpha = fast_exp2(m_used - m_new);
-        rescale = j > 0;
-        m_used = m_new;
-      }
-      // P as bf16 pairs; with kSplitP also the bf16 remainder P - bf16(P),
-      // so that the two P.V passes together carry ~16 significant bits.
-      uint32_t pk[64];
-      uint32_t pl[kSplitP ? 64 : 1];
-      float rs = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = fast_exp2(__uint_as_float(sr[c][i]) - m_used);
-          const float p1 = fast_exp2(__uint_as_float(sr[c][i + 1]) - m_used);
-          const uint32_t w = pack_bf16x2(p0, p1);
-          pk[c * 16 + i / 2] = w;
-          if constexpr (kSplitP) {
-            pl[c * 16 + i / 2] = pack_bf16x2(p0 - bf16lo_to_f32(w), p1 - bf16hi_to_f32(w));
-            rs += p0 + p1;
-          } else {
-            rs += bf16lo_to_f32(w) + bf16hi_to_f32(w);
-          }
-        }
-      }
-      l = l * alpha + rs;
-
-      if (j > 0) {
-        // PV(j-1) has finished: O is stable and the P buffer is free.
-        mbar_wait(&sm.o_done, (j - 1) & 1, prm.status, &sm.abort_flag, 37);
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tmem_o + lane_off + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem_o + lane_off + c * 32, o);
-          }
-          tmem_wait_st();
-        }
-      }
-      if (key0 + kBN > ctx) {
-        // Keys at or past the context end hold whatever the cache slot
-        // contains; zero their V rows so that P=0 never meets a NaN.
-        mbar_wait(&sm.v_full[st], (j >> 1) & 1, prm.status, &sm.abort_flag, 38);
-        if (key0 + row >= ctx) {
-          uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.v[st][0]) + row * 128)[c] = z;
-            reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.v[st][1]) + row * 128)[c] = z;
-          }
-        }
-      }
-      // P row -> shared memory, UMMA K-major layout with 128-byte swizzle.
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const int half = c >> 3, cc = c & 7;
-        const int off = row * 128 + ((cc ^ (row & 7)) * 16);
-        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.p[half]) + off) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-        if constexpr (kSplitP)
-          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.p_lo[half]) + off) =
-              make_uint4(pl[4 * c], pl[4 * c + 1], pl[4 * c + 2], pl[4 * c + 3]);
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full);
-    }
-
-    // ------------------------------------------------------------ epilogue
-    mbar_wait(&sm.o_done, (n_kv - 1) & 1, prm.status, &sm.abort_flag, 39);
-    tc_fence_after();
-    const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
-    float* dst = prm.out + ((long long)(q0 + mt * kBM + row) * prm.Hq + h) * kD;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t o[32];
-      tmem_ld32(tmem_o + lane_off + c * 32, o);
-      tmem_wait_ld();
-      if (row < rows) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(dst + c * 32 + i) =
-              make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
-                          __uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
-      }
-    }
+    regs_inc<192>();
+    softmax_role<kSplitP>(sm, tmem, prm, w, warp, lane);
   }
 
   tc_fence_before();
@@ -357,7 +416,7 @@ template <bool kSplitP>
 nvattn_status launch_variant(dim3 grid, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                              const CUtensorMap& tm_v, const PrefillParams& prm,
                              cudaStream_t stream) {
-  const size_t smem = sizeof(PrefillSmem<kSplitP>) + 1024;
+  const size_t smem = sizeof(PrefillSmem) + 1024;
   // The attribute is per device; remember which devices have it.
   static unsigned long long attr_set_mask = 0;
   int dev = 0;
@@ -403,6 +462,7 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   prm.block_size = h->cfg.block_size;
   prm.max_blocks = max_blocks;
   prm.n_mtiles = (max_q_len + kBM - 1) / kBM;
+  prm.pair_heads = prm.G >= 2 ? 1 : 0;
   prm.n_slots = h->n_slots;
   prm.num_blocks = h->cfg.num_blocks;
   prm.scale_log2 = h->cfg.scale * kLog2e;
@@ -413,11 +473,11 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   prm.out = out;
   prm.status = h->status_dev;
 
-  const long long gx = (long long)prm.n_mtiles * prm.G;
+  const long long gx = prm.pair_heads ? (long long)prm.n_mtiles * (prm.G / 2)
+                                      : (long long)(prm.n_mtiles + 1) / 2;
   if (gx > 0x7fffffffLL || Hkv > 65535 || n_seqs > 65535) return NVATTN_ERR_UNSUPPORTED;
   dim3 grid((unsigned)gx, Hkv, n_seqs);
-  if (h->cfg.prefill_split_p)
-    return launch_variant<true>(grid, tm_q, *tk, *tv, prm, stream);
+  if (h->cfg.prefill_split_p) return launch_variant<true>(grid, tm_q, *tk, *tv, prm, stream);
   return launch_variant<false>(grid, tm_q, *tk, *tv, prm, stream);
 }
 
