@@ -86,6 +86,12 @@ def prefill_workload(kind):
         lens = rng.integers(512, 4097, 8).astype(np.int64)
         cached = np.where(lens > 1024, 1024, 256 * ((lens - 1) // 256)).astype(np.int64)
         n_shared = 4
+    elif kind == "chunk_small":
+        # profiling-sized case of the chunk workload: 2 sequences, 32k context
+        name, Hq, Hkv = "chunked_prefill_qwen3_32b_2x2048_at_30720", 64, 8
+        lens = np.full(2, 32768, np.int64)
+        cached = np.full(2, 30720, np.int64)
+        n_shared = 0
     else:
         name, Hq, Hkv = "chunked_prefill_qwen3_32b_16x2048_at_129024", 64, 8
         lens = np.full(16, 131072, np.int64)
@@ -120,7 +126,7 @@ def bench_prefill(kind, args, world, rank, device):
     max_ctx = int(cl.max())
     cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
                               max_seqs=len(lens), max_context=max_ctx, max_position=max_ctx,
-                              device=device.index)
+                              device=device.index, prefill_split_p=args.prefill_split)
     h = nvattn.Handle(cfg)
     gen = torch.Generator(device=device)
     gen.manual_seed(2000 + rank)
@@ -178,7 +184,7 @@ def bench_prefill(kind, args, world, rank, device):
     h.close()
     fields = {"workload": name, "q_heads": Hq, "kv_heads": Hkv, "n_seqs": len(lens),
               "new_tokens": T, "sum_context": int(cl.sum()), "flops_per_step": flops,
-              "steps": steps, "p_split": 1}
+              "steps": steps, "p_split": args.prefill_split}
     return fields, pre_ms, step_ms
 
 
@@ -367,6 +373,8 @@ def main():
     ap.add_argument("--prefill", default="prefix_hit,chunk",
                     help="comma list of prefill workloads to time (prefix_hit, chunk) or none")
     ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--prefill-split", type=int, default=1, choices=[0, 1],
+                    help="prefill P.V precision: 1 = bf16 hi+lo split (default), 0 = one pass")
     ap.add_argument("--only-prefill", action="store_true",
                     help="skip the decode workload (for profiling the prefill kernel)")
     args = ap.parse_args()

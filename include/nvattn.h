@@ -63,7 +63,9 @@ typedef enum nvattn_status {
   NVATTN_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed */
   NVATTN_ERR_TIMEOUT = 4,      /* a bounded device wait ran out */
   NVATTN_ERR_UNSUPPORTED = 5,  /* shape not built (head_dim != 128, ...) */
-  NVATTN_ERR_NO_MEMORY = 6     /* workspace allocation failed */
+  NVATTN_ERR_NO_MEMORY = 6,    /* workspace allocation failed */
+  NVATTN_ERR_SCRATCH_LIMIT = 7 /* nvattn_paged_decode_noalloc: the call needs
+                                  more split-KV scratch than its fixed array */
 } nvattn_status;
 
 typedef enum nvattn_dtype {
@@ -198,6 +200,44 @@ NVATTN_API nvattn_status nvattn_paged_prefill(
     const int32_t* block_tables_dev, int max_blocks, int max_q_len,
     const uint16_t* k_cache_dev, const uint16_t* v_cache_dev, float* out_dev,
     nvattn_stream_t stream);
+
+/* ---- decode without any allocation -------------------------------------- */
+
+/* Where a kernel records the first error it meets (device memory owned by
+ * the caller; zero it before use).  Same meaning as nvattn_get_error's
+ * status and detail. */
+typedef struct nvattn_device_status {
+  int32_t code;   /* nvattn_status */
+  int32_t site;   /* which check fired */
+  int64_t detail; /* the offending value */
+} nvattn_device_status;
+
+/* No counterpart in the reference: an extra entry point of this library.
+ *
+ * nvattn_paged_decode for callers that cannot allocate device memory: an
+ * engine that has already handed nearly all of the GPU to its KV cache (the
+ * reference sizes the cache from gpu_memory_utilization = 0.9), or a host
+ * that may not call cudaMalloc while serving a step, where an allocation
+ * could fail or synchronise the device.  It needs no handle and allocates
+ * nothing: cfg supplies the shapes (as for nvattn_create), the caller passes
+ * every input and output, and the split-KV partial results go to a fixed
+ * 32 MiB device array inside the library (held by every GPU that loads the
+ * library until the process exits).  A call whose partials do not fit
+ * (n_seqs * n_q_heads * splits * 520 bytes > 32 MiB, splits chosen as for a
+ * handle created from cfg) returns NVATTN_ERR_SCRATCH_LIMIT.
+ * It runs on the caller's current device, which must be cfg->device.  The
+ * first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  All calls share the one array and
+ * it keeps the last call's contents: calls whose kernels overlap on the GPU
+ * (other streams, other threads) race on it, so serialise them.
+ * status_dev (nullable) receives errors the kernels detect; results equal
+ * nvattn_paged_decode's for the same cfg. */
+NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
+    const nvattn_config* cfg, int layer, int n_seqs, const float* q_dev,
+    const uint16_t* k_cache_dev, const uint16_t* v_cache_dev,
+    const int32_t* block_tables_dev, int max_blocks,
+    const int32_t* context_lens_dev, int max_context_len, float* out_dev,
+    nvattn_device_status* status_dev, nvattn_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -112,6 +112,8 @@ const char* nvattn_status_string(nvattn_status s) {
     case NVATTN_ERR_TIMEOUT: return "bounded device wait timed out";
     case NVATTN_ERR_UNSUPPORTED: return "unsupported shape";
     case NVATTN_ERR_NO_MEMORY: return "out of device memory";
+    case NVATTN_ERR_SCRATCH_LIMIT:
+      return "split-KV partials exceed the 32 MiB static scratch of nvattn_paged_decode_noalloc";
   }
   return "unknown status";
 }

@@ -371,16 +371,29 @@ nvattn_status launch_g(const CUtensorMap* tk, const CUtensorMap* tv, const Decod
 // Tokens per split: whole 256-token blocks, small enough that the grid fills
 // the GPU several times over when sequences are short, and at most 2048 so
 // that log-uniform context lengths still balance across SMs.
-int decode_split_tokens(const nvattn_handle* h, int n_seqs, int max_context_len) {
-  const int bs = h->cfg.block_size;
-  const long long target_ctas = 4LL * 2 * h->sm_count;
-  long long units = (long long)n_seqs * h->cfg.n_kv_heads;
+static int split_tokens_for(int sm_count, int block_size, int n_kv_heads, int max_splits,
+                            int n_seqs, int max_context_len) {
+  const long long target_ctas = 4LL * 2 * sm_count;
+  const long long units = (long long)n_seqs * n_kv_heads;
   int split = 2048;
-  while (split > bs && units * ((max_context_len + split - 1) / split) < target_ctas) split /= 2;
-  if (split < bs) split = bs;
+  while (split > block_size && units * ((max_context_len + split - 1) / split) < target_ctas)
+    split /= 2;
+  if (split < block_size) split = block_size;
   // never more splits per sequence than the workspace holds
-  while ((max_context_len + split - 1) / split > h->max_splits) split *= 2;
+  while ((max_context_len + split - 1) / split > max_splits) split *= 2;
   return split;
+}
+
+// Splits per (sequence, kv head) that the workspace of a handle created with
+// this max_context holds (the same rule nvattn_create applies).
+static int workspace_max_splits(const nvattn_config& c) {
+  const long long splits = (c.max_context + c.block_size - 1) / c.block_size;
+  return (int)(splits < 64 ? splits : 64);
+}
+
+int decode_split_tokens(const nvattn_handle* h, int n_seqs, int max_context_len) {
+  return split_tokens_for(h->sm_count, h->cfg.block_size, h->cfg.n_kv_heads, h->max_splits,
+                          n_seqs, max_context_len);
 }
 
 nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const float* q,
@@ -424,4 +437,115 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
   }
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free decode (nvattn_paged_decode_noalloc).
+//
+// The split-KV partials live in this file-scope device array instead of a
+// handle's cudaMalloc'd workspace.  Every GPU that loads the library holds
+// these 32 MiB until the process exits.  The array's name is only a host-side
+// stand-in for the device symbol, so the host fetches its real device address
+// with cudaGetSymbolAddress, once per device, and passes that to the kernel.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static_assert(sizeof(DeviceStatus) == sizeof(nvattn_device_status), "status layout");
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void* g_noalloc_scratch_addr[kMaxDevices];  // device address per device (set once)
+int g_noalloc_sm_count[kMaxDevices];
+}  // namespace
+
 }  // namespace nvattn
+
+extern "C" NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
+    const nvattn_config* cfg, int layer, int n_seqs, const float* q_dev,
+    const uint16_t* k_cache_dev, const uint16_t* v_cache_dev, const int32_t* block_tables_dev,
+    int max_blocks, const int32_t* context_lens_dev, int max_context_len, float* out_dev,
+    nvattn_device_status* status_dev, nvattn_stream_t stream) {
+  using namespace nvattn;
+  if (cfg == nullptr) return NVATTN_ERR_INVALID_ARG;
+  const nvattn_config& c = *cfg;
+  if (c.n_layer <= 0 || c.n_q_heads <= 0 || c.n_kv_heads <= 0 || c.num_blocks <= 0 ||
+      c.block_size <= 0 || c.max_context <= 0 || c.n_q_heads % c.n_kv_heads != 0 ||
+      !(c.scale > 0.0f))
+    return NVATTN_ERR_INVALID_ARG;
+  const int G = c.n_q_heads / c.n_kv_heads;
+  if (c.head_dim != kD || c.block_size % 128 != 0 || c.block_size > 1024 ||
+      !(G == 1 || G == 2 || G == 4 || G == 8))
+    return NVATTN_ERR_UNSUPPORTED;
+  const long long n_slots = c.num_blocks * (long long)c.block_size;
+  if ((long long)c.n_layer * n_slots >= (1LL << 31)) return NVATTN_ERR_UNSUPPORTED;
+  if (layer < 0 || layer >= c.n_layer || n_seqs < 0 || max_blocks <= 0 || max_context_len < 0 ||
+      max_context_len > c.max_context ||
+      (long long)max_context_len > (long long)max_blocks * c.block_size)
+    return NVATTN_ERR_INVALID_ARG;
+  if (n_seqs == 0) return NVATTN_OK;
+  const void* ptrs[] = {q_dev, k_cache_dev, v_cache_dev, out_dev};
+  for (const void* p : ptrs)
+    if (p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15u) != 0) return NVATTN_ERR_INVALID_ARG;
+  if (block_tables_dev == nullptr || context_lens_dev == nullptr) return NVATTN_ERR_INVALID_ARG;
+
+  // Runs on the caller's current device, which must be cfg->device.
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
+  if (dev != c.device || dev < 0 || dev >= kMaxDevices) return NVATTN_ERR_INVALID_ARG;
+  // One-time set-up on this device: the scratch's device address and the SM
+  // count (neither allocates).
+  if (g_noalloc_scratch_addr[dev] == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || addr == nullptr)
+      return NVATTN_ERR_CUDA;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return NVATTN_ERR_CUDA;
+    g_noalloc_sm_count[dev] = sms;
+    g_noalloc_scratch_addr[dev] = addr;
+  }
+
+  // Same split rule as a handle created from this config, so the result
+  // equals nvattn_paged_decode's.
+  const int split = split_tokens_for(g_noalloc_sm_count[dev], c.block_size, c.n_kv_heads,
+                                     workspace_max_splits(c), n_seqs, max_context_len);
+  const int n_splits = max_context_len > 0 ? (max_context_len + split - 1) / split : 1;
+  const size_t rows = n_splits > 1 ? (size_t)n_seqs * c.n_q_heads * n_splits : 0;
+  if (rows * (kD + 2) * sizeof(float) > kNoAllocScratchBytes) return NVATTN_ERR_SCRATCH_LIMIT;
+
+  CUtensorMap tk, tv;
+  nvattn_status st = encode_tensor_map_3d(&tk, k_cache_dev, kD, (uint64_t)c.n_kv_heads,
+                                          (uint64_t)c.n_layer * (uint64_t)n_slots, kD * 2,
+                                          (uint64_t)c.n_kv_heads * kD * 2, kD, 1, kTile, 0);
+  if (st != NVATTN_OK) return st;
+  st = encode_tensor_map_3d(&tv, v_cache_dev, kD, (uint64_t)c.n_kv_heads,
+                            (uint64_t)c.n_layer * (uint64_t)n_slots, kD * 2,
+                            (uint64_t)c.n_kv_heads * kD * 2, kD, 1, kTile, 0);
+  if (st != NVATTN_OK) return st;
+
+  float* scratch = static_cast<float*>(g_noalloc_scratch_addr[dev]);
+  DecodeParams prm;
+  prm.Hq = c.n_q_heads;
+  prm.Hkv = c.n_kv_heads;
+  prm.layer = layer;
+  prm.block_size = c.block_size;
+  prm.max_blocks = max_blocks;
+  prm.max_context = max_context_len;
+  prm.split_tokens = split;
+  prm.max_splits = n_splits;  // partial-row stride
+  prm.n_slots = n_slots;
+  prm.num_blocks = c.num_blocks;
+  prm.scale_log2 = c.scale * kLog2e;
+  prm.q = q_dev;
+  prm.block_tables = block_tables_dev;
+  prm.context_lens = context_lens_dev;
+  prm.out = out_dev;
+  prm.ws_o = scratch;
+  prm.ws_ml = scratch + rows * kD;
+  prm.status = reinterpret_cast<DeviceStatus*>(status_dev);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (G) {
+    case 1: return launch_g<1>(&tk, &tv, prm, n_seqs, max_context_len, s);
+    case 2: return launch_g<2>(&tk, &tv, prm, n_seqs, max_context_len, s);
+    case 4: return launch_g<4>(&tk, &tv, prm, n_seqs, max_context_len, s);
+    default: return launch_g<8>(&tk, &tv, prm, n_seqs, max_context_len, s);
+  }
+}

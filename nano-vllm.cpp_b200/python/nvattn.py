@@ -29,7 +29,9 @@ EXPORTED = [
     "nvattn_config_init_qwen3", "nvattn_create", "nvattn_destroy", "nvattn_status_string",
     "nvattn_version", "nvattn_get_error", "nvattn_plan_prefill", "nvattn_plan_decode",
     "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
+    "nvattn_paged_decode_noalloc",
 ]
+ERR_SCRATCH_LIMIT = 7
 
 
 class NvattnError(RuntimeError):
@@ -94,6 +96,8 @@ def lib():
                                           _vp, _vp]
         L.nvattn_paged_prefill.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32,
                                            _i32, _vp, _vp, _vp, _vp]
+        L.nvattn_paged_decode_noalloc.argtypes = [ctypes.POINTER(Config), _i32, _i32, _vp, _vp,
+                                                  _vp, _vp, _i32, _vp, _i32, _vp, _vp, _vp]
         # every other entry point returns nvattn_status (ctypes' default c_int)
         _lib = L
     return _lib
@@ -201,6 +205,19 @@ class Handle:
         if check:
             _check(st, "nvattn_paged_prefill")
         return st
+
+
+def decode_noalloc(cfg, layer, q, k_cache, v_cache, block_tables, context_lens,
+                   max_context_len, out, status=None, stream=None):
+    """nvattn_paged_decode_noalloc: decode without a handle and without any
+    device allocation (split-KV partials go to the library's fixed 32 MiB
+    scratch).  `status` (optional) is a caller-owned 16-byte device buffer
+    (e.g. torch.zeros(4, dtype=torch.int32, device=...)) that receives the
+    first error a kernel detects.  Returns the status code."""
+    return lib().nvattn_paged_decode_noalloc(
+        ctypes.byref(cfg), layer, context_lens.shape[0], _ptr(q), _ptr(k_cache), _ptr(v_cache),
+        _ptr(block_tables), block_tables.shape[1], _ptr(context_lens), int(max_context_len),
+        _ptr(out), _ptr(status), _stream_ptr(stream))
 
 
 def kv_head_shard(n_q_heads, n_kv_heads, world, rank):
