@@ -1,4 +1,5 @@
-// decode.cu -- paged GQA split-KV decode attention over the BF16 block cache.
+// decode.cu -- paged GQA split-KV decode attention over the BF16 block cache,
+// on the tcgen05 tensor cores (sm_100a).
 //
 // Replaces the reference's decode attention path: LoadHistoryKV's per-token
 // gather through block_table + bf16->f32 + reorder (src/engine/
@@ -8,15 +9,26 @@
 // row over all sequences' concatenated history (O(B * sum L)); here each
 // (sequence, kv head) reads only its own blocks, once, for all its GQA heads.
 //
-// Grid (split, kv_head, seq).  A split is a run of split_tokens tokens of one
-// sequence.  Warp 4 is the producer: one lane streams 64-token K and V tiles
-// (16 KiB each, TMA boxes {128, 1, 64} over the cache viewed as
-// [layer*slot][kv_head][128]) into a 3-stage shared-memory ring guarded by
-// mbarriers.  Warps 0-3 are consumers: each owns 16 tokens of a tile; a lane
-// owns 4 head dims.  Scores use a transposed butterfly reduction, softmax is
-// online in the log2 domain, and P.V accumulates in fp32 registers.  A split
-// writes either the final row (single split) or its (m, l, O) partial, which
-// paged_decode_combine_kernel merges.
+// Grid (split, kv head, sequence); a split is a run of split_tokens tokens.
+// 128-token K and V tiles (32 KiB each, two TMA boxes {64, 1, 128} with
+// 128-byte swizzle over the cache viewed as [layer*slot][kv head][128])
+// stream through a 3-slot ring; two CTAs share an SM.
+//   warp 0      TMA producer.
+//   warp 1      TMEM allocation; one lane issues the MMAs:
+//                 S^T = K Q^T   M = 128 tokens, N = 16, K = 128 dims
+//                 O^T += V^T P^T M = 128 dims, N = 16, K = 128 tokens
+//               N holds the G query heads twice: bf16(q) in columns [0, G)
+//               and the bf16 remainder q - bf16(q) in [G, 2G) (zero above),
+//               so S carries ~16 significant bits of q; P^T is split the
+//               same way.  The padding to N = 16 makes the split free.
+//   warps 2-5   thread = token of the tile (S^T lane) and = head dim (O^T
+//               lane): per-head tile max by shuffles + shared memory, online
+//               softmax in the log2 domain with lazy O rescaling (only when a
+//               head's max grows by more than 2^8), per-thread partial row
+//               sums reduced once per split, P^T written to shared memory in
+//               the UMMA operand layout.
+// A split writes either the final row (single split) or its (m, l, O)
+// partial, which paged_decode_combine_kernel merges.
 #include "common.cuh"
 #include "internal.h"
 
@@ -24,13 +36,14 @@ namespace nvattn {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kTile = 64;
-constexpr int kStages = 3;
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kTokPerWarp = kTile / kConsumerWarps;  // 16
-constexpr int kTileBytes = kTile * kD * 2;           // 16 KiB
+constexpr int kTile = 128;  // tokens per KV tile
+constexpr int kSlots = 3;
+constexpr int kThreads = 6 * 32;
+constexpr int kHalfBytes = 128 * 64 * 2;  // one 128-row x 64-column bf16 box: 16 KiB
+constexpr int kN = 16;                    // MMA N: heads x {hi, lo}, zero padded
+constexpr uint32_t kTmemCols = 64;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct DecodeParams {
   int Hq, Hkv, layer, block_size, max_blocks, split_tokens, max_splits;
@@ -48,63 +61,35 @@ struct DecodeParams {
 
 template <int G>
 struct __align__(1024) DecodeSmem {
-  uint16_t k[kStages][kTile * kD];
-  uint16_t v[kStages][kTile * kD];
-  float s[G][kTile];  // scores, log2 domain
-  float p[kTile][G];  // probabilities
-  float alpha[G];
-  float m_run[G];
-  float l_run[G];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint16_t kv[kSlots][2][kTile * 64];  // [slot][d half][token][64]
+  uint16_t qt[2][kN * 64];             // Q^T operand: [d half][row][64]
+  uint16_t pt[2][kN * 64];             // P^T operand: [token half][row][64]
+  float red[2][4][kN];                 // per-warp tile maxima (double-buffered)
+  float red_sum[4][kN];
+  uint64_t full[kSlots], empty[kSlots];
+  uint64_t q_ready, s_full[2], p_full, o_done;
+  uint32_t tmem_base;
   int abort_flag;  // raised by the first wait that times out
 };
 
-// Butterfly transpose-reduction of V per-lane partial sums across the warp.
-// Afterwards, for V >= 32 lane l holds the totals of indices l*(V/32) + j in
-// v[j]; for V < 32 every lane holds the total of index l >> (5 - log2 V).
-template <int V>
-__device__ __forceinline__ void transpose_reduce(float (&v)[V], int lane) {
-  int n = V;
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    if (n > 1) {
-      const bool upper = (lane & o) != 0;
-#pragma unroll
-      for (int i = 0; i < V / 2; ++i) {
-        if (i < n / 2) {
-          const float send = upper ? v[i] : v[i + n / 2];
-          const float keep = upper ? v[i + n / 2] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-      }
-      n >>= 1;
-    } else {
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-    }
-  }
+__device__ __forceinline__ int ring_slot(int idx) { return idx % kSlots; }
+__device__ __forceinline__ uint32_t ring_parity(int idx) { return (uint32_t)(idx / kSlots) & 1u; }
+
+// Byte offset of element (row n, column c) of a K-major, 128-byte-swizzled
+// operand region of 64 columns: rows at 128 B, 16-byte chunks XOR row % 8.
+__device__ __forceinline__ int sw128_offset(int n, int c) {
+  return n * 128 + ((((c >> 3) ^ n) & 7) << 4) + (c & 7) * 2;
 }
 
-template <int G>
-__device__ __forceinline__ void load_p(const float* row, float (&pg)[G]) {
-  if constexpr (G == 1) {
-    pg[0] = row[0];
-  } else if constexpr (G == 2) {
-    const float2 a = *reinterpret_cast<const float2*>(row);
-    pg[0] = a.x; pg[1] = a.y;
-  } else {
-#pragma unroll
-    for (int i = 0; i < G / 4; ++i) {
-      const float4 a = reinterpret_cast<const float4*>(row)[i];
-      pg[4 * i] = a.x; pg[4 * i + 1] = a.y; pg[4 * i + 2] = a.z; pg[4 * i + 3] = a.w;
-    }
-  }
+__device__ __forceinline__ uint16_t bf16_rn(float x) {
+  return (uint16_t)(cvt_bf16x2(x, 0.0f) & 0xffffu);
 }
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, DecodeParams prm) {
+  static_assert(2 * G <= kN, "GQA group too large for N = 16");
   extern __shared__ uint8_t smem_raw[];
   DecodeSmem<G>& sm = *reinterpret_cast<DecodeSmem<G>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -124,198 +109,276 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int t_end = min(ctx, t_begin + prm.split_tokens);
   const int n_tiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
   const int n_splits = ctx > 0 ? (ctx + prm.split_tokens - 1) / prm.split_tokens : 1;
+  volatile int* abort_flag = &sm.abort_flag;
 
   if (threadIdx.x == 0) {
-#pragma unroll
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kSlots; ++i) {
       mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], kConsumerWarps);
+      mbar_init(&sm.empty[i], 1);
     }
+    mbar_init(&sm.q_ready, 4);
+    mbar_init(&sm.s_full[0], 1);
+    mbar_init(&sm.s_full[1], 1);
+    mbar_init(&sm.p_full, 4);
+    mbar_init(&sm.o_done, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
   }
-  if (threadIdx.x < G) {
-    sm.m_run[threadIdx.x] = -INFINITY;
-    sm.l_run[threadIdx.x] = 0.0f;
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
   }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
 
-  if (warp == kConsumerWarps) {
-    // ---------------- producer ----------------
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       const uint64_t policy = l2_policy_evict_first();
-      for (int i = 0; i < n_tiles; ++i) {
-        const int stage = i % kStages;
-        if (i >= kStages) mbar_wait(&sm.empty[stage], ((i / kStages) & 1) ^ 1, prm.status, &sm.abort_flag, 11);
-        const int tok = t_begin + i * kTile;
-        const int bi = tok / prm.block_size;
-        long long bid = prm.block_tables[(long long)seq * prm.max_blocks + bi];
-        if (bid < 0 || bid >= prm.num_blocks) {
-          record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 12, bid);
-          bid = 0;  // keep the pipeline flowing; the result is flagged invalid
+      const int n_loads = 2 * n_tiles;
+      long long bid = 0;
+      for (int idx = 0; idx < n_loads; ++idx) {
+        const int slot = ring_slot(idx);
+        if (idx >= kSlots)
+          mbar_wait(&sm.empty[slot], ring_parity(idx) ^ 1u, prm.status, abort_flag, 11);
+        const int tok = t_begin + (idx >> 1) * kTile;
+        if ((idx & 1) == 0) {
+          bid = prm.block_tables[(long long)seq * prm.max_blocks + tok / prm.block_size];
+          if (bid < 0 || bid >= prm.num_blocks) {
+            record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 12, bid);
+            bid = 0;  // keep the pipeline flowing; the result is flagged invalid
+          }
         }
         const int row = (int)((long long)prm.layer * prm.n_slots + bid * prm.block_size +
                               tok % prm.block_size);
-        mbar_arrive_expect_tx(&sm.full[stage], 2 * kTileBytes);
-        tma_load_3d_hint(sm.k[stage], &tm_k, &sm.full[stage], 0, kvh, row, policy);
-        tma_load_3d_hint(sm.v[stage], &tm_v, &sm.full[stage], 0, kvh, row, policy);
+        const CUtensorMap* map = (idx & 1) ? &tm_v : &tm_k;
+        mbar_arrive_expect_tx(&sm.full[slot], 2 * kHalfBytes);
+        tma_load_3d_hint(sm.kv[slot][0], map, &sm.full[slot], 0, kvh, row, policy);
+        tma_load_3d_hint(sm.kv[slot][1], map, &sm.full[slot], 64, kvh, row, policy);
       }
+      // Drain: the last load of every slot has landed before the CTA exits.
+      for (int idx = max(0, n_loads - kSlots); idx < n_loads; ++idx)
+        mbar_wait(&sm.full[ring_slot(idx)], ring_parity(idx), prm.status, 14);
     }
-    return;
-  }
-
-  // ---------------- consumers ----------------
-  float qr[G][4];
-  {
-    const float* qp = prm.q + ((long long)seq * prm.Hq + (long long)kvh * G) * kD + 4 * lane;
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kTile, kN, 0, 0);
+      constexpr uint32_t idesc_o = umma_idesc_bf16_f32(kD, kN, 1, 0);
+      mbar_wait(&sm.q_ready, 0, prm.status, abort_flag, 15);
+      auto issue_s = [&](int j) {
+        const int slot = ring_slot(2 * j);
+        mbar_wait(&sm.full[slot], ring_parity(2 * j), prm.status, abort_flag, 16);
+        tc_fence_after();
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float4 a = *reinterpret_cast<const float4*>(qp + g * kD);
-      qr[g][0] = a.x * prm.scale_log2;
-      qr[g][1] = a.y * prm.scale_log2;
-      qr[g][2] = a.z * prm.scale_log2;
-      qr[g][3] = a.w * prm.scale_log2;
-    }
-  }
-  float acc[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[g][j] = 0.0f;
-
-  constexpr int TB = (G >= 8) ? 8 : 16;  // tokens per reduction batch
-  constexpr int V = G * TB;              // values reduced per batch
-
-  for (int i = 0; i < n_tiles; ++i) {
-    const int stage = i % kStages;
-    mbar_wait(&sm.full[stage], (i / kStages) & 1, prm.status, &sm.abort_flag, 13);
-    const uint16_t* kt = sm.k[stage];
-    const uint16_t* vt = sm.v[stage];
-    const int tok0 = t_begin + i * kTile;
-    const int n_valid = min(kTile, t_end - tok0);
-
-    // ---- scores for this warp's 16 tokens ----
-#pragma unroll
-    for (int b = 0; b < kTokPerWarp / TB; ++b) {
-      float vals[V];
-#pragma unroll
-      for (int tt = 0; tt < TB; ++tt) {
-        const int tl = warp * kTokPerWarp + b * TB + tt;
-        const uint2 kr = *reinterpret_cast<const uint2*>(kt + tl * kD + 4 * lane);
-        const float k0 = bf16lo_to_f32(kr.x), k1 = bf16hi_to_f32(kr.x);
-        const float k2 = bf16lo_to_f32(kr.y), k3 = bf16hi_to_f32(kr.y);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float a = qr[g][0] * k0;
-          a = fmaf(qr[g][1], k1, a);
-          a = fmaf(qr[g][2], k2, a);
-          a = fmaf(qr[g][3], k3, a);
-          vals[tt * G + g] = a;
+        for (int k = 0; k < kD / 16; ++k) {
+          const uint32_t koff = (uint32_t)(k & 3) * 32;
+          const uint64_t a = umma_desc_sw128(smem_u32(sm.kv[slot][k >> 2]) + koff, 16, 1024);
+          const uint64_t b = umma_desc_sw128(smem_u32(sm.qt[k >> 2]) + koff, 16, 1024);
+          umma_bf16(tmem + (j & 1) * kN, a, b, idesc_s, k > 0 ? 1u : 0u);
         }
-      }
-      transpose_reduce<V>(vals, lane);
-      if constexpr (V >= 32) {
+        umma_commit(&sm.s_full[j & 1]);
+        umma_commit(&sm.empty[slot]);
+      };
+      issue_s(0);
+      for (int j = 0; j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) issue_s(j + 1);
+        const int vslot = ring_slot(2 * j + 1);
+        mbar_wait(&sm.p_full, j & 1, prm.status, abort_flag, 17);
+        mbar_wait(&sm.full[vslot], ring_parity(2 * j + 1), prm.status, abort_flag, 18);
+        tc_fence_after();
+        const uint32_t vbase = smem_u32(sm.kv[vslot][0]);
 #pragma unroll
-        for (int j = 0; j < V / 32; ++j) {
-          const int idx = lane * (V / 32) + j;
-          const int tl = warp * kTokPerWarp + b * TB + idx / G;
-          sm.s[idx % G][tl] = tl < n_valid ? vals[j] : -INFINITY;
+        for (int k = 0; k < kTile / 16; ++k) {
+          const uint64_t a = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kHalfBytes, 1024);
+          const uint64_t b =
+              umma_desc_sw128(smem_u32(sm.pt[k >> 2]) + (uint32_t)(k & 3) * 32, 16, 1024);
+          umma_bf16(tmem + 2 * kN, a, b, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
         }
-      } else {
-        if ((lane & 1) == 0) {
-          const int tl = warp * kTokPerWarp + b * TB + (lane >> 1);
-          sm.s[0][tl] = tl < n_valid ? vals[0] : -INFINITY;
-        }
+        umma_commit(&sm.o_done);
+        umma_commit(&sm.empty[vslot]);
       }
+      // Drain: every MMA has completed before TMEM is released.
+      mbar_wait(&sm.o_done, (n_tiles - 1) & 1, prm.status, 19);
     }
-    named_barrier_sync(1, kConsumerWarps * 32);
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32)
+    const int r = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
 
-    // ---- online softmax statistics: warp w owns heads w, w+4, ... ----
-    for (int g = warp; g < G; g += kConsumerWarps) {
-      const float s0 = sm.s[g][lane], s1 = sm.s[g][lane + 32];
-      float mx = fmaxf(s0, s1);
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float m_old = sm.m_run[g];
-      const float m_new = fmaxf(m_old, mx);
-      float p0 = 0.0f, p1 = 0.0f, alpha = 1.0f;
-      if (m_new != -INFINITY) {
-        p0 = fast_exp2(s0 - m_new);
-        p1 = fast_exp2(s1 - m_new);
-        alpha = fast_exp2(m_old - m_new);
-      }
-      sm.p[lane][g] = p0;
-      sm.p[lane + 32][g] = p1;
-      float sum = p0 + p1;
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      __syncwarp();
-      if (lane == 0) {
-        sm.l_run[g] = sm.l_run[g] * alpha + sum;
-        sm.m_run[g] = m_new;
-        sm.alpha[g] = alpha;
-      }
-    }
-    named_barrier_sync(1, kConsumerWarps * 32);
-
-    // ---- P.V for this warp's 16 tokens ----
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float a = sm.alpha[g];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[g][j] *= a;
-    }
-    const int tl0 = warp * kTokPerWarp;
-    const int n_mine = min(kTokPerWarp, n_valid - tl0);
-#pragma unroll 4
-    for (int tt = 0; tt < n_mine; ++tt) {
-      const int tl = tl0 + tt;
-      const uint2 vr = *reinterpret_cast<const uint2*>(vt + tl * kD + 4 * lane);
-      const float v0 = bf16lo_to_f32(vr.x), v1 = bf16hi_to_f32(vr.x);
-      const float v2 = bf16lo_to_f32(vr.y), v3 = bf16hi_to_f32(vr.y);
-      float pg[G];
-      load_p<G>(&sm.p[tl][0], pg);
+    // Q^T operand: row g = bf16(q_g * scale*log2e), row G+g = the bf16
+    // remainder, rows >= 2G zero; thread r fills column (dim) r.  P^T rows
+    // >= 2G are zeroed once and never written again.
+    {
+      const float* qp = prm.q + ((long long)seq * prm.Hq + (long long)kvh * G) * kD + r;
+      uint8_t* qt = reinterpret_cast<uint8_t*>(sm.qt[r >> 6]);
+      uint8_t* pt = reinterpret_cast<uint8_t*>(sm.pt[r >> 6]);
+      const int c = r & 63;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        acc[g][0] = fmaf(pg[g], v0, acc[g][0]);
-        acc[g][1] = fmaf(pg[g], v1, acc[g][1]);
-        acc[g][2] = fmaf(pg[g], v2, acc[g][2]);
-        acc[g][3] = fmaf(pg[g], v3, acc[g][3]);
+        const float x = qp[g * kD] * prm.scale_log2;
+        const uint16_t hi = bf16_rn(x);
+        const uint16_t lo = bf16_rn(x - __uint_as_float((uint32_t)hi << 16));
+        *reinterpret_cast<uint16_t*>(qt + sw128_offset(g, c)) = hi;
+        *reinterpret_cast<uint16_t*>(qt + sw128_offset(G + g, c)) = lo;
+      }
+#pragma unroll
+      for (int n = 2 * G; n < kN; ++n) {
+        *reinterpret_cast<uint16_t*>(qt + sw128_offset(n, c)) = 0;
+        *reinterpret_cast<uint16_t*>(pt + sw128_offset(n, c)) = 0;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.q_ready);
+    }
+
+    float m_used[G], l_part[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      m_used[g] = -INFINITY;
+      l_part[g] = 0.0f;
+    }
+
+    for (int j = 0; j < n_tiles; ++j) {
+      mbar_wait(&sm.s_full[j & 1], (j >> 1) & 1, prm.status, abort_flag, 20);
+      tc_fence_after();
+      uint32_t sv[16];
+      tmem_ld16(tmem + lane_off + (j & 1) * kN, sv);
+      tmem_wait_ld();
+      const int tile0 = t_begin + j * kTile;
+      const bool valid = tile0 + r < t_end;
+      float sg[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        sg[g] = valid ? __uint_as_float(sv[g]) + __uint_as_float(sv[G + g]) : -INFINITY;
+
+      // per-head maximum over the tile's 128 tokens
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float v = sg[g];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) sm.red[j & 1][quad][g] = v;
+      }
+      named_barrier_sync(1, 128);
+      float alpha[G];
+      bool rescale = false;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float tmax = fmaxf(fmaxf(sm.red[j & 1][0][g], sm.red[j & 1][1][g]),
+                                 fmaxf(sm.red[j & 1][2][g], sm.red[j & 1][3][g]));
+        const float m_new = fmaxf(m_used[g], tmax);
+        alpha[g] = 1.0f;
+        if (m_new > m_used[g] + kRescaleThreshold) {
+          alpha[g] = fast_exp2(m_used[g] - m_new);
+          rescale = rescale || j > 0;
+          m_used[g] = m_new;
+        }
+      }
+      float p[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        p[g] = valid ? fast_exp2(sg[g] - m_used[g]) : 0.0f;
+        l_part[g] = fmaf(l_part[g], alpha[g], p[g]);
+      }
+
+      if (j > 0) {
+        // PV(j-1) has finished: O is stable and the P^T buffer is free.
+        mbar_wait(&sm.o_done, (j - 1) & 1, prm.status, abort_flag, 21);
+        tc_fence_after();
+      }
+      if (rescale) {  // the same for every thread (shared tile maxima)
+        uint32_t ov[16];
+        tmem_ld16(tmem + lane_off + 2 * kN, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int n = 0; n < 2 * G; ++n)
+          ov[n] = __float_as_uint(__uint_as_float(ov[n]) * alpha[n < G ? n : n - G]);
+        tmem_st16(tmem + lane_off + 2 * kN, ov);
+        tmem_wait_st();
+      }
+      if (tile0 + kTile > t_end) {
+        // Keys at or past the context end hold whatever the cache slot
+        // contains; zero their V rows so that P = 0 never meets a NaN.
+        const int vidx = 2 * j + 1;
+        mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 22);
+        if (!valid) {
+          const uint4 z = make_uint4(0, 0, 0, 0);
+          uint4* v0 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.kv[ring_slot(vidx)][0]) + r * 128);
+          uint4* v1 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.kv[ring_slot(vidx)][1]) + r * 128);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            v0[c] = z;
+            v1[c] = z;
+          }
+        }
+      }
+      // P^T column r (token): row g = bf16(p_g), row G+g = remainder.
+      uint8_t* pt = reinterpret_cast<uint8_t*>(sm.pt[r >> 6]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const uint16_t hi = bf16_rn(p[g]);
+        const uint16_t lo = bf16_rn(p[g] - __uint_as_float((uint32_t)hi << 16));
+        *reinterpret_cast<uint16_t*>(pt + sw128_offset(g, r & 63)) = hi;
+        *reinterpret_cast<uint16_t*>(pt + sw128_offset(G + g, r & 63)) = lo;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full);
+    }
+
+    // ---- epilogue: thread r = head dim r ----
+    float l_tot[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float v = l_part[g];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) sm.red_sum[quad][g] = v;
+    }
+    named_barrier_sync(1, 128);
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      l_tot[g] = (sm.red_sum[0][g] + sm.red_sum[1][g]) + (sm.red_sum[2][g] + sm.red_sum[3][g]);
+    uint32_t ov[16];
+    if (n_tiles > 0) {
+      mbar_wait(&sm.o_done, (n_tiles - 1) & 1, prm.status, abort_flag, 23);
+      tc_fence_after();
+      tmem_ld16(tmem + lane_off + 2 * kN, ov);
+      tmem_wait_ld();
+    } else {
+#pragma unroll
+      for (int n = 0; n < 16; ++n) ov[n] = 0u;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float o = __uint_as_float(ov[g]) + __uint_as_float(ov[G + g]);
+      const int h = kvh * G + g;
+      if (n_splits == 1) {
+        prm.out[((long long)seq * prm.Hq + h) * kD + r] = l_tot[g] > 0.0f ? o / l_tot[g] : 0.0f;
+      } else {
+        const long long pidx =
+            ((long long)(seq * prm.Hkv + kvh) * prm.max_splits + split) * G + g;
+        prm.ws_o[pidx * kD + r] = o;
+        if (r == 0) {
+          prm.ws_ml[pidx * 2 + 0] = m_used[g];
+          prm.ws_ml[pidx * 2 + 1] = l_tot[g];
+        }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[stage]);
   }
 
-  // ---- cross-warp reduction of the 4 partial accumulators ----
-  named_barrier_sync(1, kConsumerWarps * 32);  // every stage consumed
-  float* red = reinterpret_cast<float*>(&sm.k[0][0]);  // [4][G][128] fp32 <= 16 KiB
-  static_assert(kConsumerWarps * G * kD * 4 <= kTileBytes * kStages * 2, "reduction buffer");
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-    *reinterpret_cast<float4*>(red + (warp * G + g) * kD + 4 * lane) =
-        make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-  named_barrier_sync(1, kConsumerWarps * 32);
-  const int d = threadIdx.x;  // 0..127
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float o = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) o += red[(w * G + g) * kD + d];
-    const int h = kvh * G + g;
-    if (n_splits == 1) {
-      const float l = sm.l_run[g];
-      prm.out[((long long)seq * prm.Hq + h) * kD + d] = l > 0.0f ? o / l : 0.0f;
-    } else {
-      const long long pidx = ((long long)(seq * prm.Hkv + kvh) * prm.max_splits + split) * G + g;
-      prm.ws_o[pidx * kD + d] = o;
-      if (d == 0) {
-        prm.ws_ml[pidx * 2 + 0] = sm.m_run[g];
-        prm.ws_ml[pidx * 2 + 1] = sm.l_run[g];
-      }
-    }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -404,9 +467,9 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
   if (n_seqs == 0) return NVATTN_OK;
   const CUtensorMap* tk = nullptr;
   const CUtensorMap* tv = nullptr;
-  nvattn_status st = get_cache_tensor_map(h, k_cache, kD, kTile, 0, &tk);
+  nvattn_status st = get_cache_tensor_map(h, k_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
   if (st != NVATTN_OK) return st;
-  st = get_cache_tensor_map(h, v_cache, kD, kTile, 0, &tv);
+  st = get_cache_tensor_map(h, v_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tv);
   if (st != NVATTN_OK) return st;
 
   DecodeParams prm;
@@ -514,11 +577,13 @@ extern "C" NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
   CUtensorMap tk, tv;
   nvattn_status st = encode_tensor_map_3d(&tk, k_cache_dev, kD, (uint64_t)c.n_kv_heads,
                                           (uint64_t)c.n_layer * (uint64_t)n_slots, kD * 2,
-                                          (uint64_t)c.n_kv_heads * kD * 2, kD, 1, kTile, 0);
+                                          (uint64_t)c.n_kv_heads * kD * 2, 64, 1, kTile,
+                                          CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NVATTN_OK) return st;
   st = encode_tensor_map_3d(&tv, v_cache_dev, kD, (uint64_t)c.n_kv_heads,
                             (uint64_t)c.n_layer * (uint64_t)n_slots, kD * 2,
-                            (uint64_t)c.n_kv_heads * kD * 2, kD, 1, kTile, 0);
+                            (uint64_t)c.n_kv_heads * kD * 2, 64, 1, kTile,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NVATTN_OK) return st;
 
   float* scratch = static_cast<float*>(g_noalloc_scratch_addr[dev]);
