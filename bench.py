@@ -42,9 +42,9 @@ SEED = 0
 
 # DRAM traffic per decode launch of this workload (dram__bytes_read.sum +
 # dram__bytes_write.sum): the 32-sequence ncu capture summarised in
-# profiles/paged_decode_qwen3_8b_256seq.md read 1.0062x its algorithmic
-# bytes; scaled to the full launch's 10.987 GB of algorithmic bytes.
-NCU_TRAFFIC_BYTES_N1 = 11.055e9
+# profiles/paged_decode_qwen3_8b_256seq.md moved 1.3767 GB for 1.3632 GB of
+# algorithmic bytes (x1.0099); scaled to the full launch's 10.987 GB.
+NCU_TRAFFIC_BYTES_N1 = 11.096e9
 
 
 def log(*a):
@@ -202,10 +202,11 @@ def run_prefills(args, world, rank, device):
             import torch.distributed as dist
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pre_ms, step_ms = t.tolist()
-        achieved = fields["flops_per_step"] / (pre_ms / 1e3) / 1e12
+        job_tflops = fields["flops_per_step"] / (pre_ms / 1e3) / 1e12
+        achieved = job_tflops / world  # per GPU, against one GPU's peak
         fields.update({
             "tokens_per_s": fields["new_tokens"] / (step_ms / 1e3), "ms_per_step": step_ms,
-            "tflops": achieved,
+            "tflops": job_tflops,
             "roofline": {"bound": "tensor", "kernel": "paged_prefill (tcgen05)",
                          "achieved": achieved, "peak": tflops_peak, "unit": "TFLOP/s",
                          "frac": achieved / tflops_peak, "peak_source": peak_kind,
