@@ -126,7 +126,7 @@ def bench_prefill(kind, args, world, rank, device):
     max_ctx = int(cl.max())
     cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
                               max_seqs=len(lens), max_context=max_ctx, max_position=max_ctx,
-                              device=device.index, prefill_split_p=args.prefill_split)
+                              device=device.index)
     h = nvattn.Handle(cfg)
     gen = torch.Generator(device=device)
     gen.manual_seed(2000 + rank)
@@ -152,13 +152,14 @@ def bench_prefill(kind, args, world, rank, device):
     evs = []
 
     def step():
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        z, a, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        z.record(stream)
         h.kv_store(0, q, k, v, qw16, kw16, d["pos"], d["slot"], qb, kc16, vc16, stream=stream)
         a.record(stream)
         h.prefill(0, qb, d["cu"], d["qs"], d["cl"], d["bt"], max_q, kc16, vc16, out,
                   stream=stream)
         b.record(stream)
-        evs.append((a, b))
+        evs.append((z, a, b))
 
     steps = max(2, args.prefill_steps)
     for _ in range(max(3, min(args.warmup, 5))):
@@ -177,15 +178,114 @@ def bench_prefill(kind, args, world, rank, device):
     torch.cuda.synchronize(device)
     h.check_device(f"prefill {name}")
     step_ms = t0.elapsed_time(t1) / steps
-    pre_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    pre_ms = sum(a.elapsed_time(b) for _, a, b in evs) / len(evs)
+    store_ms = sum(z.elapsed_time(a) for z, a, _ in evs) / len(evs)
     # algorithmic causal FLOPs (whole job, all heads): 4*d*Hq per visible (q, k) pair
     pairs = sum(int(((np.arange(qs[s], cl[s]) + 1)).sum()) for s in range(len(lens)))
     flops = 4.0 * D * Hq * pairs
     h.close()
     fields = {"workload": name, "q_heads": Hq, "kv_heads": Hkv, "n_seqs": len(lens),
               "new_tokens": T, "sum_context": int(cl.sum()), "flops_per_step": flops,
-              "steps": steps, "p_split": args.prefill_split}
+              "steps": steps, "pv_precision": "f16 P x f16 V (V converted in smem)",
+              "kv_store": kv_store_roofline(T, hq, hkv, store_ms, q_out_bytes=2)}
     return fields, pre_ms, step_ms
+
+
+def kv_store_roofline(T, hq, hkv, ms, q_out_bytes):
+    """Algorithmic bytes of the fused q/k norm + RoPE + K/V store on one GPU:
+    read q, k, v (f32) and one RoPE row per token, write q (f32 or bf16) and
+    the bf16 K/V rows; positions and slots 8 B per token."""
+    hbm_peak, _, kind = peaks()
+    per_tok = (hq + 2 * hkv) * D * 4 + D * 4 + hq * D * q_out_bytes + 2 * hkv * D * 2 + 8
+    gbs = T * per_tok / (ms / 1e3) / 1e9
+    return {"bound": "hbm", "kernel": "kv_store_qk_norm_rope", "tokens": T, "ms": ms,
+            "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+            "peak_source": kind, "bytes_per_token": per_tok}
+
+
+def bench_decode_long(args, world, rank, device):
+    """Secondary decode workload: the Qwen3-32B attention shape (64 q / 8 kv
+    heads) with 16 sequences at 131104 cached tokens (the middle of the 64
+    decode steps that follow the 2048-token chunk), kv-head sharded like the
+    headline workload.  Device-resident inputs; returns a JSON-ready dict."""
+    import torch
+    import nvattn
+    Hq, Hkv, B, L = 64, 8, 16, 131104
+    hq, hkv = Hq // world, Hkv // world
+    need = (L + BS - 1) // BS
+    num_blocks = B * need + 8
+    rng = np.random.default_rng(SEED + 3)
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    bt_np = perm[:B * need].reshape(B, need)
+    lens = np.full(B, L, np.int64)
+    cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
+                              max_seqs=B, max_context=L, max_position=L, device=device.index)
+    h = nvattn.Handle(cfg)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(3000 + rank)
+    n_slots = num_blocks * BS
+    kc = torch.empty((n_slots, hkv, D), dtype=torch.bfloat16, device=device)
+    vc = torch.empty_like(kc)
+    for t in (kc, vc):
+        for i in range(0, n_slots, 1 << 16):
+            t[i:i + (1 << 16)].copy_(torch.randn((min(1 << 16, n_slots - i), hkv, D),
+                                                 generator=gen, device=device))
+    cl, pos_np, slot_np = nvattn.plan_decode(lens, bt_np)
+    bt, ctx = torch.from_numpy(bt_np).to(device), torch.from_numpy(cl).to(device)
+    pos, slots = torch.from_numpy(pos_np).to(device), torch.from_numpy(slot_np).to(device)
+    q0 = torch.randn((B, hq, D), generator=gen, device=device)
+    kn = torch.randn((B, hkv, D), generator=gen, device=device)
+    vn = torch.randn((B, hkv, D), generator=gen, device=device)
+    w16 = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16).view(
+        torch.int16)
+    q, out = torch.empty_like(q0), torch.empty((B, hq, D), device=device)
+    kc16, vc16 = kc.view(torch.int16), vc.view(torch.int16)
+    stream = torch.cuda.current_stream(device)
+    evs = []
+
+    def step():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        q.copy_(q0)
+        h.kv_store(0, q, kn, vn, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
+        a.record(stream)
+        h.decode(0, q, kc16, vc16, bt, ctx, L, out, stream=stream)
+        b.record(stream)
+        evs.append((a, b))
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(device)
+    h.check_device("decode_long warmup")
+    evs.clear()
+    steps = max(5, args.prefill_steps * 2)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[device.index])
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize(device)
+    h.check_device("decode_long")
+    h.close()
+    t = torch.tensor([t0.elapsed_time(t1) / steps,
+                      sum(a.elapsed_time(b) for a, b in evs) / len(evs)],
+                     dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, dec_ms = t.tolist()
+    hbm_peak, _, kind = peaks()
+    alg = B * L * hkv * D * 2 * 2 + B * hq * D * 4 * 2 + B * need * 4 + B * 4
+    gbs = alg / (dec_ms / 1e3) / 1e9
+    return {"workload": "decode_qwen3_32b_attn_16seq_ctx131104", "q_heads": Hq, "kv_heads": Hkv,
+            "n_seqs": B, "context": L, "steps": steps, "ms_per_step": step_ms,
+            "tokens_per_s": B / (step_ms / 1e3),
+            "roofline": {"bound": "hbm", "kernel": "paged_decode (main + split combine)",
+                         "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": gbs / hbm_peak, "peak_source": kind, "decode_ms": dec_ms,
+                         "algorithmic_bytes": alg, "frac_of_8tbs": gbs / 8000.0}}
 
 
 def run_prefills(args, world, rank, device):
@@ -374,8 +474,8 @@ def main():
     ap.add_argument("--prefill", default="prefix_hit,chunk",
                     help="comma list of prefill workloads to time (prefix_hit, chunk) or none")
     ap.add_argument("--prefill-steps", type=int, default=5)
-    ap.add_argument("--prefill-split", type=int, default=1, choices=[0, 1],
-                    help="prefill P.V precision: 1 = bf16 hi+lo split (default), 0 = one pass")
+    ap.add_argument("--no-decode-long", action="store_true",
+                    help="skip the secondary 32B-shape long-context decode workload")
     ap.add_argument("--only-prefill", action="store_true",
                     help="skip the decode workload (for profiling the prefill kernel)")
     args = ap.parse_args()
@@ -445,6 +545,7 @@ def main():
 
     def step():
         q.copy_(q0)  # the fused kernel writes q in place; keep every step identical
+        ev_z.record(stream)
         h.kv_store(0, q, k_new, v_new, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
         ev_a.record(stream)
         h.decode(0, q, kc16, vc16, bt, ctx, max_ctx, out, stream=stream)
@@ -457,6 +558,7 @@ def main():
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(device)
 
+    ev_z = torch.cuda.Event(enable_timing=True)
     ev_a = torch.cuda.Event(enable_timing=True)
     ev_b = torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local_rank)
@@ -474,15 +576,17 @@ def main():
     pairs = []
     t0.record(stream)
     for _ in range(args.steps):
+        ev_z = torch.cuda.Event(enable_timing=True)
         ev_a = torch.cuda.Event(enable_timing=True)
         ev_b = torch.cuda.Event(enable_timing=True)
         step()
-        pairs.append((ev_a, ev_b))
+        pairs.append((ev_z, ev_a, ev_b))
     t1.record(stream)
     barrier()
     clk = clocks.stop(mark)
     elapsed = t0.elapsed_time(t1) / 1e3
-    dec_ms = sum(a.elapsed_time(b) for a, b in pairs) / len(pairs)
+    dec_ms = sum(a.elapsed_time(b) for _, a, b in pairs) / len(pairs)
+    store_ms = sum(z.elapsed_time(a) for z, a, _ in pairs) / len(pairs)
     h.check_device("timed region")
 
     # ---- e2e: the same step through the C ABI with pinned host buffers ----
@@ -556,6 +660,7 @@ def main():
     del kc, vc, kc16, vc16
     torch.cuda.empty_cache()
     prefill_results = run_prefills(args, world, rank, device)
+    decode_long = None if args.no_decode_long else bench_decode_long(args, world, rank, device)
 
     if rank == 0:
         hbm_peak, _, peak_kind = peaks()
@@ -589,6 +694,8 @@ def main():
             "gpu_launches": args.steps * (2 + splits),
             "clocks": clk,
             "prefill": prefill_results,
+            "decode_long": decode_long,
+            "kv_store": kv_store_roofline(B, hq, hkv, store_ms, q_out_bytes=4),
         }
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base

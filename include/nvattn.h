@@ -96,11 +96,6 @@ typedef struct nvattn_config {
   int max_seqs;         /* largest n_seqs of any call */
   int max_context;      /* largest context length of any call */
   int device;           /* CUDA device ordinal */
-  /* Prefill P.V precision: 1 (default) splits the softmax probabilities P
-   * into bf16 P_hi + bf16 (P - P_hi) and runs the P.V product twice
-   * (~16 significant bits in P); 0 rounds P to bf16 once (faster, ~1e-3
-   * larger relative error on the output). */
-  int prefill_split_p;
 } nvattn_config;
 
 typedef struct nvattn_handle nvattn_handle;

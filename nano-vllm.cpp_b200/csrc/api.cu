@@ -140,7 +140,6 @@ void nvattn_config_init_qwen3(nvattn_config* c) {
   c->max_seqs = 512;       // Config::max_num_seqs
   c->max_context = 40960;  // Qwen3Hparams::n_ctx
   c->device = 0;
-  c->prefill_split_p = 1;
 }
 
 nvattn_status nvattn_create(const nvattn_config* cfg, nvattn_handle** out) {

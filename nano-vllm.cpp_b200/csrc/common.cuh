@@ -230,6 +230,20 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N, int a_m
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor, kind::f16: f16 A and B, f32 accumulator.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_f32(int M, int N, int a_mn, int b_mn) {
+  return (1u << 4)  // D format f32; A and B format 0 = f16
+         | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+// Two floats -> packed f16x2 (lo in bits 0-15), round to nearest even.
+__device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by a single thread.
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
@@ -345,5 +359,66 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
+
+// ---------------------------------------------------------------------------
+// packed fp32 pairs (sm_100 f32x2 arithmetic) and a polynomial exp2
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of x <= 0 on the FMA pipe (relieves the XU port that
+// ex2.approx uses).  x is clamped to -125 (2^-125 stands in for anything
+// smaller; callers use it only where no element is masked to -inf).
+// Method: x = j + f with j = rint(x) (add/subtract 1.5*2^23) and f in
+// [-1/2, 1/2]; 2^f by a degree-4 polynomial fitted to 2^f on [-1/2, 1/2]
+// by weighted least squares towards minimax relative error (max relative
+// error 2.7e-6 in fp32 evaluation); 2^j added into the exponent field
+// (the low bits of the rounding sum, shifted left by 23, equal j << 23).
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  unpack2(x2, x0, x1);
+  const uint64_t xc = pack2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t magic = pack2(kMagic, kMagic);
+  const uint64_t t = fadd2(xc, magic);
+  const uint64_t f = fsub2(xc, fsub2(t, magic));
+  uint64_t p = ffma2(pack2(0.00957008171826601f, 0.00957008171826601f), f,
+                     pack2(0.05591785907745361f, 0.05591785907745361f));
+  p = ffma2(p, f, pack2(0.2402474582195282f, 0.2402474582195282f));
+  p = ffma2(p, f, pack2(0.6931217908859253f, 0.6931217908859253f));
+  p = ffma2(p, f, pack2(0.9999992847442627f, 0.9999992847442627f));
+  float t0, t1, p0, p1;
+  unpack2(t, t0, t1);
+  unpack2(p, p0, p1);
+  const float r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  const float r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+  return pack2(r0, r1);
+}
 
 }  // namespace nvattn

@@ -5,14 +5,14 @@
 // StorePrefillKV / AppendDecodeKV + WriteKVToCache
 // (src/engine/model_runner.cpp:248-296, 380-415; src/models/qwen3.cpp:411-422).
 //
-// One half-warp owns one 128-element head row (8 elements per lane, two
-// 16-byte loads and one 16-byte bf16 store per lane).  Rows are ordered per
-// token as [Hq q rows | Hkv k rows | Hkv v rows].
+// Eight lanes own one 128-element head row (16 elements per lane: four
+// 16-byte loads, two 16-byte bf16 stores); a warp handles four rows.  Rows are
+// ordered per token as [Hq q rows | Hkv k rows | Hkv v rows].
 //
 // Bit-exactness with the reference's ggml CPU path:
 //  * RMSNorm: ggml sums float squares in double in index order, rounds
 //    mean = sum/128 to float, scale = 1/sqrtf(mean+eps), y = (x*scale)*w.
-//    Here the squares are summed in double by a 16-lane tree.  The tree and
+//    Here the squares are summed in double by an 8-lane tree.  The tree and
 //    the sequential sum both lie within 2^-45*sum of the exact sum, so the
 //    float mean can only differ when sum/128 lies within that distance of a
 //    float rounding boundary.  That case is detected (both ends of the
@@ -28,8 +28,10 @@ namespace nvattn {
 namespace {
 
 constexpr int kD = 128;
+constexpr int kLanesPerRow = 8;
+constexpr int kElems = kD / kLanesPerRow;  // 16 per lane
 constexpr int kThreads = 256;
-constexpr int kRowsPerBlock = kThreads / 16;
+constexpr int kRowsPerBlock = kThreads / kLanesPerRow;
 
 struct KvStoreParams {
   int n_tokens, Hq, Hkv, layer, max_position;
@@ -49,34 +51,30 @@ struct KvStoreParams {
   DeviceStatus* status;
 };
 
-__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
-  // Plain loads: q_out may alias q (each row is read before it is written,
-  // by the same half-warp).
-  const float4 a = reinterpret_cast<const float4*>(p)[0];
-  const float4 b = reinterpret_cast<const float4*>(p)[1];
-  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-}
-
-__device__ __forceinline__ uint4 pack8_bf16(const float (&y)[8]) {
-  uint4 r;
-  r.x = pack_bf16x2(y[0], y[1]);
-  r.y = pack_bf16x2(y[2], y[3]);
-  r.z = pack_bf16x2(y[4], y[5]);
-  r.w = pack_bf16x2(y[6], y[7]);
-  return r;
+__device__ __forceinline__ void store16_bf16(uint16_t* dst, const float (&y)[kElems]) {
+  uint4 a, b;
+  a.x = pack_bf16x2(y[0], y[1]);
+  a.y = pack_bf16x2(y[2], y[3]);
+  a.z = pack_bf16x2(y[4], y[5]);
+  a.w = pack_bf16x2(y[6], y[7]);
+  b.x = pack_bf16x2(y[8], y[9]);
+  b.y = pack_bf16x2(y[10], y[11]);
+  b.z = pack_bf16x2(y[12], y[13]);
+  b.w = pack_bf16x2(y[14], y[15]);
+  reinterpret_cast<uint4*>(dst)[0] = a;
+  reinterpret_cast<uint4*>(dst)[1] = b;
 }
 
 template <bool kQOutBf16>
 __global__ void __launch_bounds__(kThreads) kv_store_qk_norm_rope_kernel(KvStoreParams p) {
   const int lane = threadIdx.x & 31;
-  const int hl = lane & 15;  // lane within the half-warp
+  const int l8 = lane & 7;  // lane within the row's 8-lane group
   const int rows_per_token = p.Hq + 2 * p.Hkv;
   const long long total_rows = (long long)p.n_tokens * rows_per_token;
-  const long long row_g = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 4);
+  const long long row_g = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 3);
   const bool valid = row_g < total_rows;
-  // Out-of-range half-warps redo the last row (so every lane joins the
-  // shuffles) and store nothing.
+  // Groups past the last row redo it (so every lane joins the shuffles) and
+  // store nothing.
   const long long row = valid ? row_g : total_rows - 1;
   const int t = (int)(row / rows_per_token);
   const int rr = (int)(row % rows_per_token);
@@ -93,57 +91,68 @@ __global__ void __launch_bounds__(kThreads) kv_store_qk_norm_rope_kernel(KvStore
     src = p.v + ((long long)t * p.Hkv + head) * kD;
   }
 
-  float x[8];
-  load8(src + 8 * hl, x);
+  // Plain loads: q_out may alias q (each row is read before it is written,
+  // by the same lanes).
+  float x[kElems];
+#pragma unroll
+  for (int i = 0; i < kElems / 4; ++i) {
+    const float4 a = reinterpret_cast<const float4*>(src + kElems * l8)[i];
+    x[4 * i] = a.x; x[4 * i + 1] = a.y; x[4 * i + 2] = a.z; x[4 * i + 3] = a.w;
+  }
 
   // ---- RMSNorm (q and k rows) ----
-  float sq[8];
+  float sq[kElems];
   double s = 0.0;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
+  for (int e = 0; e < kElems; ++e) {
     sq[e] = __fmul_rn(x[e], x[e]);
     s = __dadd_rn(s, (double)sq[e]);
   }
 #pragma unroll
-  for (int o = 8; o >= 1; o >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o, 16));
+  for (int o = kLanesPerRow / 2; o >= 1; o >>= 1)
+    s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o, kLanesPerRow));
 
+  // sum / 128 is exact as a multiplication by 2^-7 (no double division).
+  constexpr double kInvD = 1.0 / kD;
+  static_assert(kD == 128, "1/kD must be a power of two");
   const double delta = s * 0x1p-44;
   const bool ambiguous =
-      kind != 2 && __double2float_rn(__ddiv_rn(s - delta, (double)kD)) !=
-                       __double2float_rn(__ddiv_rn(s + delta, (double)kD));
+      kind != 2 && __double2float_rn((s - delta) * kInvD) != __double2float_rn((s + delta) * kInvD);
   if (__any_sync(0xffffffffu, ambiguous)) {
-    // ggml's order: element 0, 1, ..., 127 of this half-warp's row.
+    // ggml's order: element 0, 1, ..., 127 of this group's row.
     double seq = 0.0;
-    for (int srcl = 0; srcl < 16; ++srcl) {
+    for (int srcl = 0; srcl < kLanesPerRow; ++srcl) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float v = __shfl_sync(0xffffffffu, sq[e], srcl, 16);
+      for (int e = 0; e < kElems; ++e) {
+        const float v = __shfl_sync(0xffffffffu, sq[e], srcl, kLanesPerRow);
         seq = __dadd_rn(seq, (double)v);
       }
     }
     s = seq;
   }
-  const float mean = __double2float_rn(__ddiv_rn(s, (double)kD));
+  const float mean = __double2float_rn(s * kInvD);
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
 
-  float y[8];
+  float y[kElems];
   if (kind != 2) {
-    const uint4 wraw = __ldg(reinterpret_cast<const uint4*>((kind == 0 ? p.qw : p.kw) + 8 * hl));
-    const uint32_t w4[4] = {wraw.x, wraw.y, wraw.z, wraw.w};
+    const uint4* wp = reinterpret_cast<const uint4*>((kind == 0 ? p.qw : p.kw) + kElems * l8);
+    const uint4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+    const uint32_t w8[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float w = (e & 1) ? bf16hi_to_f32(w4[e >> 1]) : bf16lo_to_f32(w4[e >> 1]);
+    for (int e = 0; e < kElems; ++e) {
+      const float w = (e & 1) ? bf16hi_to_f32(w8[e >> 1]) : bf16lo_to_f32(w8[e >> 1]);
       y[e] = __fmul_rn(__fmul_rn(x[e], scale), w);
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = x[e];
+    for (int e = 0; e < kElems; ++e) y[e] = x[e];
   }
 
-  // ---- NEOX RoPE: element i pairs with i+64 (lane hl pairs with hl^8) ----
-  float partner[8];
+  // ---- NEOX RoPE: element i pairs with i+64 (lane l8 pairs with l8^4) ----
+  float partner[kElems];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 8, 16);
+  for (int e = 0; e < kElems; ++e)
+    partner[e] = __shfl_xor_sync(0xffffffffu, y[e], kLanesPerRow / 2, kLanesPerRow);
 
   const int pos = p.positions[t];
   bool ok = valid;
@@ -152,20 +161,21 @@ __global__ void __launch_bounds__(kThreads) kv_store_qk_norm_rope_kernel(KvStore
     ok = false;
   }
   if (kind != 2 && ok) {
-    const float4* cs = reinterpret_cast<const float4*>(p.rope + (long long)pos * (kD / 2) + 8 * (hl & 7));
-    float c[8], sn[8];
+    const float4* cs =
+        reinterpret_cast<const float4*>(p.rope + (long long)pos * (kD / 2) + kElems * (l8 & 3));
+    float c[kElems], sn[kElems];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < kElems / 2; ++j) {
       const float4 a = __ldg(cs + j);
       c[2 * j] = a.x; sn[2 * j] = a.y; c[2 * j + 1] = a.z; sn[2 * j + 1] = a.w;
     }
-    if (hl < 8) {
+    if (l8 < 4) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
+      for (int e = 0; e < kElems; ++e)
         y[e] = __fsub_rn(__fmul_rn(y[e], c[e]), __fmul_rn(partner[e], sn[e]));
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
+      for (int e = 0; e < kElems; ++e)
         y[e] = __fadd_rn(__fmul_rn(partner[e], sn[e]), __fmul_rn(y[e], c[e]));
     }
   }
@@ -173,13 +183,14 @@ __global__ void __launch_bounds__(kThreads) kv_store_qk_norm_rope_kernel(KvStore
 
   // ---- stores ----
   if (kind == 0) {
-    const long long off = ((long long)t * p.Hq + head) * kD + 8 * hl;
+    const long long off = ((long long)t * p.Hq + head) * kD + kElems * l8;
     if (kQOutBf16) {
-      *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.q_out) + off) = pack8_bf16(y);
+      store16_bf16(static_cast<uint16_t*>(p.q_out) + off, y);
     } else {
       float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.q_out) + off);
-      o[0] = make_float4(y[0], y[1], y[2], y[3]);
-      o[1] = make_float4(y[4], y[5], y[6], y[7]);
+#pragma unroll
+      for (int i = 0; i < kElems / 4; ++i)
+        o[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
     }
     return;
   }
@@ -190,9 +201,8 @@ __global__ void __launch_bounds__(kThreads) kv_store_qk_norm_rope_kernel(KvStore
     return;
   }
   uint16_t* cache = kind == 1 ? p.k_cache : p.v_cache;
-  const long long off =
-      (((long long)p.layer * p.n_slots + slot) * p.Hkv + head) * kD + 8 * hl;
-  *reinterpret_cast<uint4*>(cache + off) = pack8_bf16(y);
+  store16_bf16(cache + (((long long)p.layer * p.n_slots + slot) * p.Hkv + head) * kD + kElems * l8,
+               y);
 }
 
 }  // namespace

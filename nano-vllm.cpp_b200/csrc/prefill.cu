@@ -9,6 +9,12 @@
 // position P attends keys [0, P] of its sequence through the block table,
 // which covers prefix-cache hits and chunked prefill alike.
 //
+// Precision: S = Q K^T multiplies bf16 Q with the bf16 cache K.  For P.V the
+// softmax probabilities are rounded to f16 (11 significant bits, vs 8 for
+// bf16) and each V tile is converted bf16 -> f16 in shared memory, exactly
+// the F16 V the reference hands to ggml_flash_attn_ext (qwen3.cpp:388-393,
+// including its overflow above 65504).  Accumulation is f32.
+//
 // One CTA owns two 128-row query tiles that read the same keys: the two GQA
 // heads of a pair (same rows, same kv head), or, when a kv head serves one q
 // head, two consecutive row tiles.  Keys come in 128-key tiles.
@@ -21,17 +27,20 @@
 //                  PV0(j), S0(j+1), PV1(j), S1(j+1), ...
 //                S_t = Q_t K^T (M=128, N=128, K=128; A and B K-major, smem)
 //                O_t += P_t V  (A = P from TMEM, B = V MN-major from smem)
+//   warps 2-3    V converters: bf16 -> f16 in place, rows past the context
+//                zeroed (a cache slot past a sequence's end may hold NaN bits).
 //   warps 4-7    softmax of tile 0; warps 8-11 softmax of tile 1: thread =
 //                query row = TMEM lane.  Causal mask, online softmax in the
-//                log2 domain, P written as bf16 into the TMEM columns of its
+//                log2 domain, P written as f16 into the TMEM columns of its
 //                own S (S was read to registers), lazy O rescaling (only when
 //                a row max grows by more than 2^8), epilogue O / l.
 // MMAs issued by one thread execute in order, so S(j+1) may overwrite the
 // columns of P(j) right after PV(j) is issued, and the completion of S(j+1)
 // implies PV(j) is done (its O may then be rescaled).
 // TMEM columns: tile t uses [256t, 256t+128) for S/P and [256t+128, 256t+256)
-// for O.  Split-P mode keeps bf16(P) in the first 64 columns of S and the
-// bf16 remainder P - bf16(P) in the next 64, and runs P.V twice.
+// for O.
+#include <type_traits>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -43,7 +52,8 @@ constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // keys per tile
 constexpr int kSlots = 5;
 constexpr int kThreads = 12 * 32;
-constexpr int kHalfBytes = 128 * 64 * 2;  // one 128-row x 64-column bf16 box: 16 KiB
+constexpr int kConvThreads = 64;          // warps 2-3
+constexpr int kHalfBytes = 128 * 64 * 2;  // one 128-row x 64-column 16-bit box: 16 KiB
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -61,11 +71,12 @@ struct PrefillParams {
 };
 
 struct __align__(1024) PrefillSmem {
-  uint16_t q[2][2][kBM * 64];       // [tile][d half][row][64]
+  uint16_t q[2][2][kBM * 64];        // [tile][d half][row][64]
   uint16_t kv[kSlots][2][kBN * 64];  // [slot][d half][key][64]
   uint64_t q_full;
   uint64_t full[kSlots], empty[kSlots];
   uint64_t s_full[2], p_full[2];
+  uint64_t v_ready[2], v_consumed[2];  // by key-tile parity
   uint64_t o_final;
   uint32_t tmem_base;
   int abort_flag;  // raised by the first wait that times out
@@ -120,13 +131,50 @@ __device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap
     mbar_wait(&sm.full[ring_slot(idx)], ring_parity(idx), prm.status, 40);
 }
 
+// ---------------------------------------------------------------- V converters
+// Tile j is converted only after P.V of tile j-2 has finished, so each
+// barrier of a parity pair runs at most one phase ahead of its waiter.
+__device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillParams& prm,
+                                               const Work& w, int c) {
+  volatile int* abort_flag = &sm.abort_flag;
+  const int lane = c & 31;
+  for (int j = 0; j < w.n_kv; ++j) {
+    const int b = j & 1;
+    if (j >= 2) mbar_wait(&sm.v_consumed[b], ((j >> 1) - 1) & 1, prm.status, abort_flag, 43);
+    const int vidx = 2 * j + 1;
+    const int slot = ring_slot(vidx);
+    mbar_wait(&sm.full[slot], ring_parity(vidx), prm.status, abort_flag, 44);
+    const int key0 = j * kBN;
+    // 2048 16-byte chunks: half h = f / 1024, key row = (f % 1024) / 8.
+    // Consecutive threads touch consecutive chunks (no bank conflicts).
+#pragma unroll 4
+    for (int f = c; f < 2 * 128 * 8; f += kConvThreads) {
+      const int half = f >> 10, key = (f & 1023) >> 3;
+      uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.kv[slot][half]) +
+                                          (f & 1023) * 16);
+      uint4 v = *p;
+      if (key0 + key < w.ctx) {
+        v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
+        v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
+        v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
+        v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
+      } else {
+        v = make_uint4(0, 0, 0, 0);
+      }
+      *p = v;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.v_ready[b]);
+  }
+}
+
 // ---------------------------------------------------------------- MMA issuer
-template <bool kSplitP>
 __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
                                          const PrefillParams& prm, const Work& w) {
   volatile int* abort_flag = &sm.abort_flag;
   constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kBM, kBN, 0, 0);
-  constexpr uint32_t idesc_o = umma_idesc_bf16_f32(kBM, kD, 0, 1);
+  constexpr uint32_t idesc_o = umma_idesc_f16_f32(kBM, kD, 0, 1);
   const int n_kv = w.n_kv;
   mbar_wait(&sm.q_full, 0, prm.status, abort_flag, 31);
   auto issue_s = [&](int t, int j) {
@@ -147,13 +195,6 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
       umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, b, idesc_o,
                    (j > 0 || k > 0) ? 1u : 0u);
     }
-    if constexpr (kSplitP) {
-#pragma unroll
-      for (int k = 0; k < kBN / 16; ++k) {
-        const uint64_t b = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kHalfBytes, 1024);
-        umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + 64 + k * 8, b, idesc_o, 1u);
-      }
-    }
   };
   mbar_wait(&sm.full[ring_slot(0)], ring_parity(0), prm.status, abort_flag, 32);
   tc_fence_after();
@@ -164,7 +205,7 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
   umma_commit(&sm.empty[ring_slot(0)]);
   for (int j = 0; j < n_kv; ++j) {
     const int vidx = 2 * j + 1, kidx = 2 * j + 2;
-    mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 33);
+    mbar_wait(&sm.v_ready[j & 1], (j >> 1) & 1, prm.status, abort_flag, 33);
     mbar_wait(&sm.p_full[0], j & 1, prm.status, abort_flag, 34);
     tc_fence_after();
     issue_pv(0, j);
@@ -177,6 +218,7 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
     mbar_wait(&sm.p_full[1], j & 1, prm.status, abort_flag, 36);
     tc_fence_after();
     issue_pv(1, j);
+    umma_commit(&sm.v_consumed[j & 1]);
     umma_commit(&sm.empty[ring_slot(vidx)]);
     if (j + 1 < n_kv) {
       issue_s(1, j + 1);
@@ -190,7 +232,6 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
 }
 
 // ---------------------------------------------------------------- softmax
-template <bool kSplitP>
 __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
                                              const PrefillParams& prm, const Work& w, int warp,
                                              int lane) {
@@ -208,31 +249,36 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
   const int pos_row = my_rows > 0 ? w.q_start + my_row0 + min(row, my_rows - 1) : w.p_last0;
   const int vis_last = min(pos_row, w.ctx - 1);  // last visible key
   const float sc = prm.scale_log2;
+  const uint64_t sc2 = pack2(sc, sc);
   float m_used = -INFINITY;
   float l = 0.0f;
 
   for (int j = 0; j < w.n_kv; ++j) {
     mbar_wait(&sm.s_full[t], j & 1, prm.status, abort_flag, 37);
     tc_fence_after();
-    uint32_t sr[128];
+    uint32_t sr[kBN];
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
     tmem_wait_ld();
 
     const int lim = vis_last - j * kBN;  // keys c <= lim are visible
-    if (lim < kBN - 1) {
+    // Warp-uniform: the paths below end in tcgen05.st, a warp-collective
+    // instruction that every lane of the warp must execute together.
+    const bool masked = __any_sync(0xffffffffu, lim < kBN - 1);
+    if (masked) {
 #pragma unroll
       for (int c = 0; c < kBN; ++c)
         if (c > lim) sr[c] = __float_as_uint(-INFINITY);
     }
-    float mx[8];
+    float mx[4];
 #pragma unroll
-    for (int a = 0; a < 8; ++a) mx[a] = __uint_as_float(sr[a]);
+    for (int a = 0; a < 4; ++a) mx[a] = __uint_as_float(sr[a]);
 #pragma unroll
-    for (int c = 8; c < kBN; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sr[c]));
-    const float tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                 fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
+    for (int c = 4; c < kBN; c += 2)
+      mx[(c >> 1) & 3] =
+          fmax3(mx[(c >> 1) & 3], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+    const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sc;
     const float m_new = fmaxf(m_used, tile_max);
     float alpha = 1.0f;
     bool rescale = false;
@@ -241,25 +287,44 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
       rescale = j > 0;
       m_used = m_new;
     }
-    const float neg_m = -m_used;
-    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {  // 32 keys per chunk -> 16 packed columns
-      uint32_t hi[16];
-      uint32_t lo[kSplitP ? 16 : 1];
+    // p = 2^(s*sc - m) in f32 pairs, stored as f16.  Tiles with no masked key
+    // send one pair in four to the FMA-pipe polynomial, the rest to
+    // ex2.approx (XU).
+    const uint64_t nm2 = pack2(-m_used, -m_used);
+    uint64_t sum2 = pack2(0.0f, 0.0f);
+    auto chunk = [&](int c, auto poly) {  // 32 keys -> 16 packed columns
+      constexpr bool kPoly = decltype(poly)::value;
+      uint32_t ph[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[c * 32 + 2 * i]), sc, neg_m));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[c * 32 + 2 * i + 1]), sc, neg_m));
-        sum[i & 3] += p0 + p1;
-        hi[i] = cvt_bf16x2(p0, p1);
-        if constexpr (kSplitP)
-          lo[i] = cvt_bf16x2(p0 - bf16lo_to_f32(hi[i]), p1 - bf16hi_to_f32(hi[i]));
+        const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c * 32 + 2 * i]),
+                                        __uint_as_float(sr[c * 32 + 2 * i + 1])),
+                                  sc2, nm2);
+        uint64_t p2;
+        if (kPoly && (i & 3) == 3) {
+          p2 = exp2_poly2(x2);
+        } else {
+          float x0, x1;
+          unpack2(x2, x0, x1);
+          p2 = pack2(fast_exp2(x0), fast_exp2(x1));
+        }
+        sum2 = fadd2(sum2, p2);
+        float p0, p1;
+        unpack2(p2, p0, p1);
+        ph[i] = cvt_f16x2(p0, p1);
       }
-      tmem_st16(s_col + c * 16, hi);
-      if constexpr (kSplitP) tmem_st16(s_col + 64 + c * 16, lo);
+      tmem_st16(s_col + c * 16, ph);
+    };
+    if (masked) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) chunk(c, std::false_type{});
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) chunk(c, std::true_type{});
     }
-    l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+    float s0, s1;
+    unpack2(sum2, s0, s1);
+    l = l * alpha + (s0 + s1);
 
     // O_t: the completion of S_t(j) implies PV_t(j-1) has completed.
     if (__any_sync(0xffffffffu, rescale)) {
@@ -273,26 +338,7 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
         tmem_st32(o_col + c * 32, o);
       }
     }
-    bool zeroed = false;
-    if (t == 0 && j * kBN + kBN > w.ctx) {
-      // Keys at or past the context end hold whatever the cache slot
-      // contains; zero their V rows so that P = 0 never meets a NaN.
-      const int vidx = 2 * j + 1;
-      mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 38);
-      if (j * kBN + row >= w.ctx) {
-        const uint4 z = make_uint4(0, 0, 0, 0);
-        uint8_t* v0 = reinterpret_cast<uint8_t*>(sm.kv[ring_slot(vidx)][0]) + row * 128;
-        uint8_t* v1 = reinterpret_cast<uint8_t*>(sm.kv[ring_slot(vidx)][1]) + row * 128;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          reinterpret_cast<uint4*>(v0)[c] = z;
-          reinterpret_cast<uint4*>(v1)[c] = z;
-        }
-      }
-      zeroed = true;
-    }
     tmem_wait_st();
-    if (zeroed) fence_proxy_async_smem();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.p_full[t]);
@@ -318,7 +364,6 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
   }
 }
 
-template <bool kSplitP>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
@@ -378,6 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.p_full[t], 4);
+      mbar_init(&sm.v_ready[t], kConvThreads / 32);
+      mbar_init(&sm.v_consumed[t], 1);
     }
     mbar_init(&sm.o_final, 1);
     sm.abort_flag = 0;
@@ -392,16 +439,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  // 384 threads x 168 registers at launch: warpgroup 0 (TMA, MMA, two idle
-  // warps) gives back down to 112, the two softmax warpgroups take 192 each
-  // (128*112 + 256*192 = 63488 <= 384*168 = 64512).
+  // 384 threads x 168 registers at launch: warpgroup 0 (TMA, MMA, the two
+  // converter warps) gives back down to 112, the two softmax warpgroups take
+  // 192 each (128*112 + 256*192 = 63488 <= 384*168 = 64512).
   if (warp < 4) {
     regs_dec<112>();
     if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm, w);
-    if (warp == 1 && lane == 0) mma_role<kSplitP>(sm, tmem, prm, w);
+    if (warp == 1 && lane == 0) mma_role(sm, tmem, prm, w);
+    if (warp >= 2) converter_role(sm, prm, w, threadIdx.x - 64);
   } else {
     regs_inc<192>();
-    softmax_role<kSplitP>(sm, tmem, prm, w, warp, lane);
+    softmax_role(sm, tmem, prm, w, warp, lane);
   }
 
   tc_fence_before();
@@ -410,26 +458,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-}
-
-template <bool kSplitP>
-nvattn_status launch_variant(dim3 grid, const CUtensorMap& tm_q, const CUtensorMap& tm_k,
-                             const CUtensorMap& tm_v, const PrefillParams& prm,
-                             cudaStream_t stream) {
-  const size_t smem = sizeof(PrefillSmem) + 1024;
-  // The attribute is per device; remember which devices have it.
-  static unsigned long long attr_set_mask = 0;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
-  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
-    if (cudaFuncSetAttribute(paged_prefill_kernel<kSplitP>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
-      return NVATTN_ERR_CUDA;
-    if (dev < 64) attr_set_mask |= 1ull << dev;
-  }
-  paged_prefill_kernel<kSplitP><<<grid, kThreads, smem, stream>>>(tm_q, tm_k, tm_v, prm);
-  return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 
 }  // namespace
@@ -477,8 +505,19 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
                                       : (long long)(prm.n_mtiles + 1) / 2;
   if (gx > 0x7fffffffLL || Hkv > 65535 || n_seqs > 65535) return NVATTN_ERR_UNSUPPORTED;
   dim3 grid((unsigned)gx, Hkv, n_seqs);
-  if (h->cfg.prefill_split_p) return launch_variant<true>(grid, tm_q, *tk, *tv, prm, stream);
-  return launch_variant<false>(grid, tm_q, *tk, *tv, prm, stream);
+  const size_t smem = sizeof(PrefillSmem) + 1024;
+  // The attribute is per device; remember which devices have it.
+  static unsigned long long attr_set_mask = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
+  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
+    if (cudaFuncSetAttribute(paged_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return NVATTN_ERR_CUDA;
+    if (dev < 64) attr_set_mask |= 1ull << dev;
+  }
+  paged_prefill_kernel<<<grid, kThreads, smem, stream>>>(tm_q, *tk, *tv, prm);
+  return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 
 }  // namespace nvattn

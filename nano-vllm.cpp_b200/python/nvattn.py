@@ -61,7 +61,6 @@ class Config(ctypes.Structure):
         ("max_seqs", ctypes.c_int),
         ("max_context", ctypes.c_int),
         ("device", ctypes.c_int),
-        ("prefill_split_p", ctypes.c_int),
     ]
 
 

@@ -1,8 +1,9 @@
 """GPU parity of nvattn_paged_prefill (tcgen05 kernel) against the oracle.
 
 The kernel multiplies bf16 Q and bf16 K on the tensor cores, rounds the
-softmax probabilities P to bf16 for the P.V product, and accumulates in
-fp32.  Tolerances (north-star: BF16 inputs, FP32 accumulate):
+softmax probabilities P to f16 and converts V to f16 (as the reference's
+ggml_cast does) for the P.V product, and accumulates in fp32.  Tolerances
+(north-star: BF16 inputs, FP32 accumulate):
   * against fp64 math on the same bf16 inputs: max-abs-err <= 2e-2 and
     mean-rel-err <= 1e-3 (sum|a-b| / sum|b|);
   * against the reference's dtype chain (oracle GGML mode): max-abs-err <= 2e-2
@@ -162,16 +163,15 @@ def test_long_chunk_over_long_prefix(cuda):
 
 
 @pytest.mark.parametrize("Hq,Hkv", [(16, 8), (64, 8)])
-def test_single_pass_bf16_p_mode(cuda, Hq, Hkv):
-    """prefill_split_p = 0 rounds P to bf16 once: the output carries the
-    bf16 rounding noise of P (a random walk of +-2^-9 relative errors), so the
-    mean relative error bound for this mode is 2.5e-3 instead of 1e-3."""
+def test_pv_precision_headroom(cuda, Hq, Hkv):
+    """P is rounded to f16 (11 significant bits) for the P.V product, so the
+    output's rounding noise stays well inside the 1e-3 bound (a bf16 P, with
+    8 bits, would sit at ~1.4e-3 on these inputs)."""
     c = cases.prefill_case(78 + Hq, Hq, Hkv, [1000, 700, 300], [0, 512, 44])
-    h = handle(Hq, Hkv, c.cache.num_blocks, max_seqs=3, prefill_split_p=0)
-    h, got = run_prefill(c, h=h)
+    h, got = run_prefill(c)
     h.check_device()
     mx, mr = O.err_stats(got, oracle_truth(c))
-    assert mx <= MAX_ABS and mr <= 2.5e-3, (mx, mr)
+    assert mx <= MAX_ABS and mr <= 6e-4, (mx, mr)
 
 
 def test_bad_block_id_is_reported(cuda):
