@@ -5,9 +5,14 @@
 // StorePrefillKV / AppendDecodeKV + WriteKVToCache
 // (src/engine/model_runner.cpp:248-296, 380-415; src/models/qwen3.cpp:411-422).
 //
-// Eight lanes own one 128-element head row (16 elements per lane: four
-// 16-byte loads, two 16-byte bf16 stores); a warp handles four rows.  Rows are
-// ordered per token as [Hq q rows | Hkv k rows | Hkv v rows].
+// Eight lanes own a 128-element head row.  Lane l holds elements
+// [8l, 8l+8) and their NEOX partners [64+8l, 64+8l+8), so the rotation needs
+// no shuffle and each lane needs only 8 (cos, sin) pairs.  Each half is two
+// 16-byte loads and one 16-byte bf16 store.  An 8-lane group walks
+// `rows_per_group` consecutive rows of the flattened [token][Hq q | Hkv k |
+// Hkv v] row list, reloads the norm weights only when the row kind changes
+// and the (cos, sin) pairs only when the token changes, and prefetches
+// the next row's input while it works on the current one.
 //
 // Bit-exactness with the reference's ggml CPU path:
 //  * RMSNorm: ggml sums float squares in double in index order, rounds
@@ -28,13 +33,16 @@ namespace nvattn {
 namespace {
 
 constexpr int kD = 128;
+constexpr int kHalf = kD / 2;
 constexpr int kLanesPerRow = 8;
-constexpr int kElems = kD / kLanesPerRow;  // 16 per lane
+constexpr int kPer = kHalf / kLanesPerRow;  // 8 elements per lane per half
 constexpr int kThreads = 256;
-constexpr int kRowsPerBlock = kThreads / kLanesPerRow;
+constexpr int kGroupsPerBlock = kThreads / kLanesPerRow;
+constexpr int kMaxRowsPerGroup = 8;
 
 struct KvStoreParams {
-  int n_tokens, Hq, Hkv, layer, max_position;
+  int n_tokens, Hq, Hkv, layer, max_position, rows_per_group;
+  int total_rows;
   long long n_slots;
   float eps;
   const float* q;
@@ -51,158 +59,175 @@ struct KvStoreParams {
   DeviceStatus* status;
 };
 
-__device__ __forceinline__ void store16_bf16(uint16_t* dst, const float (&y)[kElems]) {
-  uint4 a, b;
+__device__ __forceinline__ uint4 pack8_bf16(const float* y) {
+  uint4 a;
   a.x = pack_bf16x2(y[0], y[1]);
   a.y = pack_bf16x2(y[2], y[3]);
   a.z = pack_bf16x2(y[4], y[5]);
   a.w = pack_bf16x2(y[6], y[7]);
-  b.x = pack_bf16x2(y[8], y[9]);
-  b.y = pack_bf16x2(y[10], y[11]);
-  b.z = pack_bf16x2(y[12], y[13]);
-  b.w = pack_bf16x2(y[14], y[15]);
-  reinterpret_cast<uint4*>(dst)[0] = a;
-  reinterpret_cast<uint4*>(dst)[1] = b;
+  return a;
+}
+
+// Input row of flattened row (t, rr): q, k or v head row.
+__device__ __forceinline__ const float* row_src(const KvStoreParams& p, int t, int rr) {
+  if (rr < p.Hq) return p.q + ((long long)t * p.Hq + rr) * kD;
+  if (rr < p.Hq + p.Hkv) return p.k + ((long long)t * p.Hkv + (rr - p.Hq)) * kD;
+  return p.v + ((long long)t * p.Hkv + (rr - p.Hq - p.Hkv)) * kD;
+}
+
+// Streaming loads (evict-first): every input byte is read once.  Plain
+// coherent loads, because q_out may alias q (a row is read before the same
+// lanes write it).
+__device__ __forceinline__ void load_row(const float* src, int l8, float (&x)[2 * kPer]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float4* s4 = reinterpret_cast<const float4*>(src + h * kHalf + kPer * l8);
+    const float4 a = __ldcs(s4), b = __ldcs(s4 + 1);
+    x[h * kPer + 0] = a.x; x[h * kPer + 1] = a.y; x[h * kPer + 2] = a.z; x[h * kPer + 3] = a.w;
+    x[h * kPer + 4] = b.x; x[h * kPer + 5] = b.y; x[h * kPer + 6] = b.z; x[h * kPer + 7] = b.w;
+  }
 }
 
 template <bool kQOutBf16>
-__global__ void __launch_bounds__(kThreads) kv_store_qk_norm_rope_kernel(KvStoreParams p) {
-  const int lane = threadIdx.x & 31;
-  const int l8 = lane & 7;  // lane within the row's 8-lane group
+__global__ void __launch_bounds__(kThreads, 3) kv_store_qk_norm_rope_kernel(KvStoreParams p) {
+  const int l8 = threadIdx.x & 7;  // lane within the row's 8-lane group
   const int rows_per_token = p.Hq + 2 * p.Hkv;
-  const long long total_rows = (long long)p.n_tokens * rows_per_token;
-  const long long row_g = (long long)blockIdx.x * kRowsPerBlock + (threadIdx.x >> 3);
-  const bool valid = row_g < total_rows;
+  const int group = blockIdx.x * kGroupsPerBlock + (threadIdx.x >> 3);
+  const int row0 = group * p.rows_per_group;
+
   // Groups past the last row redo it (so every lane joins the shuffles) and
   // store nothing.
-  const long long row = valid ? row_g : total_rows - 1;
-  const int t = (int)(row / rows_per_token);
-  const int rr = (int)(row % rows_per_token);
-  int kind, head;
-  const float* src;
-  if (rr < p.Hq) {
-    kind = 0; head = rr;
-    src = p.q + ((long long)t * p.Hq + head) * kD;
-  } else if (rr < p.Hq + p.Hkv) {
-    kind = 1; head = rr - p.Hq;
-    src = p.k + ((long long)t * p.Hkv + head) * kD;
-  } else {
-    kind = 2; head = rr - p.Hq - p.Hkv;
-    src = p.v + ((long long)t * p.Hkv + head) * kD;
-  }
+  int row = min(row0, p.total_rows - 1);
+  int t = row / rows_per_token;
+  int rr = row - t * rows_per_token;
+  float xn[2 * kPer];
+  load_row(row_src(p, t, rr), l8, xn);
 
-  // Plain loads: q_out may alias q (each row is read before it is written,
-  // by the same lanes).
-  float x[kElems];
-#pragma unroll
-  for (int i = 0; i < kElems / 4; ++i) {
-    const float4 a = reinterpret_cast<const float4*>(src + kElems * l8)[i];
-    x[4 * i] = a.x; x[4 * i + 1] = a.y; x[4 * i + 2] = a.z; x[4 * i + 3] = a.w;
-  }
+  int cur_t = -1, pos = 0, cur_kind = -1;
+  bool pos_ok = false;
+  float c[kPer], sn[kPer];
+  uint4 w[2];  // norm weights of this lane's 16 elements (packed bf16 pairs)
 
-  // ---- RMSNorm (q and k rows) ----
-  float sq[kElems];
-  double s = 0.0;
+  for (int it = 0; it < p.rows_per_group; ++it) {
+    const bool valid = row0 + it < p.total_rows;
+    const int t_row = t, rr_row = rr;
+    float x[2 * kPer];
 #pragma unroll
-  for (int e = 0; e < kElems; ++e) {
-    sq[e] = __fmul_rn(x[e], x[e]);
-    s = __dadd_rn(s, (double)sq[e]);
-  }
-#pragma unroll
-  for (int o = kLanesPerRow / 2; o >= 1; o >>= 1)
-    s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o, kLanesPerRow));
+    for (int e = 0; e < 2 * kPer; ++e) x[e] = xn[e];
+    // advance to (and prefetch) the next row
+    if (it + 1 < p.rows_per_group && row0 + it + 1 < p.total_rows) {
+      if (++rr == rows_per_token) { rr = 0; ++t; }
+      load_row(row_src(p, t, rr), l8, xn);
+    }
+    const int kind = rr_row < p.Hq ? 0 : (rr_row < p.Hq + p.Hkv ? 1 : 2);
 
-  // sum / 128 is exact as a multiplication by 2^-7 (no double division).
-  constexpr double kInvD = 1.0 / kD;
-  static_assert(kD == 128, "1/kD must be a power of two");
-  const double delta = s * 0x1p-44;
-  const bool ambiguous =
-      kind != 2 && __double2float_rn((s - delta) * kInvD) != __double2float_rn((s + delta) * kInvD);
-  if (__any_sync(0xffffffffu, ambiguous)) {
-    // ggml's order: element 0, 1, ..., 127 of this group's row.
-    double seq = 0.0;
-    for (int srcl = 0; srcl < kLanesPerRow; ++srcl) {
+    if (t_row != cur_t) {
+      cur_t = t_row;
+      pos = p.positions[t_row];
+      pos_ok = pos >= 0 && pos < p.max_position;
+      if (pos_ok) {
+        const float4* cs =
+            reinterpret_cast<const float4*>(p.rope + (long long)pos * kHalf + kPer * l8);
 #pragma unroll
-      for (int e = 0; e < kElems; ++e) {
-        const float v = __shfl_sync(0xffffffffu, sq[e], srcl, kLanesPerRow);
-        seq = __dadd_rn(seq, (double)v);
+        for (int j = 0; j < kPer / 2; ++j) {
+          const float4 a = __ldg(cs + j);
+          c[2 * j] = a.x; sn[2 * j] = a.y; c[2 * j + 1] = a.z; sn[2 * j + 1] = a.w;
+        }
       }
     }
-    s = seq;
-  }
-  const float mean = __double2float_rn(s * kInvD);
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
 
-  float y[kElems];
-  if (kind != 2) {
-    const uint4* wp = reinterpret_cast<const uint4*>((kind == 0 ? p.qw : p.kw) + kElems * l8);
-    const uint4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
-    const uint32_t w8[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    // ---- RMSNorm (q and k rows; v rows compute it too and discard it) ----
+    double s = 0.0;
 #pragma unroll
-    for (int e = 0; e < kElems; ++e) {
-      const float w = (e & 1) ? bf16hi_to_f32(w8[e >> 1]) : bf16lo_to_f32(w8[e >> 1]);
-      y[e] = __fmul_rn(__fmul_rn(x[e], scale), w);
-    }
-  } else {
+    for (int e = 0; e < 2 * kPer; ++e) s = __dadd_rn(s, (double)__fmul_rn(x[e], x[e]));
 #pragma unroll
-    for (int e = 0; e < kElems; ++e) y[e] = x[e];
-  }
+    for (int o = kLanesPerRow / 2; o >= 1; o >>= 1)
+      s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o, kLanesPerRow));
 
-  // ---- NEOX RoPE: element i pairs with i+64 (lane l8 pairs with l8^4) ----
-  float partner[kElems];
+    // sum / 128 is exact as a multiplication by 2^-7 (no double division).
+    constexpr double kInvD = 1.0 / kD;
+    static_assert(kD == 128, "1/kD must be a power of two");
+    const double delta = s * 0x1p-44;
+    const bool ambiguous = kind != 2 && __double2float_rn((s - delta) * kInvD) !=
+                                            __double2float_rn((s + delta) * kInvD);
+    if (__any_sync(0xffffffffu, ambiguous)) {
+      // ggml's order: elements 0..63 (lanes 0..7, first halves), then 64..127.
+      double seq = 0.0;
 #pragma unroll
-  for (int e = 0; e < kElems; ++e)
-    partner[e] = __shfl_xor_sync(0xffffffffu, y[e], kLanesPerRow / 2, kLanesPerRow);
+      for (int h = 0; h < 2; ++h) {
+        for (int srcl = 0; srcl < kLanesPerRow; ++srcl) {
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) {
+            const float v = __shfl_sync(0xffffffffu, x[h * kPer + e], srcl, kLanesPerRow);
+            seq = __dadd_rn(seq, (double)__fmul_rn(v, v));
+          }
+        }
+      }
+      s = seq;
+    }
 
-  const int pos = p.positions[t];
-  bool ok = valid;
-  if (valid && (pos < 0 || pos >= p.max_position)) {
-    record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 1, pos);
-    ok = false;
-  }
-  if (kind != 2 && ok) {
-    const float4* cs =
-        reinterpret_cast<const float4*>(p.rope + (long long)pos * (kD / 2) + kElems * (l8 & 3));
-    float c[kElems], sn[kElems];
+    if (valid && !pos_ok) record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 1, pos);
+    const bool ok = valid && pos_ok;
+    if (kind != 2) {
+      const float mean = __double2float_rn(s * kInvD);
+      const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+      if (kind != cur_kind) {
+        cur_kind = kind;
+        const uint16_t* wp = (kind == 0 ? p.qw : p.kw) + kPer * l8;
+        w[0] = __ldg(reinterpret_cast<const uint4*>(wp));
+        w[1] = __ldg(reinterpret_cast<const uint4*>(wp + kHalf));
+      }
 #pragma unroll
-    for (int j = 0; j < kElems / 2; ++j) {
-      const float4 a = __ldg(cs + j);
-      c[2 * j] = a.x; sn[2 * j] = a.y; c[2 * j + 1] = a.z; sn[2 * j + 1] = a.w;
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t w4[4] = {w[h].x, w[h].y, w[h].z, w[h].w};
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          const float wf = (e & 1) ? bf16hi_to_f32(w4[e >> 1]) : bf16lo_to_f32(w4[e >> 1]);
+          x[h * kPer + e] = __fmul_rn(__fmul_rn(x[h * kPer + e], scale), wf);
+        }
+      }
+      // ---- NEOX RoPE: element i pairs with i+64 ----
+      if (ok) {
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          const float x0 = x[e], x1 = x[kPer + e];
+          x[e] = __fsub_rn(__fmul_rn(x0, c[e]), __fmul_rn(x1, sn[e]));
+          x[kPer + e] = __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, c[e]));
+        }
+      }
     }
-    if (l8 < 4) {
-#pragma unroll
-      for (int e = 0; e < kElems; ++e)
-        y[e] = __fsub_rn(__fmul_rn(y[e], c[e]), __fmul_rn(partner[e], sn[e]));
-    } else {
-#pragma unroll
-      for (int e = 0; e < kElems; ++e)
-        y[e] = __fadd_rn(__fmul_rn(partner[e], sn[e]), __fmul_rn(y[e], c[e]));
-    }
-  }
-  if (!ok) return;
+    if (!ok) continue;
 
-  // ---- stores ----
-  if (kind == 0) {
-    const long long off = ((long long)t * p.Hq + head) * kD + kElems * l8;
-    if (kQOutBf16) {
-      store16_bf16(static_cast<uint16_t*>(p.q_out) + off, y);
-    } else {
-      float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.q_out) + off);
+    // ---- stores ----
+    if (kind == 0) {
+      const long long off = ((long long)t_row * p.Hq + rr_row) * kD + kPer * l8;
+      if (kQOutBf16) {
+        uint16_t* o = static_cast<uint16_t*>(p.q_out) + off;
+        *reinterpret_cast<uint4*>(o) = pack8_bf16(x);
+        *reinterpret_cast<uint4*>(o + kHalf) = pack8_bf16(x + kPer);
+      } else {
+        float* o = static_cast<float*>(p.q_out) + off;
 #pragma unroll
-      for (int i = 0; i < kElems / 4; ++i)
-        o[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+        for (int h = 0; h < 2; ++h) {
+          float4* o4 = reinterpret_cast<float4*>(o + h * kHalf);
+          o4[0] = make_float4(x[h * kPer], x[h * kPer + 1], x[h * kPer + 2], x[h * kPer + 3]);
+          o4[1] = make_float4(x[h * kPer + 4], x[h * kPer + 5], x[h * kPer + 6], x[h * kPer + 7]);
+        }
+      }
+      continue;
     }
-    return;
+    const int slot = p.slots[t_row];
+    if (slot < 0) continue;
+    if ((long long)slot >= p.n_slots) {
+      record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 2, slot);
+      continue;
+    }
+    const int head = kind == 1 ? rr_row - p.Hq : rr_row - p.Hq - p.Hkv;
+    uint16_t* dst = (kind == 1 ? p.k_cache : p.v_cache) +
+                    (((long long)p.layer * p.n_slots + slot) * p.Hkv + head) * kD + kPer * l8;
+    *reinterpret_cast<uint4*>(dst) = pack8_bf16(x);
+    *reinterpret_cast<uint4*>(dst + kHalf) = pack8_bf16(x + kPer);
   }
-  const int slot = p.slots[t];
-  if (slot < 0) return;
-  if ((long long)slot >= p.n_slots) {
-    record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 2, slot);
-    return;
-  }
-  uint16_t* cache = kind == 1 ? p.k_cache : p.v_cache;
-  store16_bf16(cache + (((long long)p.layer * p.n_slots + slot) * p.Hkv + head) * kD + kElems * l8,
-               y);
 }
 
 }  // namespace
@@ -230,8 +255,14 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
   p.v_cache = v_cache;
   p.status = h->status_dev;
   const long long rows = (long long)n_tokens * (p.Hq + 2 * p.Hkv);
-  const long long blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-  if (blocks > 0x7fffffffLL) return NVATTN_ERR_INVALID_ARG;
+  if (rows > 0x7fffffffLL - kMaxRowsPerGroup * kGroupsPerBlock) return NVATTN_ERR_INVALID_ARG;
+  p.total_rows = (int)rows;
+  // Enough groups for about four resident blocks per SM; beyond that each
+  // group takes more rows so the per-token loads are shared.
+  const long long per_wave = (long long)h->sm_count * 4 * kGroupsPerBlock;
+  p.rows_per_group = (int)std::max(1LL, std::min<long long>(kMaxRowsPerGroup, rows / per_wave));
+  const long long groups = (rows + p.rows_per_group - 1) / p.rows_per_group;
+  const long long blocks = (groups + kGroupsPerBlock - 1) / kGroupsPerBlock;
   if (q_out_dtype == NVATTN_DTYPE_BF16)
     kv_store_qk_norm_rope_kernel<true><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
   else

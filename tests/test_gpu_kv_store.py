@@ -36,7 +36,10 @@ def test_golden_fixture_bit_exact(cuda):
     assert np.array_equal(host_bits(vc)[0, slots], fx["v_rows"])
 
 
-@pytest.mark.parametrize("Hq,Hkv,T", [(16, 8, 3000), (32, 8, 777), (8, 1, 513), (64, 8, 129)])
+# (8, 1, 20000): ten rows per token, so an 8-lane group's run of rows crosses
+# token boundaries and the (cos, sin) reload path is exercised.
+@pytest.mark.parametrize("Hq,Hkv,T", [(16, 8, 3000), (32, 8, 777), (8, 1, 513), (64, 8, 129),
+                                      (8, 1, 20000)])
 @pytest.mark.parametrize("q_bf16", [False, True])
 def test_random_tokens_bit_exact(cuda, Hq, Hkv, T, q_bf16):
     rng = np.random.default_rng(Hq * 1000 + T)
@@ -108,3 +111,31 @@ def test_in_place_f32_q(cuda):
     oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos, slots, np.zeros((1, 512, Hkv, 128), np.uint16),
                               np.zeros((1, 512, Hkv, 128), np.uint16))
     assert np.array_equal(dq.cpu().numpy().view(np.uint32), oq.view(np.uint32))
+
+
+def test_rms_mean_on_rounding_midpoint_uses_sequential_sum(cuda):
+    """Rows whose sum of squares / 128 sits exactly on a float rounding
+    midpoint (1 + 2^-24): the kernel's 8-lane tree sum is flagged as
+    ambiguous there and redone in the reference's index order."""
+    rng = np.random.default_rng(8)
+    T, Hq, Hkv = 64, 16, 8
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    mid = np.ones(128, np.float32)
+    mid[77] = np.float32(1 + 2.0 ** -18)  # square rounds to 1 + 2^-17 exactly
+    q[::3, 5] = mid
+    k[1::5, 2] = mid[::-1]
+    w = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(128)).astype(np.float32))
+    pos = rng.integers(0, 40960, T).astype(np.int32)
+    slots = np.arange(T, dtype=np.int32)
+    h = handle(Hq, Hkv, 1)
+    qo, kc, vc = run_store(h, 0, q, k, v, w, w, pos, slots, 256, Hkv)
+    h.check_device()
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=256)
+    okc = np.zeros((1, 256, Hkv, 128), np.uint16)
+    ovc = np.zeros_like(okc)
+    oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos, slots, okc, ovc)
+    assert np.array_equal(qo.cpu().numpy().view(np.uint32), oq.view(np.uint32))
+    assert np.array_equal(host_bits(kc), okc)
+    assert np.array_equal(host_bits(vc), ovc)
