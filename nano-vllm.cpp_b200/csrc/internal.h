@@ -31,7 +31,7 @@ struct nvattn_handle {
   int64_t n_slots;  // num_blocks * block_size (slots per layer)
   int sm_count;
 
-  float* rope_table_dev = nullptr;  // [max_position][head_dim/2][2] (cos, sin)
+  float* rope_table_dev = nullptr;  // [max_position][cos x head_dim/2 | sin x head_dim/2]
   nvattn::DeviceStatus* status_dev = nullptr;
 
   // split-KV workspace for decode

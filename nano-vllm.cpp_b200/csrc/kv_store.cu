@@ -7,25 +7,40 @@
 //
 // Eight lanes own a 128-element head row.  Lane l holds elements
 // [8l, 8l+8) and their NEOX partners [64+8l, 64+8l+8), so the rotation needs
-// no shuffle and each lane needs only 8 (cos, sin) pairs.  Each half is two
-// 16-byte loads and one 16-byte bf16 store.  An 8-lane group walks
-// `rows_per_group` consecutive rows of the flattened [token][Hq q | Hkv k |
-// Hkv v] row list, reloads the norm weights only when the row kind changes
-// and the (cos, sin) pairs only when the token changes, and prefetches
-// the next row's input while it works on the current one.
+// no shuffle and each lane needs only 8 cos and 8 sin values.  Each half
+// leaves as one 16-byte bf16 store.  The arithmetic runs on packed f32x2
+// instructions where no add follows a product (squares, norm scaling); the
+// rotation, a sum of two products, stays scalar.
+//
+// Two kernels share that row math:
+//  * kv_store_staged_kernel (large batches): one persistent CTA per SM.  A
+//    producer warp streams chunks of whole tokens -- their q, k and v rows
+//    (three contiguous ranges) and each token's cos/sin row -- into a ring of
+//    shared-memory stages with bulk async copies, so ~150 KB per SM are in
+//    flight without holding registers.  The number of consumer warps is
+//    chosen per model so that each stage's rows split evenly over them (four
+//    rows per warp per pass, no idle groups).
+//  * kv_store_rows_kernel (small batches, e.g. one decode token per
+//    sequence): each 8-lane group walks a short run of consecutive rows with
+//    register loads and a one-row prefetch.
 //
 // Bit-exactness with the reference's ggml CPU path:
 //  * RMSNorm: ggml sums float squares in double in index order, rounds
 //    mean = sum/128 to float, scale = 1/sqrtf(mean+eps), y = (x*scale)*w.
-//    Here the squares are summed in double by an 8-lane tree.  The tree and
-//    the sequential sum both lie within 2^-45*sum of the exact sum, so the
-//    float mean can only differ when sum/128 lies within that distance of a
-//    float rounding boundary.  That case is detected (both ends of the
-//    interval are rounded) and the warp then redoes the sum in ggml's exact
-//    index order.
+//    Here the squares are summed in double by a tree.  The tree and the
+//    sequential sum both lie within 2^-45*sum of the exact sum, so the float
+//    mean can only differ when sum/128 lies within that distance of a float
+//    rounding boundary.  That case is detected (both ends of the interval are
+//    rounded) and the warp then redoes the sum in ggml's exact index order.
 //  * RoPE: cos/sin come from the host-built table (ggml's float recurrence);
-//    the rotation uses separately rounded products (no FMA contraction).
-//  * Store: ggml_compute_fp32_to_bf16 rounding.
+//    the rotation uses separately rounded products (scalar .rn intrinsics,
+//    which are never contracted into an FMA).
+//  * Store: ggml_compute_fp32_to_bf16 rounding.  For finite values that is
+//    round-to-nearest-even, i.e. cvt.rn.bf16x2.f32; a row that may hold a NaN
+//    (non-finite input, or norm weights of magnitude >= 2^120) takes ggml's
+//    bit rule instead, which keeps the NaN payload.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -34,11 +49,22 @@ namespace {
 
 constexpr int kD = 128;
 constexpr int kHalf = kD / 2;
+constexpr int kRowBytes = kD * 4;
 constexpr int kLanesPerRow = 8;
 constexpr int kPer = kHalf / kLanesPerRow;  // 8 elements per lane per half
 constexpr int kThreads = 256;
 constexpr int kGroupsPerBlock = kThreads / kLanesPerRow;
 constexpr int kMaxRowsPerGroup = 8;
+
+// staged kernel
+constexpr int kMinConsumerWarps = 8;
+constexpr int kMaxConsumerWarps = 20;
+constexpr int kStageMaxThreads = (kMaxConsumerWarps + 1) * 32;
+constexpr int kMaxStages = 8;
+constexpr int kMaxTokensPerStage = 32;  // one producer lane per token
+constexpr int kStageHeader = 4096;      // barriers, flags, per-stage positions/slots
+constexpr int kStageMaxBytes = 56 * 1024;
+constexpr int kStageSmemBudget = 227 * 1024;
 
 struct KvStoreParams {
   int n_tokens, Hq, Hkv, layer, max_position, rows_per_group;
@@ -52,20 +78,194 @@ struct KvStoreParams {
   const uint16_t* kw;
   const int32_t* positions;
   const int32_t* slots;
-  const float2* rope;  // [max_position][64] (cos, sin)
+  const float* rope;  // [max_position][cos x 64 | sin x 64]
   void* q_out;
   uint16_t* k_cache;
   uint16_t* v_cache;
   DeviceStatus* status;
 };
 
-__device__ __forceinline__ uint4 pack8_bf16(const float* y) {
+// Per-lane norm weights of one row kind (16 bf16, packed in pairs) and
+// whether they are small enough (|w| < 2^120, finite) that a finite input
+// row cannot produce a NaN.
+struct LaneWeights {
+  uint32_t w[kPer];
+  bool tame;
+};
+
+__device__ __forceinline__ void load_weights(const uint16_t* wsrc, int l8, LaneWeights& lw) {
+  const uint4 a = __ldg(reinterpret_cast<const uint4*>(wsrc + kPer * l8));
+  const uint4 b = __ldg(reinterpret_cast<const uint4*>(wsrc + kHalf + kPer * l8));
+  const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  bool tame = true;
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    lw.w[e] = u[e];
+    // bf16 magnitude bits < 0x7b80 <=> |w| < 2^120 (inf and NaN excluded)
+    tame = tame && (u[e] & 0x7fffu) < 0x7b80u && ((u[e] >> 16) & 0x7fffu) < 0x7b80u;
+  }
+  lw.tame = tame;
+}
+
+// RMSNorm scale 1/sqrt(mean(x^2) + eps) of the group's row, bit-exact with
+// ggml's double accumulation.  Warp-collective: every lane of the warp calls
+// it (rows that are not normed pass norm_row = false).  `finite` tells
+// whether the whole row is finite (sum of squares finite).
+__device__ __forceinline__ float rms_scale(const float (&x)[2 * kPer], bool norm_row, float eps,
+                                           bool& finite) {
+  double d[2 * kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const uint64_t x2 = pack2(x[2 * k], x[2 * k + 1]);
+    float s0, s1;
+    unpack2(fmul2(x2, x2), s0, s1);
+    d[2 * k] = (double)s0;
+    d[2 * k + 1] = (double)s1;
+  }
+#pragma unroll
+  for (int w = 1; w < 2 * kPer; w *= 2) {
+#pragma unroll
+    for (int e = 0; e < 2 * kPer; e += 2 * w) d[e] = __dadd_rn(d[e], d[e + w]);
+  }
+  double s = d[0];
+#pragma unroll
+  for (int o = kLanesPerRow / 2; o >= 1; o >>= 1)
+    s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o, kLanesPerRow));
+  finite = s <= 1.7976931348623157e308;  // false for inf and NaN
+
+  // sum / 128 is exact as a multiplication by 2^-7 (no double division).
+  constexpr double kInvD = 1.0 / kD;
+  static_assert(kD == 128, "1/kD must be a power of two");
+  // Rounding d = sum/128 to float drops the low 29 of its 52 mantissa bits;
+  // d sits near a float rounding boundary when those bits are within 512
+  // double ulps (> 2^-44 relative, three times the largest tree-vs-sequential
+  // difference) of one half.  Outside the normal float range the exact sum
+  // is always redone.
+  const double dm = s * kInvD;
+  const int hi = __double2hiint(dm);
+  const int ex = (hi >> 20) & 0x7ff;
+  const int dropped = __double2loint(dm) & 0x1fffffff;
+  const bool ambiguous =
+      norm_row && (abs(dropped - 0x10000000) <= 512 || ex < 1023 - 126 || ex > 1023 + 127);
+  if (__any_sync(0xffffffffu, ambiguous)) {
+    // ggml's order: elements 0..63 (lanes 0..7, first halves), then 64..127.
+    double seq = 0.0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      for (int srcl = 0; srcl < kLanesPerRow; ++srcl) {
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          const float v = __shfl_sync(0xffffffffu, x[h * kPer + e], srcl, kLanesPerRow);
+          seq = __dadd_rn(seq, (double)__fmul_rn(v, v));
+        }
+      }
+    }
+    s = seq;
+  }
+  if (!norm_row) return 1.0f;
+  const float mean = __double2float_rn(s * kInvD);
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+// y = (x * scale) * w, then the NEOX rotation (element i with i+64):
+//   y_i' = y_i*cos - y_{i+64}*sin,  y_{i+64}' = y_i*sin + y_{i+64}*cos.
+__device__ __forceinline__ void norm_rope(float (&x)[2 * kPer], float scale,
+                                          const float (&w)[2 * kPer], const float (&c)[kPer],
+                                          const float (&sn)[kPer]) {
+  const uint64_t sc = pack2(scale, scale);
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const uint64_t y =
+        fmul2(fmul2(pack2(x[2 * k], x[2 * k + 1]), sc), pack2(w[2 * k], w[2 * k + 1]));
+    unpack2(y, x[2 * k], x[2 * k + 1]);
+  }
+  // Scalar .rn intrinsics here: ptxas fuses a packed mul.rn.f32x2 with a
+  // following packed add/sub into an FMA (even under -fmad=false), which
+  // would skip the rounding of one product.
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    const float x0 = x[e], x1 = x[kPer + e];
+    x[e] = __fsub_rn(__fmul_rn(x0, c[e]), __fmul_rn(x1, sn[e]));
+    x[kPer + e] = __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, c[e]));
+  }
+}
+
+__device__ __forceinline__ uint4 pack8_bf16(const float* y, bool nan_rule) {
   uint4 a;
-  a.x = pack_bf16x2(y[0], y[1]);
-  a.y = pack_bf16x2(y[2], y[3]);
-  a.z = pack_bf16x2(y[4], y[5]);
-  a.w = pack_bf16x2(y[6], y[7]);
+  if (!nan_rule) {
+    a.x = cvt_bf16x2(y[0], y[1]);
+    a.y = cvt_bf16x2(y[2], y[3]);
+    a.z = cvt_bf16x2(y[4], y[5]);
+    a.w = cvt_bf16x2(y[6], y[7]);
+  } else {
+    a.x = pack_bf16x2(y[0], y[1]);
+    a.y = pack_bf16x2(y[2], y[3]);
+    a.z = pack_bf16x2(y[4], y[5]);
+    a.w = pack_bf16x2(y[6], y[7]);
+  }
   return a;
+}
+
+// Writes the finished row: q rows to q_out, k/v rows to slot_mapping[t] of
+// the cache (slot < 0: not stored; slot >= n_slots: reported).
+template <bool kQOutBf16>
+__device__ __forceinline__ void store_row(const KvStoreParams& p, const float (&x)[2 * kPer],
+                                          int t, int rr, int kind, int slot, bool nan_rule,
+                                          int l8) {
+  if (kind == 0) {
+    const long long off = ((long long)t * p.Hq + rr) * kD + kPer * l8;
+    if (kQOutBf16) {
+      uint16_t* o = static_cast<uint16_t*>(p.q_out) + off;
+      *reinterpret_cast<uint4*>(o) = pack8_bf16(x, nan_rule);
+      *reinterpret_cast<uint4*>(o + kHalf) = pack8_bf16(x + kPer, nan_rule);
+    } else {
+      float* o = static_cast<float*>(p.q_out) + off;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float4* o4 = reinterpret_cast<float4*>(o + h * kHalf);
+        o4[0] = make_float4(x[h * kPer], x[h * kPer + 1], x[h * kPer + 2], x[h * kPer + 3]);
+        o4[1] = make_float4(x[h * kPer + 4], x[h * kPer + 5], x[h * kPer + 6], x[h * kPer + 7]);
+      }
+    }
+    return;
+  }
+  if (slot < 0) return;
+  if ((long long)slot >= p.n_slots) {
+    record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 2, slot);
+    return;
+  }
+  const int head = kind == 1 ? rr - p.Hq : rr - p.Hq - p.Hkv;
+  uint16_t* dst = (kind == 1 ? p.k_cache : p.v_cache) +
+                  (((long long)p.layer * p.n_slots + slot) * p.Hkv + head) * kD + kPer * l8;
+  *reinterpret_cast<uint4*>(dst) = pack8_bf16(x, nan_rule);
+  *reinterpret_cast<uint4*>(dst + kHalf) = pack8_bf16(x + kPer, nan_rule);
+}
+
+// Norm, rotate and store one row (x already loaded; every lane of the warp
+// calls this, `active` false for padding rows).  get_w(w) and get_cs(c, sn)
+// supply the lane's norm weights and cos/sin values; they run after the
+// norm's dependency chain so the values are live only where they are used.
+template <bool kQOutBf16, class GetW, class GetCs>
+__device__ __forceinline__ void finish_row(const KvStoreParams& p, float (&x)[2 * kPer],
+                                           bool active, int t, int rr, int kind, int pos,
+                                           bool pos_ok, int slot, GetW get_w, bool w_tame,
+                                           GetCs get_cs, int l8) {
+  bool finite;
+  const float scale = rms_scale(x, kind != 2, p.eps, finite);
+  if (!active) return;
+  if (!pos_ok) {
+    record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 1, pos);
+    return;
+  }
+  bool nan_rule = !finite;
+  if (kind != 2) {
+    float w[2 * kPer], c[kPer], sn[kPer];
+    get_w(w);
+    get_cs(c, sn);
+    norm_rope(x, scale, w, c, sn);
+    nan_rule = nan_rule || !w_tame;
+  }
+  store_row<kQOutBf16>(p, x, t, rr, kind, slot, nan_rule, l8);
 }
 
 // Input row of flattened row (t, rr): q, k or v head row.
@@ -89,7 +289,7 @@ __device__ __forceinline__ void load_row(const float* src, int l8, float (&x)[2 
 }
 
 template <bool kQOutBf16>
-__global__ void __launch_bounds__(kThreads, 3) kv_store_qk_norm_rope_kernel(KvStoreParams p) {
+__global__ void __launch_bounds__(kThreads, 2) kv_store_rows_kernel(KvStoreParams p) {
   const int l8 = threadIdx.x & 7;  // lane within the row's 8-lane group
   const int rows_per_token = p.Hq + 2 * p.Hkv;
   const int group = blockIdx.x * kGroupsPerBlock + (threadIdx.x >> 3);
@@ -106,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 3) kv_store_qk_norm_rope_kernel(KvSt
   int cur_t = -1, pos = 0, cur_kind = -1;
   bool pos_ok = false;
   float c[kPer], sn[kPer];
-  uint4 w[2];  // norm weights of this lane's 16 elements (packed bf16 pairs)
+  LaneWeights lw;
 
   for (int it = 0; it < p.rows_per_group; ++it) {
     const bool valid = row0 + it < p.total_rows;
@@ -120,114 +320,297 @@ __global__ void __launch_bounds__(kThreads, 3) kv_store_qk_norm_rope_kernel(KvSt
       load_row(row_src(p, t, rr), l8, xn);
     }
     const int kind = rr_row < p.Hq ? 0 : (rr_row < p.Hq + p.Hkv ? 1 : 2);
-
     if (t_row != cur_t) {
       cur_t = t_row;
       pos = p.positions[t_row];
       pos_ok = pos >= 0 && pos < p.max_position;
       if (pos_ok) {
         const float4* cs =
-            reinterpret_cast<const float4*>(p.rope + (long long)pos * kHalf + kPer * l8);
+            reinterpret_cast<const float4*>(p.rope + (long long)pos * kD + kPer * l8);
 #pragma unroll
-        for (int j = 0; j < kPer / 2; ++j) {
-          const float4 a = __ldg(cs + j);
-          c[2 * j] = a.x; sn[2 * j] = a.y; c[2 * j + 1] = a.z; sn[2 * j + 1] = a.w;
+        for (int j = 0; j < 2; ++j) {
+          const float4 a = __ldg(cs + j), b = __ldg(cs + kHalf / 4 + j);
+          c[4 * j] = a.x; c[4 * j + 1] = a.y; c[4 * j + 2] = a.z; c[4 * j + 3] = a.w;
+          sn[4 * j] = b.x; sn[4 * j + 1] = b.y; sn[4 * j + 2] = b.z; sn[4 * j + 3] = b.w;
         }
       }
     }
-
-    // ---- RMSNorm (q and k rows; v rows compute it too and discard it) ----
-    double s = 0.0;
-#pragma unroll
-    for (int e = 0; e < 2 * kPer; ++e) s = __dadd_rn(s, (double)__fmul_rn(x[e], x[e]));
-#pragma unroll
-    for (int o = kLanesPerRow / 2; o >= 1; o >>= 1)
-      s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o, kLanesPerRow));
-
-    // sum / 128 is exact as a multiplication by 2^-7 (no double division).
-    constexpr double kInvD = 1.0 / kD;
-    static_assert(kD == 128, "1/kD must be a power of two");
-    const double delta = s * 0x1p-44;
-    const bool ambiguous = kind != 2 && __double2float_rn((s - delta) * kInvD) !=
-                                            __double2float_rn((s + delta) * kInvD);
-    if (__any_sync(0xffffffffu, ambiguous)) {
-      // ggml's order: elements 0..63 (lanes 0..7, first halves), then 64..127.
-      double seq = 0.0;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        for (int srcl = 0; srcl < kLanesPerRow; ++srcl) {
-#pragma unroll
-          for (int e = 0; e < kPer; ++e) {
-            const float v = __shfl_sync(0xffffffffu, x[h * kPer + e], srcl, kLanesPerRow);
-            seq = __dadd_rn(seq, (double)__fmul_rn(v, v));
-          }
-        }
-      }
-      s = seq;
+    if (kind != 2 && kind != cur_kind) {
+      cur_kind = kind;
+      load_weights(kind == 0 ? p.qw : p.kw, l8, lw);
     }
-
-    if (valid && !pos_ok) record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 1, pos);
-    const bool ok = valid && pos_ok;
-    if (kind != 2) {
-      const float mean = __double2float_rn(s * kInvD);
-      const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-      if (kind != cur_kind) {
-        cur_kind = kind;
-        const uint16_t* wp = (kind == 0 ? p.qw : p.kw) + kPer * l8;
-        w[0] = __ldg(reinterpret_cast<const uint4*>(wp));
-        w[1] = __ldg(reinterpret_cast<const uint4*>(wp + kHalf));
-      }
+    const int slot = (valid && kind != 0) ? p.slots[t_row] : 0;
+    finish_row<kQOutBf16>(p, x, valid, t_row, rr_row, kind, pos, pos_ok, slot,
+                          [&](float (&w)[2 * kPer]) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t w4[4] = {w[h].x, w[h].y, w[h].z, w[h].w};
+                            for (int e = 0; e < kPer; ++e) {
+                              w[2 * e] = bf16lo_to_f32(lw.w[e]);
+                              w[2 * e + 1] = bf16hi_to_f32(lw.w[e]);
+                            }
+                          },
+                          lw.tame,
+                          [&](float (&cc)[kPer], float (&ss)[kPer]) {
 #pragma unroll
-        for (int e = 0; e < kPer; ++e) {
-          const float wf = (e & 1) ? bf16hi_to_f32(w4[e >> 1]) : bf16lo_to_f32(w4[e >> 1]);
-          x[h * kPer + e] = __fmul_rn(__fmul_rn(x[h * kPer + e], scale), wf);
-        }
-      }
-      // ---- NEOX RoPE: element i pairs with i+64 ----
-      if (ok) {
-#pragma unroll
-        for (int e = 0; e < kPer; ++e) {
-          const float x0 = x[e], x1 = x[kPer + e];
-          x[e] = __fsub_rn(__fmul_rn(x0, c[e]), __fmul_rn(x1, sn[e]));
-          x[kPer + e] = __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, c[e]));
-        }
-      }
-    }
-    if (!ok) continue;
-
-    // ---- stores ----
-    if (kind == 0) {
-      const long long off = ((long long)t_row * p.Hq + rr_row) * kD + kPer * l8;
-      if (kQOutBf16) {
-        uint16_t* o = static_cast<uint16_t*>(p.q_out) + off;
-        *reinterpret_cast<uint4*>(o) = pack8_bf16(x);
-        *reinterpret_cast<uint4*>(o + kHalf) = pack8_bf16(x + kPer);
-      } else {
-        float* o = static_cast<float*>(p.q_out) + off;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float4* o4 = reinterpret_cast<float4*>(o + h * kHalf);
-          o4[0] = make_float4(x[h * kPer], x[h * kPer + 1], x[h * kPer + 2], x[h * kPer + 3]);
-          o4[1] = make_float4(x[h * kPer + 4], x[h * kPer + 5], x[h * kPer + 6], x[h * kPer + 7]);
-        }
-      }
-      continue;
-    }
-    const int slot = p.slots[t_row];
-    if (slot < 0) continue;
-    if ((long long)slot >= p.n_slots) {
-      record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 2, slot);
-      continue;
-    }
-    const int head = kind == 1 ? rr_row - p.Hq : rr_row - p.Hq - p.Hkv;
-    uint16_t* dst = (kind == 1 ? p.k_cache : p.v_cache) +
-                    (((long long)p.layer * p.n_slots + slot) * p.Hkv + head) * kD + kPer * l8;
-    *reinterpret_cast<uint4*>(dst) = pack8_bf16(x);
-    *reinterpret_cast<uint4*>(dst + kHalf) = pack8_bf16(x + kPer);
+                            for (int e = 0; e < kPer; ++e) {
+                              cc[e] = c[e];
+                              ss[e] = sn[e];
+                            }
+                          },
+                          l8);
   }
+}
+
+struct StagedPlan {
+  int tokens_per_stage;  // whole tokens per shared-memory stage (nt)
+  int consumer_warps;    // W; the producer is warp W
+  int passes;            // ceil(nt * rows_per_token / (4 W)): four rows per warp per pass
+  int n_stages;          // ring depth
+  int stage_bytes;
+  int n_chunks;          // ceil(n_tokens / nt)
+};
+
+// Reads 8 consecutive floats (chunks 2*l8 and 2*l8+1 of a 64-float half row)
+// from shared memory.  The eight lanes' 32-byte pieces span 256 bytes, a
+// two-way bank conflict; shared-memory bandwidth has the room, and swapping
+// the chunk order per lane would cost more issue slots (selects) than the
+// conflict costs.
+__device__ __forceinline__ void lds_lane8(const float4* half_row, int l8, float* out) {
+  const float4 a = half_row[2 * l8];
+  const float4 b = half_row[2 * l8 + 1];
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+
+// Norm weights in shared memory as floats, laid out [kind][j][lane l8][4] so
+// that load j of the eight lanes reads 128 contiguous bytes.  Lane l8's
+// floats f = 0..15 are elements 8*l8 + f (f < 8) and 64 + 8*l8 + (f - 8).
+constexpr int kWeightsOffset = 256 + kMaxStages * 2 * kMaxTokensPerStage * 4;
+__device__ __forceinline__ int lane_weight_slot(int el) {
+  const int l8 = (el & 63) >> 3;
+  const int f = (el & 7) + (el >= 64 ? 8 : 0);
+  return ((f >> 2) * 8 + l8) * 4 + (f & 3);
+}
+
+// Stage layout (nt tokens, rows_per_token = Hq + 2 Hkv):
+//   [nt*Hq q rows][nt*Hkv k rows][nt*Hkv v rows][nt cos/sin rows], each row
+//   512 bytes; the q, k and v ranges are each one contiguous bulk copy.
+// The header holds the ring's barriers and, per stage, the chunk's positions
+// and slots (written by the producer warp before it arms the stage, so the
+// consumers never wait on a global load).
+template <bool kQOutBf16>
+__global__ void __launch_bounds__(kStageMaxThreads, 1)
+    kv_store_staged_kernel(KvStoreParams p, StagedPlan plan) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  int* abort_flag = reinterpret_cast<int*>(empty + kMaxStages);
+  int* skip = abort_flag + 1;
+  int* meta = reinterpret_cast<int*>(smem + 256);  // [stage][pos | slot][kMaxTokensPerStage]
+  float* wsm = reinterpret_cast<float*>(smem + kWeightsOffset);  // [2][128]
+  int* wild = skip + 1;  // [2]: some weight of q / k is not tame
+  uint8_t* stages = smem + kStageHeader;
+  static_assert(kWeightsOffset + 2 * kD * 4 <= kStageHeader, "header");
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int W = plan.consumer_warps;
+  const int nt = plan.tokens_per_stage;
+  const int rpt = p.Hq + 2 * p.Hkv;
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < plan.n_stages; ++b) {
+      mbar_init(&full[b], 1);
+      mbar_init(&empty[b], W);
+    }
+    *abort_flag = 0;
+    *skip = timeout_recorded(p.status) ? 1 : 0;
+    wild[0] = wild[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 2 * kD; idx += blockDim.x) {
+    const int kind = idx / kD, el = idx % kD;
+    const uint32_t b = (kind == 0 ? p.qw : p.kw)[el];
+    wsm[kind * kD + lane_weight_slot(el)] = __uint_as_float(b << 16);
+    if ((b & 0x7fffu) >= 0x7b80u) wild[kind] = 1;  // |w| >= 2^120, inf or NaN
+  }
+  __syncthreads();
+  if (*skip) return;
+
+  if (warp == W) {
+    // ---- producer warp: lane j handles token j of the chunk; lane 0 issues
+    // the three row-range copies.  The next chunk's positions and slots are
+    // loaded while this one is set up, off the critical path. ----
+    const uint64_t pol = l2_policy_evict_first();
+    int npos = 0, nslot = -1;
+    auto fetch = [&](int chk) {
+      const int t = chk * nt + lane;
+      if (chk < plan.n_chunks && lane < nt && t < p.n_tokens) {
+        npos = p.positions[t];
+        nslot = p.slots[t];
+      }
+    };
+    fetch(blockIdx.x);
+    int it = 0;
+    for (int ch = blockIdx.x; ch < plan.n_chunks; ch += gridDim.x, ++it) {
+      const int pos = npos, slot = nslot;
+      fetch(ch + gridDim.x);
+      const int buf = it % plan.n_stages;
+      const int use = it / plan.n_stages;
+      bool ok = true;
+      if (use > 0) ok = mbar_wait(&empty[buf], (use - 1) & 1, p.status, 50, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int t0 = ch * nt;
+      const int ntc = min(nt, p.n_tokens - t0);
+      const bool cs_valid = lane < ntc && pos >= 0 && pos < p.max_position;
+      if (lane < ntc) {
+        meta[(buf * 2 + 0) * kMaxTokensPerStage + lane] = pos;
+        meta[(buf * 2 + 1) * kMaxTokensPerStage + lane] = slot;
+      }
+      const uint32_t n_cs = __popc(__ballot_sync(0xffffffffu, cs_valid));
+      __syncwarp();  // the meta stores precede lane 0's arrive (release)
+      uint8_t* st = stages + (size_t)buf * plan.stage_bytes;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[buf], (uint32_t)(ntc * rpt + n_cs) * kRowBytes);
+        bulk_load(st, p.q + (long long)t0 * p.Hq * kD, ntc * p.Hq * kRowBytes, &full[buf], pol);
+        bulk_load(st + nt * p.Hq * kRowBytes, p.k + (long long)t0 * p.Hkv * kD,
+                  ntc * p.Hkv * kRowBytes, &full[buf], pol);
+        bulk_load(st + nt * (p.Hq + p.Hkv) * kRowBytes, p.v + (long long)t0 * p.Hkv * kD,
+                  ntc * p.Hkv * kRowBytes, &full[buf], pol);
+      }
+      __syncwarp();  // the stage is armed before any cos/sin copy lands
+      if (cs_valid)
+        bulk_load(st + (nt * rpt + lane) * kRowBytes, p.rope + (long long)pos * kD, kRowBytes,
+                  &full[buf], pol);
+    }
+    // Drain: the CTA must not exit with copies in flight (they only matter
+    // when the consumers gave up on a wait; otherwise these return at once).
+    const int issued = it;
+    if (lane == 0) {
+      for (int b = 0; b < plan.n_stages && b < issued; ++b) {
+        const int last = b + ((issued - 1 - b) / plan.n_stages) * plan.n_stages;
+        mbar_wait(&full[b], (last / plan.n_stages) & 1, p.status, 51);
+      }
+    }
+    return;
+  }
+
+  // ---- consumers: in pass kk, warp w's four groups take stage rows
+  // 4 (kk W + w) .. +3 (consecutive rows, usually one token).  A row's place
+  // in the stage does not depend on the stage, so pass 0's geometry is
+  // computed once. ----
+  const int l8 = lane & 7;
+  const int stage_rows = nt * rpt;
+  struct Geom {
+    int i, tl, rr, kind, srow;
+  };
+  auto geom = [&](int kk) {
+    Geom g;
+    g.i = 4 * (kk * W + warp) + (lane >> 3);
+    const int ic = min(g.i, stage_rows - 1);  // padding rows read a real row
+    g.tl = ic / rpt;
+    g.rr = ic - g.tl * rpt;
+    if (g.rr < p.Hq) {
+      g.kind = 0; g.srow = g.tl * p.Hq + g.rr;
+    } else if (g.rr < p.Hq + p.Hkv) {
+      g.kind = 1; g.srow = nt * p.Hq + g.tl * p.Hkv + (g.rr - p.Hq);
+    } else {
+      g.kind = 2; g.srow = nt * (p.Hq + p.Hkv) + g.tl * p.Hkv + (g.rr - p.Hq - p.Hkv);
+    }
+    return g;
+  };
+  const Geom g0 = geom(0);
+
+  int it = 0;
+  for (int ch = blockIdx.x; ch < plan.n_chunks; ch += gridDim.x, ++it) {
+    const int buf = it % plan.n_stages;
+    const bool got = mbar_wait(&full[buf], (it / plan.n_stages) & 1, p.status, 52, abort_flag);
+    if (!__all_sync(0xffffffffu, got)) break;
+    const int t0 = ch * nt;
+    const int rows = min(nt, p.n_tokens - t0) * rpt;
+    const uint8_t* st = stages + (size_t)buf * plan.stage_bytes;
+    const int* mpos = meta + (buf * 2 + 0) * kMaxTokensPerStage;
+    const int* mslot = meta + (buf * 2 + 1) * kMaxTokensPerStage;
+    for (int kk = 0; kk < plan.passes; ++kk) {
+      const Geom g = kk == 0 ? g0 : geom(kk);
+      const bool active = g.i < rows;
+      const float4* r4 = reinterpret_cast<const float4*>(st + g.srow * kRowBytes);
+      float x[2 * kPer];
+      lds_lane8(r4, l8, x);
+      lds_lane8(r4 + kHalf / 4, l8, x + kPer);
+      const int pos = mpos[g.tl];
+      const bool pos_ok = pos >= 0 && pos < p.max_position;
+      const float4* cs4 = reinterpret_cast<const float4*>(st + (stage_rows + g.tl) * kRowBytes);
+      const float4* w4 = reinterpret_cast<const float4*>(wsm + (g.kind == 0 ? 0 : kD)) + l8;
+      finish_row<kQOutBf16>(
+          p, x, active, t0 + g.tl, g.rr, g.kind, pos, pos_ok, mslot[g.tl],
+          [&](float (&w)[2 * kPer]) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float4 v = w4[8 * j];
+              w[4 * j] = v.x; w[4 * j + 1] = v.y; w[4 * j + 2] = v.z; w[4 * j + 3] = v.w;
+            }
+          },
+          !wild[g.kind == 0 ? 0 : 1],
+          [&](float (&cc)[kPer], float (&ss)[kPer]) {
+            lds_lane8(cs4, l8, cc);
+            lds_lane8(cs4 + kHalf / 4, l8, ss);
+          },
+          l8);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[buf]);
+  }
+}
+
+// Picks the stage size and consumer-warp count: among stages of whole tokens
+// up to kStageMaxBytes whose rows split into passes of four rows per warp
+// with no remainder, the one with the most consumer warps (more warps hide
+// the latency of the norm's dependency chain), then the fewest tokens.
+// Without an exact split: 16 warps and a partly idle last pass.
+StagedPlan plan_staged(int n_tokens, int Hq, int Hkv) {
+  const int rpt = Hq + 2 * Hkv;
+  const int token_bytes = (rpt + 1) * kRowBytes;
+  StagedPlan s{};
+  for (int nt = 1; nt <= kMaxTokensPerStage; ++nt) {
+    const int sb = nt * token_bytes;
+    if (sb > kStageMaxBytes && nt > 1) break;
+    const int rows = nt * rpt;
+    if (rows % 4) continue;
+    const int quads = rows / 4;
+    int W = 0;
+    for (int w = kMaxConsumerWarps; w >= kMinConsumerWarps && !W; --w)
+      if (quads % w == 0) W = w;
+    if (W > s.consumer_warps) s = StagedPlan{nt, W, quads / W, 0, sb, 0};
+  }
+  if (!s.tokens_per_stage) {
+    s.tokens_per_stage =
+        std::min(kMaxTokensPerStage, std::max(1, kStageMaxBytes / 2 / token_bytes));
+    s.consumer_warps = 16;
+    s.stage_bytes = s.tokens_per_stage * token_bytes;
+    s.passes = (s.tokens_per_stage * rpt + 63) / 64;
+  }
+  s.n_stages = std::min(kMaxStages, (kStageSmemBudget - kStageHeader) / s.stage_bytes);
+  s.n_chunks = (n_tokens + s.tokens_per_stage - 1) / s.tokens_per_stage;
+  return s;
+}
+
+template <bool kQOutBf16>
+nvattn_status launch_staged(const KvStoreParams& p, const StagedPlan& plan, int sm_count,
+                            cudaStream_t stream) {
+  static unsigned long long attr_set_mask = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
+  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
+    if (cudaFuncSetAttribute(kv_store_staged_kernel<kQOutBf16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kStageSmemBudget) != cudaSuccess)
+      return NVATTN_ERR_CUDA;
+    if (dev < 64) attr_set_mask |= 1ull << dev;
+  }
+  const int grid = std::min(sm_count, plan.n_chunks);
+  const size_t smem = kStageHeader + (size_t)plan.n_stages * plan.stage_bytes;
+  kv_store_staged_kernel<kQOutBf16>
+      <<<grid, (plan.consumer_warps + 1) * 32, smem, stream>>>(p, plan);
+  return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 
 }  // namespace
@@ -249,7 +632,7 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
   p.q = q; p.k = k; p.v = v; p.qw = qw; p.kw = kw;
   p.positions = positions;
   p.slots = slots;
-  p.rope = reinterpret_cast<const float2*>(h->rope_table_dev);
+  p.rope = h->rope_table_dev;
   p.q_out = q_out;
   p.k_cache = k_cache;
   p.v_cache = v_cache;
@@ -257,16 +640,27 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
   const long long rows = (long long)n_tokens * (p.Hq + 2 * p.Hkv);
   if (rows > 0x7fffffffLL - kMaxRowsPerGroup * kGroupsPerBlock) return NVATTN_ERR_INVALID_ARG;
   p.total_rows = (int)rows;
+  const bool bf16_q = q_out_dtype == NVATTN_DTYPE_BF16;
+
+  // Large batches: bulk-copy staging (at least four stages per CTA so the
+  // ring pipelines).  Small batches: the register-row kernel, which spreads
+  // a few thousand rows over every SM.
+  const StagedPlan plan = plan_staged(n_tokens, p.Hq, p.Hkv);
+  if (plan.n_stages >= 3 && plan.n_chunks >= 4 * h->sm_count) {
+    p.rows_per_group = 0;
+    return bf16_q ? launch_staged<true>(p, plan, h->sm_count, stream)
+                  : launch_staged<false>(p, plan, h->sm_count, stream);
+  }
   // Enough groups for about four resident blocks per SM; beyond that each
   // group takes more rows so the per-token loads are shared.
   const long long per_wave = (long long)h->sm_count * 4 * kGroupsPerBlock;
   p.rows_per_group = (int)std::max(1LL, std::min<long long>(kMaxRowsPerGroup, rows / per_wave));
   const long long groups = (rows + p.rows_per_group - 1) / p.rows_per_group;
   const long long blocks = (groups + kGroupsPerBlock - 1) / kGroupsPerBlock;
-  if (q_out_dtype == NVATTN_DTYPE_BF16)
-    kv_store_qk_norm_rope_kernel<true><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+  if (bf16_q)
+    kv_store_rows_kernel<true><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
   else
-    kv_store_qk_norm_rope_kernel<false><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+    kv_store_rows_kernel<false><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 

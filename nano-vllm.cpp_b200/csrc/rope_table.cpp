@@ -40,8 +40,9 @@ void build_rope_table(const nvattn_config& cfg, int n_pos, float* table) {
     corr[1] = std::fmin((float)(n_dims - 1), end);
   }
   const float theta_scale = powf(cfg.rope_theta, -2.0f / n_dims);
+  const int half = n_dims / 2;
   for (int pos = 0; pos < n_pos; ++pos) {
-    float* row = table + (long long)pos * n_dims;
+    float* row = table + (long long)pos * n_dims;  // [cos x half | sin x half]
     float theta_extrap = (float)pos;
     for (int i0 = 0; i0 < n_dims; i0 += 2) {
       const float theta_interp = cfg.rope_freq_scale * theta_extrap;
@@ -52,8 +53,8 @@ void build_rope_table(const nvattn_config& cfg, int n_pos, float* table) {
         theta = theta_interp * (1 - ramp_mix) + theta_extrap * ramp_mix;
         mscale *= 1.0f + 0.1f * logf(1.0f / cfg.rope_freq_scale);
       }
-      row[i0] = cosf(theta) * mscale;
-      row[i0 + 1] = sinf(theta) * mscale;
+      row[i0 / 2] = cosf(theta) * mscale;
+      row[half + i0 / 2] = sinf(theta) * mscale;
       theta_extrap *= theta_scale;
     }
   }

@@ -92,33 +92,40 @@ def test_negative_slot_is_skipped_and_bad_slot_is_reported(cuda):
     assert h.get_error()[0] == nvattn.OK  # cleared after reading
 
 
-def test_in_place_f32_q(cuda):
+# 300 tokens take the register-row kernel, 3000 the bulk-copy staged kernel
+@pytest.mark.parametrize("T", [300, 3000])
+def test_in_place_f32_q(cuda, T):
     import torch
     rng = np.random.default_rng(6)
-    T, Hq, Hkv = 300, 16, 8
+    Hq, Hkv = 16, 8
     q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
     k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
     v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
     w = O.f32_to_bf16(np.ones(128, np.float32))
     pos = np.arange(T, dtype=np.int32)
     slots = np.arange(T, dtype=np.int32)
-    h = handle(Hq, Hkv, 2)
+    nb = (T + 255) // 256
+    h = handle(Hq, Hkv, nb)
     dq = dev(q)
-    kc = torch.zeros((1, 512, Hkv, 128), dtype=torch.int16, device="cuda")
+    kc = torch.zeros((1, nb * 256, Hkv, 128), dtype=torch.int16, device="cuda")
     vc = torch.zeros_like(kc)
     h.kv_store(0, dq, dev(k), dev(v), dev(w), dev(w), dev(pos), dev(slots), dq, kc, vc)
-    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=512)
-    oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos, slots, np.zeros((1, 512, Hkv, 128), np.uint16),
-                              np.zeros((1, 512, Hkv, 128), np.uint16))
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=nb * 256)
+    okc = np.zeros((1, nb * 256, Hkv, 128), np.uint16)
+    ovc = np.zeros_like(okc)
+    oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos, slots, okc, ovc)
+    assert np.array_equal(host_bits(kc), okc)
+    assert np.array_equal(host_bits(vc), ovc)
     assert np.array_equal(dq.cpu().numpy().view(np.uint32), oq.view(np.uint32))
 
 
-def test_rms_mean_on_rounding_midpoint_uses_sequential_sum(cuda):
+@pytest.mark.parametrize("T", [64, 2000])
+def test_rms_mean_on_rounding_midpoint_uses_sequential_sum(cuda, T):
     """Rows whose sum of squares / 128 sits exactly on a float rounding
     midpoint (1 + 2^-24): the kernel's 8-lane tree sum is flagged as
     ambiguous there and redone in the reference's index order."""
     rng = np.random.default_rng(8)
-    T, Hq, Hkv = 64, 16, 8
+    Hq, Hkv = 16, 8
     q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
     k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
     v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
@@ -129,13 +136,49 @@ def test_rms_mean_on_rounding_midpoint_uses_sequential_sum(cuda):
     w = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(128)).astype(np.float32))
     pos = rng.integers(0, 40960, T).astype(np.int32)
     slots = np.arange(T, dtype=np.int32)
-    h = handle(Hq, Hkv, 1)
-    qo, kc, vc = run_store(h, 0, q, k, v, w, w, pos, slots, 256, Hkv)
+    nb = (T + 255) // 256
+    h = handle(Hq, Hkv, nb)
+    qo, kc, vc = run_store(h, 0, q, k, v, w, w, pos, slots, nb * 256, Hkv)
     h.check_device()
-    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=256)
-    okc = np.zeros((1, 256, Hkv, 128), np.uint16)
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=nb * 256)
+    okc = np.zeros((1, nb * 256, Hkv, 128), np.uint16)
     ovc = np.zeros_like(okc)
     oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos, slots, okc, ovc)
     assert np.array_equal(qo.cpu().numpy().view(np.uint32), oq.view(np.uint32))
     assert np.array_equal(host_bits(kc), okc)
     assert np.array_equal(host_bits(vc), ovc)
+
+
+def test_staged_path_reports_bad_position_and_slot(cuda):
+    """The bulk-copy path (thousands of tokens): a token with an out-of-range
+    position stores nothing and is reported; negative slots are skipped."""
+    rng = np.random.default_rng(9)
+    T, Hq, Hkv = 4000, 16, 8
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    w = O.f32_to_bf16(np.ones(128, np.float32))
+    pos = np.arange(T, dtype=np.int32)
+    slots = np.arange(T, dtype=np.int32)
+    slots[17] = -1
+    pos[2345] = 40960
+    nb = (T + 255) // 256
+    h = handle(Hq, Hkv, nb)
+    qo, kc, vc = run_store(h, 0, q, k, v, w, w, pos, slots, nb * 256, Hkv)
+    st, detail = h.get_error()
+    assert st == nvattn.ERR_OUT_OF_RANGE and detail == 40960
+    kb, vb = host_bits(kc), host_bits(vc)
+    assert not kb[0, 2345].any() and not vb[0, 2345].any()
+    assert not kb[0, 17].any() and not vb[0, 17].any()
+    good = np.ones(T, bool)
+    good[[17, 2345]] = False
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=nb * 256)
+    okc = np.zeros((1, nb * 256, Hkv, 128), np.uint16)
+    ovc = np.zeros_like(okc)
+    pos_ok = pos.copy()
+    pos_ok[2345] = 0
+    oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos_ok, slots, okc, ovc)
+    sl = slots[good]
+    assert np.array_equal(kb[0, sl], okc[0, sl]) and np.array_equal(vb[0, sl], ovc[0, sl])
+    got_q = qo.cpu().numpy().view(np.uint32)
+    assert np.array_equal(got_q[good], oq.view(np.uint32)[good])
