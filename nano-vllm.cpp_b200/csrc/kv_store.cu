@@ -9,8 +9,8 @@
 // [8l, 8l+8) and their NEOX partners [64+8l, 64+8l+8), so the rotation needs
 // no shuffle and each lane needs only 8 cos and 8 sin values.  Each half
 // leaves as one 16-byte bf16 store.  The arithmetic runs on packed f32x2
-// instructions where no add follows a product (squares, norm scaling); the
-// rotation, a sum of two products, stays scalar.
+// instructions for the products; the rotation's sums of two products are
+// scalar .rn adds.
 //
 // Two kernels share that row math:
 //  * kv_store_staged_kernel (large batches): one persistent CTA per SM.  A
@@ -33,8 +33,8 @@
 //    rounding boundary.  That case is detected (both ends of the interval are
 //    rounded) and the warp then redoes the sum in ggml's exact index order.
 //  * RoPE: cos/sin come from the host-built table (ggml's float recurrence);
-//    the rotation uses separately rounded products (scalar .rn intrinsics,
-//    which are never contracted into an FMA).
+//    the rotation uses separately rounded products (packed products, scalar
+//    .rn sums, which ptxas does not contract into an FMA).
 //  * Store: ggml_compute_fp32_to_bf16 rounding.  For finite values that is
 //    round-to-nearest-even, i.e. cvt.rn.bf16x2.f32; a row that may hold a NaN
 //    (non-finite input, or norm weights of magnitude >= 2^120) takes ggml's
@@ -113,6 +113,14 @@ __device__ __forceinline__ void load_weights(const uint16_t* wsrc, int l8, LaneW
 // whether the whole row is finite (sum of squares finite).
 __device__ __forceinline__ float rms_scale(const float (&x)[2 * kPer], bool norm_row, float eps,
                                            bool& finite) {
+  if (__all_sync(0xffffffffu, !norm_row)) {
+    // a warp of v rows: only finiteness is needed
+    uint32_t m = 0;
+#pragma unroll
+    for (int e = 0; e < 2 * kPer; ++e) m = max(m, __float_as_uint(x[e]) & 0x7fffffffu);
+    finite = m < 0x7f800000u;
+    return 1.0f;
+  }
   double d[2 * kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
@@ -179,14 +187,25 @@ __device__ __forceinline__ void norm_rope(float (&x)[2 * kPer], float scale,
         fmul2(fmul2(pack2(x[2 * k], x[2 * k + 1]), sc), pack2(w[2 * k], w[2 * k + 1]));
     unpack2(y, x[2 * k], x[2 * k + 1]);
   }
-  // Scalar .rn intrinsics here: ptxas fuses a packed mul.rn.f32x2 with a
-  // following packed add/sub into an FMA (even under -fmad=false), which
-  // would skip the rounding of one product.
+  // Packed products, scalar .rn sums: ptxas fuses a packed mul.rn.f32x2
+  // with a following packed add/sub into an FMA (even under -fmad=false),
+  // which would skip the rounding of one product.
 #pragma unroll
-  for (int e = 0; e < kPer; ++e) {
-    const float x0 = x[e], x1 = x[kPer + e];
-    x[e] = __fsub_rn(__fmul_rn(x0, c[e]), __fmul_rn(x1, sn[e]));
-    x[kPer + e] = __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, c[e]));
+  for (int k = 0; k < kPer / 2; ++k) {
+    const uint64_t x0 = pack2(x[2 * k], x[2 * k + 1]);
+    const uint64_t x1 = pack2(x[kPer + 2 * k], x[kPer + 2 * k + 1]);
+    const uint64_t cc = pack2(c[2 * k], c[2 * k + 1]);
+    const uint64_t ss = pack2(sn[2 * k], sn[2 * k + 1]);
+    float x0c[2], x1s[2], x0s[2], x1c[2];
+    unpack2(fmul2(x0, cc), x0c[0], x0c[1]);
+    unpack2(fmul2(x1, ss), x1s[0], x1s[1]);
+    unpack2(fmul2(x0, ss), x0s[0], x0s[1]);
+    unpack2(fmul2(x1, cc), x1c[0], x1c[1]);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      x[2 * k + j] = __fsub_rn(x0c[j], x1s[j]);
+      x[kPer + 2 * k + j] = __fadd_rn(x0s[j], x1c[j]);
+    }
   }
 }
 

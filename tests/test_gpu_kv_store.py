@@ -182,3 +182,44 @@ def test_staged_path_reports_bad_position_and_slot(cuda):
     assert np.array_equal(kb[0, sl], okc[0, sl]) and np.array_equal(vb[0, sl], ovc[0, sl])
     got_q = qo.cpu().numpy().view(np.uint32)
     assert np.array_equal(got_q[good], oq.view(np.uint32)[good])
+
+
+@pytest.mark.parametrize("T", [64, 3000])
+def test_non_finite_rows(cuda, T):
+    """NaN and inf inputs.  V rows are stored as-is, so their bf16 bits must
+    match ggml's rule exactly (a NaN keeps its payload and is made quiet).
+    A normed row containing inf or NaN becomes (partly) NaN; NaN payloads from
+    arithmetic differ between CPU and GPU, so there only the NaN positions and
+    the finite values are compared."""
+    rng = np.random.default_rng(10)
+    Hq, Hkv = 16, 8
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v[3, 1, 7] = np.uint32(0x7fa00001).view(np.float32)  # signaling NaN payload
+    v[5, 0, 100] = np.inf
+    v[6, 7, 0] = -np.inf
+    k[9, 2, 64] = np.inf
+    k[11, 4, 5] = np.nan
+    q[13, 6, 127] = -np.inf
+    w = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(128)).astype(np.float32))
+    pos = rng.integers(0, 40960, T).astype(np.int32)
+    slots = np.arange(T, dtype=np.int32)
+    nb = (T + 255) // 256
+    h = handle(Hq, Hkv, nb)
+    qo, kc, vc = run_store(h, 0, q, k, v, w, w, pos, slots, nb * 256, Hkv)
+    h.check_device()
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=nb * 256)
+    okc = np.zeros((1, nb * 256, Hkv, 128), np.uint16)
+    ovc = np.zeros_like(okc)
+    oq = O.qk_norm_rope_store(p, 0, q, k, v, w, w, pos, slots, okc, ovc)
+    assert np.array_equal(host_bits(vc), ovc)
+    gk, ok = host_bits(kc), okc
+    gnan = (gk & 0x7fff) > 0x7f80
+    onan = (ok & 0x7fff) > 0x7f80
+    assert np.array_equal(gnan, onan) and gnan[0, 9, 2].any() and gnan[0, 11, 4].all()
+    assert np.array_equal(gk[~gnan], ok[~onan])
+    gq = qo.cpu().numpy()
+    assert np.array_equal(np.isnan(gq), np.isnan(oq)) and np.isnan(gq[13, 6]).any()
+    fin = ~np.isnan(gq)
+    assert np.array_equal(gq[fin].view(np.uint32), oq[fin].view(np.uint32))
