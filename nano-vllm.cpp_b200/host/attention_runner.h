@@ -48,8 +48,10 @@ class AttentionRunner {
   bool PrepareInputs(const std::vector<SequenceView*>& seqs, bool is_prefill,
                      cudaStream_t stream);
 
-  // One layer of the cut graph: q [n_tokens][Hq][d] f32 (overwritten with the
-  // normed, rotated q), k/v [n_tokens][Hkv][d] f32 (graph projections), the
+  // One layer of the cut graph: q [n_tokens][Hq][d] f32 (a decode step
+  // overwrites it with the normed, rotated q; a prefill step writes that q as
+  // bf16 to the runner's own buffer), k/v [n_tokens][Hkv][d] f32 (graph
+  // projections), the
   // layer's q/k norm weights (bf16 [d]), and the BF16 caches (all layers).
   // Writes attention output [n_tokens][Hq][d] f32.
   bool RunAttentionLayer(int layer, float* q, const float* k, const float* v,
