@@ -590,6 +590,11 @@ def main():
     h.check_device("timed region")
 
     # ---- e2e: the same step through the C ABI with pinned host buffers ----
+    # Every step uploads its inputs (q, new k/v, block tables, context
+    # lengths, positions, slots) from pinned host memory and reads its output
+    # back, as a serving loop does; uploads run on one copy stream and
+    # read-backs on another, double-buffered, so step i+1's upload and step
+    # i-1's read-back overlap step i's kernels.
     hq0 = q0.cpu().pin_memory()
     hk = k_new.cpu().pin_memory()
     hv = v_new.cpu().pin_memory()
@@ -597,36 +602,63 @@ def main():
     hctx = ctx.cpu().pin_memory()
     hpos = pos.cpu().pin_memory()
     hslot = slots.cpu().pin_memory()
-    hout = torch.empty((B, hq, D), dtype=torch.float32).pin_memory()
-    dk, dv = torch.empty_like(k_new), torch.empty_like(v_new)
-    dbt, dctx, dpos, dslot = (torch.empty_like(x) for x in (bt, ctx, pos, slots))
     h2d = sum(x.numel() * x.element_size() for x in (hq0, hk, hv, hbt, hctx, hpos, hslot))
-    d2h = hout.numel() * hout.element_size()
+    bufs = []
+    for _ in range(2):
+        bufs.append({
+            "q": torch.empty_like(q), "k": torch.empty_like(k_new), "v": torch.empty_like(v_new),
+            "bt": torch.empty_like(bt), "ctx": torch.empty_like(ctx), "pos": torch.empty_like(pos),
+            "slot": torch.empty_like(slots), "out": torch.empty_like(out),
+            "hout": torch.empty((B, hq, D), dtype=torch.float32).pin_memory(),
+            "up": torch.cuda.Event(), "done": torch.cuda.Event(), "down": torch.cuda.Event(),
+        })
+    d2h = bufs[0]["hout"].numel() * bufs[0]["hout"].element_size()
+    up_stream = torch.cuda.Stream(device=device)
+    down_stream = torch.cuda.Stream(device=device)
 
-    def e2e_step():
-        q.copy_(hq0, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        dbt.copy_(hbt, non_blocking=True)
-        dctx.copy_(hctx, non_blocking=True)
-        dpos.copy_(hpos, non_blocking=True)
-        dslot.copy_(hslot, non_blocking=True)
-        h.kv_store(0, q, dk, dv, w16, w16, dpos, dslot, q, kc16, vc16, stream=stream)
-        h.decode(0, q, kc16, vc16, dbt, dctx, max_ctx, out, stream=stream)
-        hout.copy_(out, non_blocking=True)
+    def e2e_step(i):
+        bb = bufs[i & 1]
+        with torch.cuda.stream(up_stream):
+            if i >= 2:
+                up_stream.wait_event(bb["done"])  # step i-2's kernels are done with bb
+            for name, src in (("q", hq0), ("k", hk), ("v", hv), ("bt", hbt), ("ctx", hctx),
+                              ("pos", hpos), ("slot", hslot)):
+                bb[name].copy_(src, non_blocking=True)
+            bb["up"].record(up_stream)
+        stream.wait_event(bb["up"])
+        if i >= 2:
+            stream.wait_event(bb["down"])  # step i-2's output has been read back
+        h.kv_store(0, bb["q"], bb["k"], bb["v"], w16, w16, bb["pos"], bb["slot"], bb["q"], kc16,
+                   vc16, stream=stream)
+        h.decode(0, bb["q"], kc16, vc16, bb["bt"], bb["ctx"], max_ctx, bb["out"], stream=stream)
+        bb["done"].record(stream)
+        with torch.cuda.stream(down_stream):
+            down_stream.wait_event(bb["done"])
+            bb["hout"].copy_(bb["out"], non_blocking=True)
+            bb["down"].record(down_stream)
 
-    for _ in range(3):
-        e2e_step()
+    def e2e_drain():
+        stream.wait_stream(up_stream)
+        stream.wait_stream(down_stream)
+
+    for i in range(3):
+        e2e_step(i)
+    e2e_drain()
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    up_stream.wait_event(e0)
+    down_stream.wait_event(e0)
+    for i in range(args.steps):
+        e2e_step(i)
+    e2e_drain()
     e1.record(stream)
     barrier()
     e2e_elapsed = e0.elapsed_time(e1) / 1e3
     h.check_device("e2e region")
+    # the read-back holds the last step's attention output
+    assert torch.isfinite(bufs[(args.steps - 1) & 1]["hout"]).all()
 
     times = torch.tensor([elapsed, e2e_elapsed, dec_ms], dtype=torch.float64, device=device)
     if world > 1:
