@@ -27,8 +27,11 @@
 //                  PV0(j), S0(j+1), PV1(j), S1(j+1), ...
 //                S_t = Q_t K^T (M=128, N=128, K=128; A and B K-major, smem)
 //                O_t += P_t V  (A = P from TMEM, B = V MN-major from smem)
-//   warps 2-3    V converters: bf16 -> f16 in place, rows past the context
-//                zeroed (a cache slot past a sequence's end may hold NaN bits).
+//   warps 12-15  V converters (one per SM sub-partition, so the conversion
+//                work does not fall on the sub-partitions of only some softmax
+//                warps): bf16 -> f16 in place, rows past the context zeroed (a
+//                cache slot past a sequence's end may hold NaN bits).
+//   warps 2-3    idle.
 //   warps 4-7    softmax of tile 0; warps 8-11 softmax of tile 1: thread =
 //                query row = TMEM lane.  Causal mask, online softmax in the
 //                log2 domain, P written as f16 into the TMEM columns of its
@@ -51,8 +54,8 @@ constexpr int kD = 128;
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // keys per tile
 constexpr int kSlots = 5;
-constexpr int kThreads = 12 * 32;
-constexpr int kConvThreads = 64;          // warps 2-3
+constexpr int kThreads = 16 * 32;
+constexpr int kConvThreads = 128;         // warps 12-15
 constexpr int kHalfBytes = 128 * 64 * 2;  // one 128-row x 64-column 16-bit box: 16 KiB
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -439,14 +442,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  // 384 threads x 168 registers at launch: warpgroup 0 (TMA, MMA, the two
-  // converter warps) gives back down to 112, the two softmax warpgroups take
-  // 192 each (128*112 + 256*192 = 63488 <= 384*168 = 64512).
+  // 512 threads x 128 registers at launch: warpgroup 0 (TMA, MMA) gives back
+  // down to 88, warpgroup 3 (converters) to 40, the two softmax warpgroups
+  // take 192 each (128*88 + 128*40 + 256*192 = 65536 = 512*128).
   if (warp < 4) {
-    regs_dec<112>();
+    regs_dec<88>();
     if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm, w);
     if (warp == 1 && lane == 0) mma_role(sm, tmem, prm, w);
-    if (warp >= 2) converter_role(sm, prm, w, threadIdx.x - 64);
+  } else if (warp >= 12) {
+    regs_dec<40>();
+    converter_role(sm, prm, w, threadIdx.x - 384);
   } else {
     regs_inc<192>();
     softmax_role(sm, tmem, prm, w, warp, lane);
