@@ -372,7 +372,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 // ---------------------------------------------------------------------------
-// packed fp32 pairs (sm_100 f32x2 arithmetic) and a polynomial exp2
+// packed fp32 pairs (sm_100 f32x2 arithmetic)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {
   uint64_t r;
@@ -406,35 +406,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
   return r;
-}
-
-// 2^x for a pair of x <= 0 on the FMA pipe (relieves the XU port that
-// ex2.approx uses).  x is clamped to -125 (2^-125 stands in for anything
-// smaller; callers use it only where no element is masked to -inf).
-// Method: x = j + f with j = rint(x) (add/subtract 1.5*2^23) and f in
-// [-1/2, 1/2]; 2^f by a degree-4 polynomial fitted to 2^f on [-1/2, 1/2]
-// by weighted least squares towards minimax relative error (max relative
-// error 2.7e-6 in fp32 evaluation); 2^j added into the exponent field
-// (the low bits of the rounding sum, shifted left by 23, equal j << 23).
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  float x0, x1;
-  unpack2(x2, x0, x1);
-  const uint64_t xc = pack2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
-  const uint64_t magic = pack2(kMagic, kMagic);
-  const uint64_t t = fadd2(xc, magic);
-  const uint64_t f = fsub2(xc, fsub2(t, magic));
-  uint64_t p = ffma2(pack2(0.00957008171826601f, 0.00957008171826601f), f,
-                     pack2(0.05591785907745361f, 0.05591785907745361f));
-  p = ffma2(p, f, pack2(0.2402474582195282f, 0.2402474582195282f));
-  p = ffma2(p, f, pack2(0.6931217908859253f, 0.6931217908859253f));
-  p = ffma2(p, f, pack2(0.9999992847442627f, 0.9999992847442627f));
-  float t0, t1, p0, p1;
-  unpack2(t, t0, t1);
-  unpack2(p, p0, p1);
-  const float r0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  const float r1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-  return pack2(r0, r1);
 }
 
 }  // namespace nvattn

@@ -42,8 +42,6 @@
 // implies PV(j) is done (its O may then be rescaled).
 // TMEM columns: tile t uses [256t, 256t+128) for S/P and [256t+128, 256t+256)
 // for O.
-#include <type_traits>
-
 #include "common.cuh"
 #include "internal.h"
 
@@ -290,40 +288,27 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
       rescale = j > 0;
       m_used = m_new;
     }
-    // p = 2^(s*sc - m) in f32 pairs, stored as f16.  Tiles with no masked key
-    // send one pair in four to the FMA-pipe polynomial, the rest to
-    // ex2.approx (XU).
+    // p = 2^(s*sc - m) in f32 pairs (ex2.approx on the XU port), stored as
+    // f16.  An FMA-pipe polynomial for a share of the pairs was measured
+    // slower: the softmax is issue-bound, and the polynomial costs about six
+    // issue slots per element against one.
     const uint64_t nm2 = pack2(-m_used, -m_used);
     uint64_t sum2 = pack2(0.0f, 0.0f);
-    auto chunk = [&](int c, auto poly) {  // 32 keys -> 16 packed columns
-      constexpr bool kPoly = decltype(poly)::value;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 packed columns
       uint32_t ph[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c * 32 + 2 * i]),
                                         __uint_as_float(sr[c * 32 + 2 * i + 1])),
                                   sc2, nm2);
-        uint64_t p2;
-        if (kPoly && (i & 3) == 3) {
-          p2 = exp2_poly2(x2);
-        } else {
-          float x0, x1;
-          unpack2(x2, x0, x1);
-          p2 = pack2(fast_exp2(x0), fast_exp2(x1));
-        }
-        sum2 = fadd2(sum2, p2);
-        float p0, p1;
-        unpack2(p2, p0, p1);
+        float x0, x1;
+        unpack2(x2, x0, x1);
+        const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+        sum2 = fadd2(sum2, pack2(p0, p1));
         ph[i] = cvt_f16x2(p0, p1);
       }
       tmem_st16(s_col + c * 16, ph);
-    };
-    if (masked) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) chunk(c, std::false_type{});
-    } else {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) chunk(c, std::true_type{});
     }
     float s0, s1;
     unpack2(sum2, s0, s1);
