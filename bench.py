@@ -200,7 +200,123 @@ def kv_store_roofline(T, hq, hkv, ms, q_out_bytes):
     gbs = T * per_tok / (ms / 1e3) / 1e9
     return {"bound": "hbm", "kernel": "kv_store_qk_norm_rope", "tokens": T, "ms": ms,
             "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
-            "peak_source": kind, "bytes_per_token": per_tok}
+            "peak_source": kind, "bytes_per_token": per_tok, "frac_of_8tbs": gbs / 8000.0}
+
+
+def bench_decode_small(args, world, rank, device):
+    """Small decode batch: 4 sequences of 37, 256, 513 and 1000 tokens (the new
+    token included), Qwen3-0.6B attention heads (16 q / 8 kv), 64 physical
+    blocks of a permuted pool, kv-head sharded.  Far too small to approach the
+    HBM roofline (7.4 MB of K/V); reports the step's device time (fused store +
+    decode) and the decode's GB/s.  On one GPU it also times, on the host
+    cores, the oracle's paged decode in the reference's dtype chain and the
+    reference's own decode algorithm (gather every history, append the new
+    rows, masked attention over the concatenation) on the same inputs."""
+    import torch
+    import nvattn
+    Hq, Hkv, B = 16, 8, 4
+    hq, hkv = Hq // world, Hkv // world
+    lens = np.array([37, 256, 513, 1000], np.int64)
+    num_blocks = 64
+    rng = np.random.default_rng(SEED + 4)
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    need = (lens + BS - 1) // BS
+    bt_np = np.full((B, int(need.max())), -1, np.int32)
+    off = 0
+    for s_ in range(B):
+        bt_np[s_, :need[s_]] = perm[off:off + need[s_]]
+        off += int(need[s_])
+    cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
+                              max_seqs=B, max_context=int(lens.max()), device=device.index)
+    h = nvattn.Handle(cfg)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4000 + rank)
+    n_slots = num_blocks * BS
+    kc = torch.randn((1, n_slots, hkv, D), generator=gen, device=device).to(torch.bfloat16)
+    vc = torch.randn((1, n_slots, hkv, D), generator=gen, device=device).to(torch.bfloat16)
+    cl, pos_np, slot_np = nvattn.plan_decode(lens, bt_np)
+    bt, ctx = torch.from_numpy(bt_np).to(device), torch.from_numpy(cl).to(device)
+    pos, slots = torch.from_numpy(pos_np).to(device), torch.from_numpy(slot_np).to(device)
+    q0 = torch.randn((B, hq, D), generator=gen, device=device)
+    kn = torch.randn((B, hkv, D), generator=gen, device=device)
+    vn = torch.randn((B, hkv, D), generator=gen, device=device)
+    w16 = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16).view(
+        torch.int16)
+    q, out = torch.empty_like(q0), torch.empty((B, hq, D), device=device)
+    kc16, vc16 = kc.view(torch.int16), vc.view(torch.int16)
+    stream = torch.cuda.current_stream(device)
+    evs = []
+
+    def step():
+        z, a, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        z.record(stream)
+        q.copy_(q0)
+        h.kv_store(0, q, kn, vn, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
+        a.record(stream)
+        h.decode(0, q, kc16, vc16, bt, ctx, int(lens.max()), out, stream=stream)
+        b.record(stream)
+        evs.append((z, a, b))
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize(device)
+    h.check_device("decode_small warmup")
+    evs.clear()
+    steps = 50
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize(device)
+    h.check_device("decode_small")
+    t = torch.tensor([sum(z.elapsed_time(b) for z, _, b in evs) / steps,
+                      sum(a.elapsed_time(b) for _, a, b in evs) / steps],
+                     dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, dec_ms = t.tolist()
+    hbm_peak, _, kind = peaks()
+    alg = int(lens.sum()) * hkv * D * 2 * 2 + B * hq * D * 4 * 2 + int(need.sum()) * 4 + B * 4
+    gbs = alg / (dec_ms / 1e3) / 1e9
+    res = {"workload": "decode_qwen3_0p6b_attn_4seq_len37-1000", "q_heads": Hq, "kv_heads": Hkv,
+           "lens": lens.tolist(), "steps": steps, "step_us": step_ms * 1e3,
+           "decode_us": dec_ms * 1e3,
+           "roofline": {"bound": "hbm", "kernel": "paged_decode (main + split combine)",
+                        "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                        "frac": gbs / hbm_peak, "peak_source": kind, "algorithmic_bytes": alg,
+                        "frac_of_8tbs": gbs / 8000.0}}
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        cores = os.cpu_count() or 1
+        # the cache before this step's store: regenerate it with the same seed
+        gen.manual_seed(4000 + rank)
+        kh = torch.randn((1, n_slots, hkv, D), generator=gen, device=device).to(
+            torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16)
+        vh = torch.randn((1, n_slots, hkv, D), generator=gen, device=device).to(
+            torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16)
+        p = O.params(n_q_heads=hq, n_kv_heads=hkv, n_slots=n_slots, n_threads=cores)
+        qh, knh, vnh = q.cpu().numpy(), kn.cpu().numpy(), vn.cpu().numpy()
+        lens32 = lens.astype(np.int32)
+
+        def timed(fn):
+            n, t0 = 0, time.perf_counter()
+            while True:
+                fn()
+                n += 1
+                dt = time.perf_counter() - t0
+                if dt >= 0.5 or n >= 200:
+                    return dt / n
+
+        res["cpu"] = {
+            "cores": cores,
+            "oracle_paged_ggml_us": 1e6 * timed(lambda: O.paged_decode(
+                p, O.MODE_GGML, 0, qh, kh, vh, bt_np, lens32, knh, vnh)),
+            "reference_concat_all_us": 1e6 * timed(lambda: O.concat_decode_ggml(
+                p, 0, qh, kh, vh, bt_np, lens32, knh, vnh)),
+            "note": "host cores; the reference algorithm's gather/concat/mask restated by the "
+                    "oracle (ggml itself is absent)"}
+    h.close()
+    return res
 
 
 def bench_decode_long(args, world, rank, device):
@@ -475,7 +591,8 @@ def main():
                     help="comma list of prefill workloads to time (prefix_hit, chunk) or none")
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--no-decode-long", action="store_true",
-                    help="skip the secondary 32B-shape long-context decode workload")
+                    help="skip the secondary decode workloads (32B-shape long context, "
+                         "4-sequence small batch)")
     ap.add_argument("--only-prefill", action="store_true",
                     help="skip the decode workload (for profiling the prefill kernel)")
     args = ap.parse_args()
@@ -693,6 +810,7 @@ def main():
     torch.cuda.empty_cache()
     prefill_results = run_prefills(args, world, rank, device)
     decode_long = None if args.no_decode_long else bench_decode_long(args, world, rank, device)
+    decode_small = None if args.no_decode_long else bench_decode_small(args, world, rank, device)
 
     if rank == 0:
         hbm_peak, _, peak_kind = peaks()
@@ -727,6 +845,7 @@ def main():
             "clocks": clk,
             "prefill": prefill_results,
             "decode_long": decode_long,
+            "decode_small": decode_small,
             "kv_store": kv_store_roofline(B, hq, hkv, store_ms, q_out_bytes=4),
         }
         if cpu_base is not None:
