@@ -277,41 +277,63 @@ def bench_decode_small(args, world, rank, device):
     # The eager steps above include the gaps while Python issues each call;
     # the same step captured once in a CUDA graph and replayed shows the
     # device time alone (what a C++ caller or a graph-capturing engine sees).
-    graph_us = None
-    try:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            cs = torch.cuda.current_stream(device)
-            q.copy_(q0)
-            h.kv_store(0, q, kn, vn, w16, w16, pos, slots, q, kc16, vc16, stream=cs)
-            h.decode(0, q, kc16, vc16, bt, ctx, int(lens.max()), out, stream=cs)
-        for _ in range(3):
-            g.replay()
-        torch.cuda.synchronize(device)
-        ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        ga.record(stream)
-        for _ in range(steps):
-            g.replay()
-        gb.record(stream)
-        torch.cuda.synchronize(device)
-        h.check_device("decode_small graph")
-        graph_us = ga.elapsed_time(gb) / steps * 1e3
-        del g
-    except Exception as e:  # noqa: BLE001 -- reported, not fatal
-        graph_us = f"capture failed: {e}"
-    gt = torch.tensor([graph_us if isinstance(graph_us, float) else -1.0],
+    # A decode engine that keeps its sequence lengths on the device can also
+    # capture the step's planning: the second graph derives positions, slots
+    # and context lengths with the device planner before the store and decode.
+    d_lens = torch.from_numpy(lens).to(device)
+    ctx_p, pos_p, slots_p = (torch.empty(B, dtype=torch.int32, device=device) for _ in range(3))
+
+    def plain_body(cs):
+        q.copy_(q0)
+        h.kv_store(0, q, kn, vn, w16, w16, pos, slots, q, kc16, vc16, stream=cs)
+        h.decode(0, q, kc16, vc16, bt, ctx, int(lens.max()), out, stream=cs)
+
+    def planned_body(cs):
+        h.plan_decode(d_lens, bt, ctx_p, pos_p, slots_p, stream=cs)
+        q.copy_(q0)
+        h.kv_store(0, q, kn, vn, w16, w16, pos_p, slots_p, q, kc16, vc16, stream=cs)
+        h.decode(0, q, kc16, vc16, bt, ctx_p, int(lens.max()), out, stream=cs)
+
+    def graph_us_of(body):
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                body(torch.cuda.current_stream(device))
+            for _ in range(3):
+                g.replay()
+            torch.cuda.synchronize(device)
+            ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ga.record(stream)
+            for _ in range(steps):
+                g.replay()
+            gb.record(stream)
+            torch.cuda.synchronize(device)
+            h.check_device("decode_small graph")
+            del g
+            return ga.elapsed_time(gb) / steps * 1e3
+        except Exception as e:  # noqa: BLE001 -- reported, not fatal
+            return f"capture failed: {e}"
+
+    planned_body(stream)
+    torch.cuda.synchronize(device)
+    h.check_device("decode_small planned warmup")
+    graph_us, planned_us = graph_us_of(plain_body), graph_us_of(planned_body)
+    gt = torch.tensor([v if isinstance(v, float) else -1.0 for v in (graph_us, planned_us)],
                       dtype=torch.float64, device=device)
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(gt, op=dist.ReduceOp.MAX)
     if isinstance(graph_us, float):
-        graph_us = gt.item()
+        graph_us = gt[0].item()
+    if isinstance(planned_us, float):
+        planned_us = gt[1].item()
     hbm_peak, _, kind = peaks()
     alg = int(lens.sum()) * hkv * D * 2 * 2 + B * hq * D * 4 * 2 + int(need.sum()) * 4 + B * 4
     gbs = alg / (dec_ms / 1e3) / 1e9
     res = {"workload": "decode_qwen3_0p6b_attn_4seq_len37-1000", "q_heads": Hq, "kv_heads": Hkv,
            "lens": lens.tolist(), "steps": steps, "step_us": step_ms * 1e3,
-           "graph_step_us": graph_us, "decode_us": dec_ms * 1e3,
+           "graph_step_us": graph_us, "graph_step_device_planned_us": planned_us,
+           "decode_us": dec_ms * 1e3,
            "roofline": {"bound": "hbm", "kernel": "paged_decode (main + split combine)",
                         "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
                         "frac": gbs / hbm_peak, "peak_source": kind, "algorithmic_bytes": alg,

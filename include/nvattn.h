@@ -146,6 +146,32 @@ NVATTN_API nvattn_status nvattn_plan_decode(int n_seqs, const int64_t* seq_lens,
                                  int block_size, int32_t* context_lens,
                                  int32_t* positions, int32_t* slot_mapping);
 
+/* Device-side planners: the same outputs as nvattn_plan_prefill /
+ * nvattn_plan_decode (bit for bit), computed by kernels on `stream` from
+ * device-resident sequence lengths and block tables, for an engine that keeps
+ * its block tables on the GPU (the per-step H2D copy of positions, slots and
+ * tables then disappears).  Replaces the same PrepareInputs derivation
+ * (model_runner.cpp:138-186) over BlockManager's tables
+ * (block_manager.cpp:96-184; Sequence, sequence.h:63-88); block_size comes
+ * from the handle.  Invalid input (seq_lens[s] <= 0, num_cached[s] outside
+ * [0, seq_lens[s]], more tokens than max_tokens, a position beyond
+ * max_blocks) is recorded as NVATTN_ERR_INVALID_ARG, a negative block id for
+ * a position as NVATTN_ERR_OUT_OF_RANGE, each with detail = the sequence
+ * index, and read with nvattn_get_error; the outputs are then unspecified.
+ * The caller knows the token count on the host (the scheduler's sum of
+ * seq_lens - num_cached, with 1 for a fully cached prompt), as the attention
+ * calls need it; max_tokens bounds the positions/slot_mapping arrays. */
+NVATTN_API nvattn_status nvattn_plan_prefill_device(
+    nvattn_handle* h, int n_seqs, const int64_t* seq_lens_dev, const int64_t* num_cached_dev,
+    const int32_t* block_tables_dev, int max_blocks, int max_tokens, int32_t* cu_q_lens_dev,
+    int32_t* q_starts_dev, int32_t* context_lens_dev, int32_t* positions_dev,
+    int32_t* slot_mapping_dev, nvattn_stream_t stream);
+
+NVATTN_API nvattn_status nvattn_plan_decode_device(
+    nvattn_handle* h, int n_seqs, const int64_t* seq_lens_dev, const int32_t* block_tables_dev,
+    int max_blocks, int32_t* context_lens_dev, int32_t* positions_dev,
+    int32_t* slot_mapping_dev, nvattn_stream_t stream);
+
 /* ---- device kernels ----------------------------------------------------- */
 
 /* Fused per-head q/k RMSNorm (weight = q_norm / k_norm), NEOX RoPE at

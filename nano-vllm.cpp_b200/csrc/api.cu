@@ -284,6 +284,45 @@ nvattn_status nvattn_plan_decode(int n_seqs, const int64_t* seq_lens, const int3
   return NVATTN_OK;
 }
 
+nvattn_status nvattn_plan_prefill_device(nvattn_handle* h, int n_seqs,
+                                         const int64_t* seq_lens_dev,
+                                         const int64_t* num_cached_dev,
+                                         const int32_t* block_tables_dev, int max_blocks,
+                                         int max_tokens, int32_t* cu_q_lens_dev,
+                                         int32_t* q_starts_dev, int32_t* context_lens_dev,
+                                         int32_t* positions_dev, int32_t* slot_mapping_dev,
+                                         nvattn_stream_t stream) {
+  if (h == nullptr || n_seqs < 0 || max_blocks <= 0 || max_tokens < 0)
+    return NVATTN_ERR_INVALID_ARG;
+  if (cu_q_lens_dev == nullptr) return NVATTN_ERR_INVALID_ARG;
+  if (n_seqs > 0 && (!seq_lens_dev || !num_cached_dev || !block_tables_dev || !q_starts_dev ||
+                     !context_lens_dev || !positions_dev || !slot_mapping_dev))
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  return nvattn::launch_plan_prefill(h, n_seqs, seq_lens_dev, num_cached_dev, block_tables_dev,
+                                     max_blocks, max_tokens, cu_q_lens_dev, q_starts_dev,
+                                     context_lens_dev, positions_dev, slot_mapping_dev,
+                                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+nvattn_status nvattn_plan_decode_device(nvattn_handle* h, int n_seqs,
+                                        const int64_t* seq_lens_dev,
+                                        const int32_t* block_tables_dev, int max_blocks,
+                                        int32_t* context_lens_dev, int32_t* positions_dev,
+                                        int32_t* slot_mapping_dev, nvattn_stream_t stream) {
+  if (h == nullptr || n_seqs < 0 || max_blocks <= 0) return NVATTN_ERR_INVALID_ARG;
+  if (n_seqs == 0) return NVATTN_OK;
+  if (!seq_lens_dev || !block_tables_dev || !context_lens_dev || !positions_dev ||
+      !slot_mapping_dev)
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  return nvattn::launch_plan_decode(h, n_seqs, seq_lens_dev, block_tables_dev, max_blocks,
+                                    context_lens_dev, positions_dev, slot_mapping_dev,
+                                    reinterpret_cast<cudaStream_t>(stream));
+}
+
 nvattn_status nvattn_kv_store_qk_norm_rope(nvattn_handle* h, int layer, int n_tokens,
                                            const float* q_dev, const float* k_dev,
                                            const float* v_dev, const uint16_t* q_norm_w_dev,

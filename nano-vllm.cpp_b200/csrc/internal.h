@@ -75,6 +75,19 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
                                    const uint16_t* v_cache, float* out,
                                    cudaStream_t stream);
 
+// Device-side planners (plan.cu): the host planners' outputs from
+// device-resident sequence lengths and block tables, errors to status_dev.
+nvattn_status launch_plan_prefill(nvattn_handle* h, int n_seqs, const int64_t* seq_lens,
+                                  const int64_t* num_cached, const int32_t* block_tables,
+                                  int max_blocks, int max_tokens, int32_t* cu_q,
+                                  int32_t* q_starts, int32_t* context_lens, int32_t* positions,
+                                  int32_t* slot_mapping, cudaStream_t stream);
+
+nvattn_status launch_plan_decode(nvattn_handle* h, int n_seqs, const int64_t* seq_lens,
+                                 const int32_t* block_tables, int max_blocks,
+                                 int32_t* context_lens, int32_t* positions,
+                                 int32_t* slot_mapping, cudaStream_t stream);
+
 // Host RoPE table: ggml's rope cache recurrence for positions [0, n_pos).
 void build_rope_table(const nvattn_config& cfg, int n_pos, float* table);
 

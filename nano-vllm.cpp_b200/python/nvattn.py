@@ -29,7 +29,7 @@ EXPORTED = [
     "nvattn_config_init_qwen3", "nvattn_create", "nvattn_destroy", "nvattn_status_string",
     "nvattn_version", "nvattn_get_error", "nvattn_plan_prefill", "nvattn_plan_decode",
     "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
-    "nvattn_paged_decode_noalloc",
+    "nvattn_paged_decode_noalloc", "nvattn_plan_prefill_device", "nvattn_plan_decode_device",
 ]
 ERR_SCRATCH_LIMIT = 7
 
@@ -89,6 +89,9 @@ def lib():
         L.nvattn_plan_prefill.argtypes = [_i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp,
                                           _vp, _vp]
         L.nvattn_plan_decode.argtypes = [_i32, _vp, _vp, _i32, _i32, _vp, _vp, _vp]
+        L.nvattn_plan_prefill_device.argtypes = [_vp, _i32, _vp, _vp, _vp, _i32, _i32, _vp, _vp,
+                                                 _vp, _vp, _vp, _vp]
+        L.nvattn_plan_decode_device.argtypes = [_vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp]
         L.nvattn_kv_store_qk_norm_rope.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                                                    _vp, _vp, _i32, _vp, _vp, _vp]
         L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
@@ -172,6 +175,30 @@ class Handle:
         st, d = self.get_error()
         if st != OK:
             raise NvattnError(st, f"{what} (detail {d})")
+
+    def plan_prefill(self, seq_lens, num_cached, block_tables, max_tokens, cu_q, q_starts,
+                     context_lens, positions, slot_mapping, stream=None, check=True):
+        """nvattn_plan_prefill_device: the host planner's outputs computed on the
+        device from device tensors (seq_lens/num_cached int64, block_tables
+        int32 [n_seqs][max_blocks]); per-sequence errors land in get_error()."""
+        st = lib().nvattn_plan_prefill_device(
+            self._h, seq_lens.shape[0], _ptr(seq_lens), _ptr(num_cached), _ptr(block_tables),
+            block_tables.shape[1], int(max_tokens), _ptr(cu_q), _ptr(q_starts),
+            _ptr(context_lens), _ptr(positions), _ptr(slot_mapping), _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_plan_prefill_device")
+        return st
+
+    def plan_decode(self, seq_lens, block_tables, context_lens, positions, slot_mapping,
+                    stream=None, check=True):
+        """nvattn_plan_decode_device: one decode token per sequence, on the device."""
+        st = lib().nvattn_plan_decode_device(
+            self._h, seq_lens.shape[0], _ptr(seq_lens), _ptr(block_tables),
+            block_tables.shape[1], _ptr(context_lens), _ptr(positions), _ptr(slot_mapping),
+            _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_plan_decode_device")
+        return st
 
     def kv_store(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, q_out, k_cache,
                  v_cache, stream=None, check=True):
