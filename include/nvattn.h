@@ -172,6 +172,36 @@ NVATTN_API nvattn_status nvattn_plan_decode_device(
     int max_blocks, int32_t* context_lens_dev, int32_t* positions_dev,
     int32_t* slot_mapping_dev, nvattn_stream_t stream);
 
+/* ---- token sampling ------------------------------------------------------ */
+
+/* Next-token sampling for a batch: ModelRunner::Sample
+ * (model_runner.cpp:417-489) on the device.  Row s of the logits is n_vocab
+ * f32 values at logits_dev + s*row_stride (elements).  Per row:
+ *  - penalties_dev[s] > 1: each occurrence of an id t in [0, n_vocab) among
+ *    the row's history ids -- history_dev[history_offsets_dev[s] ..
+ *    history_offsets_dev[s+1]), the prompt then the completion, int32 ids,
+ *    int64 offsets -- applies v = v < 0 ? v*p : v/p to logit t once more,
+ *    bit for bit as the reference does; other ids are skipped.  Both
+ *    history pointers may be NULL: no penalty.
+ *  - temperatures_dev[s] < 1e-6: the first index of the maximum (bit-exact);
+ *  - otherwise: inverse-CDF sampling of softmax(x/t) with the draw
+ *    uniforms_dev[s] in [0,1) -- the generate_canonical<float> value that
+ *    the reference's std::uniform_real_distribution<float>(0, sum) scales by
+ *    the sum.  The token is the first whose running probability sum reaches
+ *    u * sum, n_vocab-1 if none does (a NaN or infinite logit, as in the
+ *    reference).  Probabilities are within a few ulp of the reference's.
+ * tokens_dev[s] receives the token.  A draw outside [0,1) or unusable
+ * history offsets are recorded as NVATTN_ERR_INVALID_ARG (detail = s).
+ * n_vocab <= 2,097,152.  The first call for a vocabulary size allocates the
+ * handle's sampler workspace (max_seqs * n_vocab * 4 bytes of counts, zero
+ * between calls) and cannot be captured (NVATTN_ERR_UNSUPPORTED while the
+ * stream captures); later calls are capturable. */
+NVATTN_API nvattn_status nvattn_sample(
+    nvattn_handle* h, int n_seqs, int n_vocab, const float* logits_dev, int64_t row_stride,
+    const float* temperatures_dev, const float* penalties_dev, const int32_t* history_dev,
+    const int64_t* history_offsets_dev, const float* uniforms_dev, int32_t* tokens_dev,
+    nvattn_stream_t stream);
+
 /* ---- device kernels ----------------------------------------------------- */
 
 /* Fused per-head q/k RMSNorm (weight = q_norm / k_norm), NEOX RoPE at

@@ -211,6 +211,10 @@ nvattn_status nvattn_destroy(nvattn_handle* h) {
   if (h->status_dev) cudaFree(h->status_dev);
   if (h->ws_o) cudaFree(h->ws_o);
   if (h->ws_ml) cudaFree(h->ws_ml);
+  if (h->samp_cnt) cudaFree(h->samp_cnt);
+  if (h->samp_bits) cudaFree(h->samp_bits);
+  if (h->samp_part) cudaFree(h->samp_part);
+  if (h->samp_ticket) cudaFree(h->samp_ticket);
   delete h;
   return NVATTN_OK;
 }
@@ -321,6 +325,59 @@ nvattn_status nvattn_plan_decode_device(nvattn_handle* h, int n_seqs,
   return nvattn::launch_plan_decode(h, n_seqs, seq_lens_dev, block_tables_dev, max_blocks,
                                     context_lens_dev, positions_dev, slot_mapping_dev,
                                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+nvattn_status nvattn_sample(nvattn_handle* h, int n_seqs, int n_vocab, const float* logits_dev,
+                            int64_t row_stride, const float* temperatures_dev,
+                            const float* penalties_dev, const int32_t* history_dev,
+                            const int64_t* history_offsets_dev, const float* uniforms_dev,
+                            int32_t* tokens_dev, nvattn_stream_t stream) {
+  if (h == nullptr || n_seqs < 0 || n_seqs > h->cfg.max_seqs || n_vocab <= 0 ||
+      row_stride < n_vocab)
+    return NVATTN_ERR_INVALID_ARG;
+  if (n_vocab > nvattn::sample_max_vocab()) return NVATTN_ERR_UNSUPPORTED;
+  if (n_seqs == 0) return NVATTN_OK;
+  if (!logits_dev || !temperatures_dev || !penalties_dev || !uniforms_dev || !tokens_dev ||
+      (history_dev == nullptr) != (history_offsets_dev == nullptr))
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (n_vocab > h->samp_cap) {
+    // Workspace for this vocabulary: allocation cannot happen inside a graph
+    // capture, so the first call per vocabulary size must run eagerly.
+    cudaStreamCaptureStatus cap_status = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap_status) != cudaSuccess) return NVATTN_ERR_CUDA;
+    if (cap_status != cudaStreamCaptureStatusNone) return NVATTN_ERR_UNSUPPORTED;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return NVATTN_ERR_CUDA;
+    if (h->samp_cnt) cudaFree(h->samp_cnt);
+    if (h->samp_bits) cudaFree(h->samp_bits);
+    if (h->samp_part) cudaFree(h->samp_part);
+    if (h->samp_ticket) cudaFree(h->samp_ticket);
+    h->samp_cnt = h->samp_bits = nullptr;
+    h->samp_part = nullptr;
+    h->samp_ticket = nullptr;
+    h->samp_cap = 0;
+    const long long cap = ((long long)n_vocab + 31) / 32 * 32;
+    const size_t seqs = (size_t)h->cfg.max_seqs;
+    const size_t cnt_b = seqs * cap * 4, bits_b = seqs * (cap / 32) * 4,
+                 part_b = seqs * nvattn::sample_partial_bytes(), tick_b = seqs * 4;
+    if (cudaMalloc(&h->samp_cnt, cnt_b) != cudaSuccess ||
+        cudaMalloc(&h->samp_bits, bits_b) != cudaSuccess ||
+        cudaMalloc(&h->samp_part, part_b) != cudaSuccess ||
+        cudaMalloc(&h->samp_ticket, tick_b) != cudaSuccess) {
+      cudaGetLastError();
+      return NVATTN_ERR_NO_MEMORY;
+    }
+    if (cudaMemsetAsync(h->samp_cnt, 0, cnt_b, st) != cudaSuccess ||
+        cudaMemsetAsync(h->samp_bits, 0, bits_b, st) != cudaSuccess ||
+        cudaMemsetAsync(h->samp_ticket, 0, tick_b, st) != cudaSuccess)
+      return NVATTN_ERR_CUDA;
+    h->samp_cap = cap;
+  }
+  return nvattn::launch_sample(h, n_seqs, n_vocab, logits_dev, row_stride, temperatures_dev,
+                               penalties_dev, history_dev, history_offsets_dev, uniforms_dev,
+                               tokens_dev, st);
 }
 
 nvattn_status nvattn_kv_store_qk_norm_rope(nvattn_handle* h, int layer, int n_tokens,

@@ -40,6 +40,14 @@ struct nvattn_handle {
   int max_splits = 0;
 
   std::vector<NvattnTensorMapEntry> maps;
+
+  // sampler workspace (sample.cu), allocated by the first nvattn_sample call
+  // for a vocabulary size; all zero between calls except the partials
+  uint32_t* samp_cnt = nullptr;     // [max_seqs][samp_cap] history id counts
+  uint32_t* samp_bits = nullptr;    // [max_seqs][samp_cap/32] history id bitmap
+  void* samp_part = nullptr;        // [max_seqs][512] chunk partials
+  unsigned* samp_ticket = nullptr;  // [max_seqs] finished chunks
+  long long samp_cap = 0;           // vocabulary capacity (multiple of 32)
 };
 
 namespace nvattn {
@@ -87,6 +95,14 @@ nvattn_status launch_plan_decode(nvattn_handle* h, int n_seqs, const int64_t* se
                                  const int32_t* block_tables, int max_blocks,
                                  int32_t* context_lens, int32_t* positions,
                                  int32_t* slot_mapping, cudaStream_t stream);
+
+// Token sampler (sample.cu).
+int sample_max_vocab();
+size_t sample_partial_bytes();  // per sequence
+nvattn_status launch_sample(nvattn_handle* h, int n_seqs, int n_vocab, const float* logits,
+                            long long row_stride, const float* temps, const float* pens,
+                            const int32_t* hist, const int64_t* hist_off, const float* uniforms,
+                            int32_t* tokens, cudaStream_t stream);
 
 // Host RoPE table: ggml's rope cache recurrence for positions [0, n_pos).
 void build_rope_table(const nvattn_config& cfg, int n_pos, float* table);

@@ -30,6 +30,7 @@ EXPORTED = [
     "nvattn_version", "nvattn_get_error", "nvattn_plan_prefill", "nvattn_plan_decode",
     "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
     "nvattn_paged_decode_noalloc", "nvattn_plan_prefill_device", "nvattn_plan_decode_device",
+    "nvattn_sample",
 ]
 ERR_SCRATCH_LIMIT = 7
 
@@ -92,6 +93,7 @@ def lib():
         L.nvattn_plan_prefill_device.argtypes = [_vp, _i32, _vp, _vp, _vp, _i32, _i32, _vp, _vp,
                                                  _vp, _vp, _vp, _vp]
         L.nvattn_plan_decode_device.argtypes = [_vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp]
+        L.nvattn_sample.argtypes = [_vp, _i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
         L.nvattn_kv_store_qk_norm_rope.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                                                    _vp, _vp, _i32, _vp, _vp, _vp]
         L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
@@ -198,6 +200,21 @@ class Handle:
             _stream_ptr(stream))
         if check:
             _check(st, "nvattn_plan_decode_device")
+        return st
+
+    def sample(self, logits, temperatures, penalties, uniforms, tokens, history=None,
+               history_offsets=None, stream=None, check=True):
+        """nvattn_sample: one token per logits row ([n_seqs][row_stride] f32,
+        the first n_vocab = logits.shape[1] columns used) into tokens (int32);
+        history (int32 ids) / history_offsets (int64, n_seqs+1) feed the
+        repetition penalty."""
+        n, V = logits.shape
+        st = lib().nvattn_sample(
+            self._h, n, V, _ptr(logits), logits.stride(0), _ptr(temperatures), _ptr(penalties),
+            _ptr(history), _ptr(history_offsets), _ptr(uniforms), _ptr(tokens),
+            _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_sample")
         return st
 
     def kv_store(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, q_out, k_cache,

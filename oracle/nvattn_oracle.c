@@ -659,3 +659,79 @@ void orc_concat_decode_ggml(const orc_params* p, int layer, int n_seqs,
   free(kf);
   free(vf);
 }
+
+/* ------------------------------------------------------------------------ */
+/* token sampling (model_runner.cpp:417-489)                                */
+/* ------------------------------------------------------------------------ */
+
+static void penalize_row(int n_vocab, float* row, float penalty, const int32_t* hist,
+                         int64_t n_hist) {
+  for (int64_t j = 0; j < n_hist; ++j) {
+    const int32_t tok = hist[j];
+    if (tok < 0 || tok >= n_vocab) continue; /* size_t id >= n_vocab is skipped */
+    float* v = &row[tok];
+    *v = *v < 0.0f ? *v * penalty : *v / penalty;
+  }
+}
+
+void orc_penalize_rows(int n_seqs, int n_vocab, const float* logits, int64_t row_stride,
+                       const float* penalties, const int32_t* history,
+                       const int64_t* history_offsets, float* out) {
+  for (int s = 0; s < n_seqs; ++s) {
+    float* row = out + (int64_t)s * n_vocab;
+    memcpy(row, logits + (int64_t)s * row_stride, sizeof(float) * (size_t)n_vocab);
+    if (penalties[s] > 1.0f && history != NULL && history_offsets != NULL)
+      penalize_row(n_vocab, row, penalties[s], history + history_offsets[s],
+                   history_offsets[s + 1] - history_offsets[s]);
+  }
+}
+
+void orc_sample(int n_seqs, int n_vocab, const float* logits, int64_t row_stride,
+                const float* temperatures, const float* penalties, const int32_t* history,
+                const int64_t* history_offsets, const float* uniforms, int32_t* tokens) {
+  float* row = (float*)malloc(sizeof(float) * (size_t)n_vocab);
+  float* probs = (float*)malloc(sizeof(float) * (size_t)n_vocab);
+  for (int s = 0; s < n_seqs; ++s) {
+    /* one row: offsets shifted so that [0], [1] bound sequence s's ids */
+    orc_penalize_rows(1, n_vocab, logits + (int64_t)s * row_stride, row_stride, penalties + s,
+                      history, history_offsets ? history_offsets + s : NULL, row);
+    const float temp = temperatures[s];
+    if (temp < 1e-6f) {
+      int best = 0;
+      float best_val = row[0];
+      for (int i = 1; i < n_vocab; ++i)
+        if (row[i] > best_val) {
+          best_val = row[i];
+          best = i;
+        }
+      tokens[s] = best;
+      continue;
+    }
+    float max_logit = row[0];
+    for (int i = 1; i < n_vocab; ++i)
+      if (row[i] > max_logit) max_logit = row[i];
+    float sum = 0.0f;
+    for (int i = 0; i < n_vocab; ++i) {
+      probs[i] = expf((row[i] - max_logit) / temp);
+      sum += probs[i];
+    }
+    const float r = uniforms[s] * (sum - 0.0f) + 0.0f;
+    float cumulative = 0.0f;
+    int idx = n_vocab - 1;
+    for (int i = 0; i < n_vocab; ++i) {
+      cumulative += probs[i];
+      if (cumulative >= r) {
+        idx = i;
+        break;
+      }
+    }
+    tokens[s] = idx;
+  }
+  free(row);
+  free(probs);
+}
+
+float orc_canonical_float(uint32_t x) {
+  const float u = (float)x / 4294967296.0f;
+  return u >= 1.0f ? nextafterf(1.0f, 0.0f) : u;
+}

@@ -127,6 +127,29 @@ void orc_concat_decode_ggml(const orc_params* p, int layer, int n_seqs,
                             const int32_t* context_lens, const float* new_k,
                             const float* new_v, float* out);
 
+/* ---- token sampling (ModelRunner::Sample, model_runner.cpp:417-489) ----
+ * Row s of logits (n_vocab f32 at logits + s*row_stride):
+ *  - penalty[s] > 1: every occurrence of a history id t in [0, n_vocab)
+ *    (sequence s's ids at [history_offsets[s], history_offsets[s+1]), prompt
+ *    then completion) applies v = v < 0 ? v*penalty : v/penalty once more to
+ *    a copy of the row (:428-446);
+ *  - temperature < 1e-6: the first index of the maximum by a strict '>' scan
+ *    from index 0 (:448-456);
+ *  - otherwise: m = the same scan's maximum, p_i = expf((x_i - m)/t), S the
+ *    sequential float sum, r = u*S (std::uniform_real_distribution<float>(0, S)
+ *    = S * generate_canonical<float>), and the first i whose sequential float
+ *    prefix sum is >= r, else n_vocab-1 (:457-481).  u = uniforms[s]. */
+void orc_penalize_rows(int n_seqs, int n_vocab, const float* logits, int64_t row_stride,
+                       const float* penalties, const int32_t* history,
+                       const int64_t* history_offsets, float* out);
+void orc_sample(int n_seqs, int n_vocab, const float* logits, int64_t row_stride,
+                const float* temperatures, const float* penalties, const int32_t* history,
+                const int64_t* history_offsets, const float* uniforms, int32_t* tokens);
+
+/* libstdc++'s generate_canonical<float, 24> over one 32-bit mt19937 output:
+ * float(x) / 2^32, and the largest float below 1 when that rounds to 1. */
+float orc_canonical_float(uint32_t x);
+
 #ifdef __cplusplus
 }
 #endif

@@ -154,6 +154,49 @@ def concat_decode_ggml(p, layer, q, k_cache, v_cache, block_tables, context_lens
     return out
 
 
+def _hist_args(history, history_offsets):
+    if history is None:
+        return None, None, None
+    h = np.ascontiguousarray(history, dtype=np.int32)
+    o = np.ascontiguousarray(history_offsets, dtype=np.int64)
+    return h, o, _p(h)
+
+
+def penalize_rows(logits, penalties, history=None, history_offsets=None):
+    """Repetition-penalised copy of each logits row (model_runner.cpp:428-446)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    n, V = x.shape
+    pen = np.ascontiguousarray(penalties, dtype=np.float32)
+    h, o, hp = _hist_args(history, history_offsets)
+    out = np.empty_like(x)
+    lib().orc_penalize_rows(ctypes.c_int(n), ctypes.c_int(V), _p(x), ctypes.c_int64(V), _p(pen),
+                            hp, None if o is None else _p(o), _p(out))
+    return out
+
+
+def sample(logits, temperatures, penalties, uniforms, history=None, history_offsets=None):
+    """ModelRunner::Sample (model_runner.cpp:417-489) with the uniform draws
+    given: the reference's float chain, token per row."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    n, V = x.shape
+    t = np.ascontiguousarray(temperatures, dtype=np.float32)
+    pen = np.ascontiguousarray(penalties, dtype=np.float32)
+    u = np.ascontiguousarray(uniforms, dtype=np.float32)
+    h, o, hp = _hist_args(history, history_offsets)
+    out = np.empty(n, np.int32)
+    lib().orc_sample(ctypes.c_int(n), ctypes.c_int(V), _p(x), ctypes.c_int64(V), _p(t), _p(pen),
+                     hp, None if o is None else _p(o), _p(u), _p(out))
+    return out
+
+
+def canonical_float(x: int) -> float:
+    """generate_canonical<float> of one 32-bit mt19937 output (libstdc++)."""
+    f = lib().orc_canonical_float
+    f.restype = ctypes.c_float
+    f.argtypes = [ctypes.c_uint32]
+    return float(f(x))
+
+
 def err_stats(got: np.ndarray, ref: np.ndarray):
     """(max-abs-err, mean-rel-err = sum|got-ref| / sum|ref|)."""
     got = np.asarray(got, dtype=np.float64)
