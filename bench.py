@@ -458,6 +458,94 @@ def bench_decode_long(args, world, rank, device):
                          "algorithmic_bytes": alg, "frac_of_8tbs": gbs / 8000.0}}
 
 
+def bench_sample(args, world, rank, device):
+    """Token sampling over the headline batch: 256 rows of Qwen3's 151936
+    logits (f32, N(0, 4^2)), temperature 0.8 and repetition penalty 1.2 (the
+    reference's example settings), each sequence's history its decode
+    context length of uniform random ids (1k-32k ids, 2.9 M in all).  Two
+    logits buffers alternate (311 MB > L2).  Reports the call's device time
+    (count + chunk kernels), the same rows greedy without history (the bare
+    logits pass), GB/s of the call's algorithmic bytes, and on one GPU the
+    oracle's restatement of the reference's Sample on a bounded sample of
+    rows, timed on one host core as the reference runs it."""
+    import torch
+    import nvattn
+    V, temp, pen = 151936, 0.8, 1.2
+    lens, _, _ = workload()
+    B = lens.shape[0]
+    rng = np.random.default_rng(SEED + 5)
+    off_np = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    hist_np = rng.integers(0, V, int(off_np[-1])).astype(np.int32)
+    cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=8, n_kv_heads=8, num_blocks=1, max_seqs=B,
+                              max_context=BS, device=device.index)
+    h = nvattn.Handle(cfg)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5000 + rank)
+    xs = [4.0 * torch.randn((B, V), generator=gen, device=device) for _ in range(2)]
+    t = torch.full((B,), temp, device=device)
+    t0 = torch.zeros(B, device=device)
+    p = torch.full((B,), pen, device=device)
+    u = torch.rand(B, generator=gen, device=device)
+    hist = torch.from_numpy(hist_np).to(device)
+    off = torch.from_numpy(off_np).to(device)
+    tok = torch.empty(B, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+    steps = 50
+
+    def timed(fn):
+        for i in range(5):
+            fn(xs[i % 2])
+        torch.cuda.synchronize(device)
+        evs = []
+        for i in range(steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn(xs[i % 2])
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize(device)
+        return sum(a.elapsed_time(b) for a, b in evs) / steps
+
+    full_ms = timed(lambda x: h.sample(x, t, p, u, tok, hist, off, stream=stream))
+    greedy_ms = timed(lambda x: h.sample(x, t0, p, u, tok, None, None, stream=stream))
+    h.check_device("sample")
+    tv = torch.tensor([full_ms, greedy_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+    full_ms, greedy_ms = tv.tolist()
+    hbm_peak, _, kind = peaks()
+    logit_bytes = B * V * 4
+    # logits once, history ids twice (count, then reset), per-row scalars, tokens
+    alg = logit_bytes + int(off_np[-1]) * 4 * 2 + B * (4 * 3 + 8 + 4)
+    res = {"workload": "sample_qwen3_vocab151936_256seq_t0.8_penalty1.2",
+           "n_seqs": B, "vocab": V, "history_ids": int(off_np[-1]), "steps": steps,
+           "sample_us": full_ms * 1e3, "greedy_no_history_us": greedy_ms * 1e3,
+           "roofline": {"bound": "hbm", "kernel": "sample (count + chunk pass)",
+                        "achieved": alg / (full_ms / 1e3) / 1e9, "peak": hbm_peak,
+                        "unit": "GB/s", "frac": alg / (full_ms / 1e3) / 1e9 / hbm_peak,
+                        "peak_source": kind, "algorithmic_bytes": alg,
+                        "greedy_pass_gbs": logit_bytes / (greedy_ms / 1e3) / 1e9}}
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        n_cpu = 8
+        xh = xs[0][:n_cpu].cpu().numpy()
+        uh = u[:n_cpu].cpu().numpy()
+        t_begin = time.perf_counter()
+        O.sample(xh, np.full(n_cpu, temp, np.float32), np.full(n_cpu, pen, np.float32), uh,
+                 hist_np[:off_np[n_cpu]], off_np[:n_cpu + 1])
+        dt = time.perf_counter() - t_begin
+        res["cpu"] = {"cores": 1, "kind": "port", "us_per_row": dt / n_cpu * 1e6,
+                      "batch_us_projected": dt / n_cpu * B * 1e6,
+                      "sample": f"first {n_cpu} of the {B} rows, one host thread (the "
+                                "reference's Sample loop is sequential)"}
+    h.close()
+    del xs
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_prefills(args, world, rank, device):
     """Times every selected prefill workload; returns JSON-ready dicts (the
     per-step times are the max over ranks)."""
@@ -647,6 +735,8 @@ def main():
     ap.add_argument("--no-decode-long", action="store_true",
                     help="skip the secondary decode workloads (32B-shape long context, "
                          "4-sequence small batch)")
+    ap.add_argument("--no-sample", action="store_true",
+                    help="skip the token-sampling workload")
     ap.add_argument("--only-prefill", action="store_true",
                     help="skip the decode workload (for profiling the prefill kernel)")
     args = ap.parse_args()
@@ -865,6 +955,7 @@ def main():
     prefill_results = run_prefills(args, world, rank, device)
     decode_long = None if args.no_decode_long else bench_decode_long(args, world, rank, device)
     decode_small = None if args.no_decode_long else bench_decode_small(args, world, rank, device)
+    sample = None if args.no_sample else bench_sample(args, world, rank, device)
 
     if rank == 0:
         hbm_peak, _, peak_kind = peaks()
@@ -900,6 +991,7 @@ def main():
             "prefill": prefill_results,
             "decode_long": decode_long,
             "decode_small": decode_small,
+            "sample": sample,
             "kv_store": kv_store_roofline(B, hq, hkv, store_ms, q_out_bytes=4),
         }
         if cpu_base is not None:

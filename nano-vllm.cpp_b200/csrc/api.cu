@@ -211,10 +211,9 @@ nvattn_status nvattn_destroy(nvattn_handle* h) {
   if (h->status_dev) cudaFree(h->status_dev);
   if (h->ws_o) cudaFree(h->ws_o);
   if (h->ws_ml) cudaFree(h->ws_ml);
-  if (h->samp_cnt) cudaFree(h->samp_cnt);
-  if (h->samp_bits) cudaFree(h->samp_bits);
+  if (h->samp_nib) cudaFree(h->samp_nib);
+  if (h->samp_exact) cudaFree(h->samp_exact);
   if (h->samp_part) cudaFree(h->samp_part);
-  if (h->samp_ticket) cudaFree(h->samp_ticket);
   delete h;
   return NVATTN_OK;
 }
@@ -350,29 +349,23 @@ nvattn_status nvattn_sample(nvattn_handle* h, int n_seqs, int n_vocab, const flo
     if (cudaStreamIsCapturing(st, &cap_status) != cudaSuccess) return NVATTN_ERR_CUDA;
     if (cap_status != cudaStreamCaptureStatusNone) return NVATTN_ERR_UNSUPPORTED;
     if (cudaStreamSynchronize(st) != cudaSuccess) return NVATTN_ERR_CUDA;
-    if (h->samp_cnt) cudaFree(h->samp_cnt);
-    if (h->samp_bits) cudaFree(h->samp_bits);
+    if (h->samp_nib) cudaFree(h->samp_nib);
+    if (h->samp_exact) cudaFree(h->samp_exact);
     if (h->samp_part) cudaFree(h->samp_part);
-    if (h->samp_ticket) cudaFree(h->samp_ticket);
-    h->samp_cnt = h->samp_bits = nullptr;
+    h->samp_nib = nullptr;
+    h->samp_exact = nullptr;
     h->samp_part = nullptr;
-    h->samp_ticket = nullptr;
     h->samp_cap = 0;
-    const long long cap = ((long long)n_vocab + 31) / 32 * 32;
+    const long long g = nvattn::sample_vocab_granule();
+    const long long cap = ((long long)n_vocab + g - 1) / g * g;
     const size_t seqs = (size_t)h->cfg.max_seqs;
-    const size_t cnt_b = seqs * cap * 4, bits_b = seqs * (cap / 32) * 4,
-                 part_b = seqs * nvattn::sample_partial_bytes(), tick_b = seqs * 4;
-    if (cudaMalloc(&h->samp_cnt, cnt_b) != cudaSuccess ||
-        cudaMalloc(&h->samp_bits, bits_b) != cudaSuccess ||
-        cudaMalloc(&h->samp_part, part_b) != cudaSuccess ||
-        cudaMalloc(&h->samp_ticket, tick_b) != cudaSuccess) {
+    if (nvattn::sample_prepare_device() != NVATTN_OK) return NVATTN_ERR_CUDA;
+    if (cudaMalloc(&h->samp_nib, seqs * cap / 2) != cudaSuccess ||
+        cudaMalloc(&h->samp_exact, seqs * cap * 4) != cudaSuccess ||
+        cudaMalloc(&h->samp_part, seqs * nvattn::sample_partial_bytes()) != cudaSuccess) {
       cudaGetLastError();
       return NVATTN_ERR_NO_MEMORY;
     }
-    if (cudaMemsetAsync(h->samp_cnt, 0, cnt_b, st) != cudaSuccess ||
-        cudaMemsetAsync(h->samp_bits, 0, bits_b, st) != cudaSuccess ||
-        cudaMemsetAsync(h->samp_ticket, 0, tick_b, st) != cudaSuccess)
-      return NVATTN_ERR_CUDA;
     h->samp_cap = cap;
   }
   return nvattn::launch_sample(h, n_seqs, n_vocab, logits_dev, row_stride, temperatures_dev,

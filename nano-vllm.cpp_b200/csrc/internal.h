@@ -42,12 +42,11 @@ struct nvattn_handle {
   std::vector<NvattnTensorMapEntry> maps;
 
   // sampler workspace (sample.cu), allocated by the first nvattn_sample call
-  // for a vocabulary size; all zero between calls except the partials
-  uint32_t* samp_cnt = nullptr;     // [max_seqs][samp_cap] history id counts
-  uint32_t* samp_bits = nullptr;    // [max_seqs][samp_cap/32] history id bitmap
-  void* samp_part = nullptr;        // [max_seqs][512] chunk partials
-  unsigned* samp_ticket = nullptr;  // [max_seqs] finished chunks
-  long long samp_cap = 0;           // vocabulary capacity (multiple of 32)
+  // for a vocabulary size; no contents survive between calls
+  uint8_t* samp_nib = nullptr;     // [max_seqs][samp_cap/2] 4-bit history id counts
+  uint32_t* samp_exact = nullptr;  // [max_seqs][samp_cap] exact counts where 4 bits saturate
+  void* samp_part = nullptr;       // [max_seqs][512] chunk partials
+  long long samp_cap = 0;          // vocabulary capacity (multiple of 4096)
 };
 
 namespace nvattn {
@@ -98,7 +97,9 @@ nvattn_status launch_plan_decode(nvattn_handle* h, int n_seqs, const int64_t* se
 
 // Token sampler (sample.cu).
 int sample_max_vocab();
-size_t sample_partial_bytes();  // per sequence
+int sample_vocab_granule();      // samp_cap is a multiple of this
+size_t sample_partial_bytes();   // per sequence
+nvattn_status sample_prepare_device();  // kernel attributes, outside captures
 nvattn_status launch_sample(nvattn_handle* h, int n_seqs, int n_vocab, const float* logits,
                             long long row_stride, const float* temps, const float* pens,
                             const int32_t* hist, const int64_t* hist_off, const float* uniforms,

@@ -210,6 +210,50 @@ def test_workspace_is_clean_between_calls():
         h.close()
 
 
+@pytest.mark.parametrize("V", [QWEN3_VOCAB, 200000])
+def test_penalty_counts_are_exact_past_saturation(V):
+    """Ids seen 3, 20 (past the 4-bit count) and 300 (past the 8-bit
+    histogram) times, in both count segments of a 200000-id vocabulary: a
+    competitor one ulp below / above the oracle's penalised value flips the
+    argmax if the device's count is one too high / too low."""
+    pen = np.float32(1.01)
+    reps = {0: 3, 1: 20, 2: 300}
+    ids = {0: 17, 1: V // 2 + 5, 2: V - 9}
+    rows, hists = [], []
+    for kind in range(3):
+        tok = ids[kind]
+        for sign in (1.0, -1.0):
+            for side in (-1, 1):
+                x = np.random.default_rng(kind * 7 + (side > 0)).normal(0, 1, V).astype(np.float32)
+                x[tok] = np.float32(50.0 * sign)
+                hist = np.full(reps[kind], tok, np.int32)
+                v = O.penalize_rows(x[None], np.array([pen], np.float32), hist,
+                                    np.array([0, hist.size], np.int64))[0, tok]
+                others = np.arange(V) != tok
+                x[others] = np.minimum(x[others], v - np.float32(1.0))
+                comp = V // 3 if side < 0 else 5
+                x[comp] = np.nextafter(v, np.float32(-np.inf) if side < 0 else np.float32(np.inf))
+                rows.append(x)
+                hists.append(hist)
+    x = np.stack(rows)
+    n = x.shape[0]
+    off = np.concatenate([[0], np.cumsum([hh.size for hh in hists])]).astype(np.int64)
+    hist = np.concatenate(hists)
+    pens = np.full(n, pen, np.float32)
+    want = O.sample(x, np.zeros(n, np.float32), pens, np.zeros(n, np.float32), hist, off)
+    h = handle(8, 8, 16, max_seqs=n)
+    try:
+        got = _run(h, x, np.zeros(n), pens, np.zeros(n), hist, off)
+        assert h.get_error() == (nvattn.OK, 0)
+    finally:
+        h.close()
+    np.testing.assert_array_equal(got, want)
+    # the construction makes the penalised id win exactly when side < 0
+    for r in range(n):
+        kind, rest = divmod(r, 4)
+        assert (want[r] == ids[kind]) == (rest % 2 == 0), r
+
+
 @pytest.mark.parametrize("u_bad", [1.0, -0.25, float("nan")])
 def test_bad_draw_is_reported(u_bad):
     V, n = 300, 3
