@@ -462,12 +462,13 @@ def bench_sample(args, world, rank, device):
     """Token sampling over the headline batch: 256 rows of Qwen3's 151936
     logits (f32, N(0, 4^2)), temperature 0.8 and repetition penalty 1.2 (the
     reference's example settings), each sequence's history its decode
-    context length of uniform random ids (1k-32k ids, 2.9 M in all).  Two
+    context length of uniform random ids (1k-32k ids, 2.7 M in all).  Two
     logits buffers alternate (311 MB > L2).  Reports the call's device time
-    (count + chunk kernels), the same rows greedy without history (the bare
-    logits pass), GB/s of the call's algorithmic bytes, and on one GPU the
-    oracle's restatement of the reference's Sample on a bounded sample of
-    rows, timed on one host core as the reference runs it."""
+    (history count, logits pass and finish kernels), the same rows greedy
+    without history (the bare logits pass), GB/s of the call's algorithmic
+    bytes, and on one GPU the oracle's restatement of the reference's Sample
+    on a bounded sample of rows, timed on one host core as the reference
+    runs it."""
     import torch
     import nvattn
     V, temp, pen = 151936, 0.8, 1.2
@@ -508,20 +509,24 @@ def bench_sample(args, world, rank, device):
 
     full_ms = timed(lambda x: h.sample(x, t, p, u, tok, hist, off, stream=stream))
     greedy_ms = timed(lambda x: h.sample(x, t0, p, u, tok, None, None, stream=stream))
+    temp_ms = timed(lambda x: h.sample(x, t, p, u, tok, None, None, stream=stream))
+    greedy_pen_ms = timed(lambda x: h.sample(x, t0, p, u, tok, hist, off, stream=stream))
     h.check_device("sample")
-    tv = torch.tensor([full_ms, greedy_ms], dtype=torch.float64, device=device)
+    tv = torch.tensor([full_ms, greedy_ms, temp_ms, greedy_pen_ms], dtype=torch.float64,
+                      device=device)
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(tv, op=dist.ReduceOp.MAX)
-    full_ms, greedy_ms = tv.tolist()
+    full_ms, greedy_ms, temp_ms, greedy_pen_ms = tv.tolist()
     hbm_peak, _, kind = peaks()
     logit_bytes = B * V * 4
-    # logits once, history ids twice (count, then reset), per-row scalars, tokens
-    alg = logit_bytes + int(off_np[-1]) * 4 * 2 + B * (4 * 3 + 8 + 4)
+    # logits once, history ids once, per-row scalars and offsets, tokens
+    alg = logit_bytes + int(off_np[-1]) * 4 + B * (4 * 3 + 8 + 4)
     res = {"workload": "sample_qwen3_vocab151936_256seq_t0.8_penalty1.2",
            "n_seqs": B, "vocab": V, "history_ids": int(off_np[-1]), "steps": steps,
            "sample_us": full_ms * 1e3, "greedy_no_history_us": greedy_ms * 1e3,
-           "roofline": {"bound": "hbm", "kernel": "sample (count + chunk pass)",
+           "temperature_no_history_us": temp_ms * 1e3, "greedy_penalty_us": greedy_pen_ms * 1e3,
+           "roofline": {"bound": "hbm", "kernel": "sample (count + pass + finish)",
                         "achieved": alg / (full_ms / 1e3) / 1e9, "peak": hbm_peak,
                         "unit": "GB/s", "frac": alg / (full_ms / 1e3) / 1e9 / hbm_peak,
                         "peak_source": kind, "algorithmic_bytes": alg,
@@ -737,6 +742,8 @@ def main():
                          "4-sequence small batch)")
     ap.add_argument("--no-sample", action="store_true",
                     help="skip the token-sampling workload")
+    ap.add_argument("--only-sample", action="store_true",
+                    help="run only the token-sampling workload (one JSON line)")
     ap.add_argument("--only-prefill", action="store_true",
                     help="skip the decode workload (for profiling the prefill kernel)")
     args = ap.parse_args()
@@ -765,6 +772,14 @@ def main():
             first = res[0] if res else {}
             print(json.dumps({"metric": METRIC, "value": first.get("tokens_per_s"),
                               "unit": "tokens/s", "n_gpus": world, "prefill": res}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
+    if args.only_sample:
+        res = bench_sample(args, world, rank, device)
+        if rank == 0:
+            print(json.dumps({"n_gpus": world, "sample": res}), flush=True)
         if world > 1:
             dist.destroy_process_group()
         return 0
