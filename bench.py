@@ -191,6 +191,112 @@ def bench_prefill(kind, args, world, rank, device):
     return fields, pre_ms, step_ms
 
 
+def bench_prefill_chunked(args, world, rank, device):
+    """Chunked prefill against one-shot prefill: Qwen3-8B attention shape (32 q
+    / 8 kv heads), 8 prompts of 8192 new tokens, nothing cached.  One shot:
+    the fused q/k norm + RoPE + K/V store of all 65,536 tokens, then one
+    causal prefill.  Chunked: nvattn_schedule_prefill_chunks with a 3,000
+    token budget per step (22 steps; chunks start mid-block and a step can
+    end one prompt and begin the next); each step stores its chunks' K/V and
+    runs their prefill over everything cached so far.  Per-step inputs (q/k/v rows, plans) are built before the
+    timed region; both runs time device work only.  Reports both totals, the
+    longest step and TFLOP/s of the algorithmic causal FLOPs."""
+    import torch
+    import nvattn
+    Hq, Hkv, n, L, budget = 32, 8, 8, 8192, 3000
+    hq, hkv = Hq // world, Hkv // world
+    lens = np.full(n, L, np.int64)
+    need = (lens + BS - 1) // BS
+    num_blocks = int(need.sum()) + 8
+    rng = np.random.default_rng(SEED + 6)
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    bt_np = perm[:int(need.sum())].reshape(n, int(need.max()))
+    cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=num_blocks,
+                              max_seqs=n, max_context=L, max_position=L, device=device.index)
+    h = nvattn.Handle(cfg)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(6000 + rank)
+    n_slots = num_blocks * BS
+    kc = torch.zeros((n_slots, hkv, D), dtype=torch.int16, device=device)
+    vc = torch.zeros_like(kc)
+    T = int(lens.sum())
+    q = torch.randn((T, hq, D), generator=gen, device=device)  # token t of seq s at s*L + t
+    k = torch.randn((T, hkv, D), generator=gen, device=device)
+    v = torch.randn((T, hkv, D), generator=gen, device=device)
+    w16 = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16).view(
+        torch.int16)
+    stream = torch.cuda.current_stream(device)
+
+    def make_step(seqs, starts, ends):
+        cu, qs, cl, pos, slot = nvattn.plan_prefill(ends, starts, bt_np[seqs])
+        rows = np.concatenate([s * L + np.arange(a, b) for s, a, b in zip(seqs, starts, ends)])
+        idx = torch.from_numpy(rows).to(device)
+        t = {"q": q.index_select(0, idx), "k": k.index_select(0, idx),
+             "v": v.index_select(0, idx)}
+        t["qb"] = torch.empty(t["q"].shape, dtype=torch.bfloat16, device=device)
+        t["out"] = torch.empty(t["q"].shape, device=device)
+        for name, arr in (("cu", cu), ("qs", qs), ("cl", cl), ("pos", pos), ("slot", slot),
+                          ("bt", np.ascontiguousarray(bt_np[seqs]))):
+            t[name] = torch.from_numpy(arr).to(device)
+        t["max_q"] = int((cl - qs).max())
+        return t
+
+    def run(t):
+        h.kv_store(0, t["q"], t["k"], t["v"], w16, w16, t["pos"], t["slot"], t["qb"], kc, vc,
+                   stream=stream)
+        h.prefill(0, t["qb"], t["cu"], t["qs"], t["cl"], t["bt"], t["max_q"], kc, vc, t["out"],
+                  stream=stream)
+
+    one = make_step(list(range(n)), [0] * n, [L] * n)
+    chunks, done, held, free = [], np.zeros(n, np.int64), np.zeros(n, np.int64), num_blocks
+    while (done < lens).any():
+        idx = np.array([s for s in range(n) if done[s] < lens[s]])
+        sel, ends, adds = nvattn.schedule_prefill_chunks(lens[idx], done[idx], held[idx], free,
+                                                         256, budget)
+        seqs = [int(idx[i]) for i in sel]
+        chunks.append(make_step(seqs, [int(done[s]) for s in seqs], ends.tolist()))
+        for s, e, a_ in zip(seqs, ends.tolist(), adds.tolist()):
+            done[s], held[s] = e, held[s] + a_
+            free -= a_
+
+    def timed(steps_list, reps):
+        for _ in range(2):
+            for t in steps_list:
+                run(t)
+        torch.cuda.synchronize(device)
+        evs = []
+        for _ in range(reps):
+            for t in steps_list:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                run(t)
+                b.record(stream)
+                evs.append((a, b))
+        torch.cuda.synchronize(device)
+        per = [a.elapsed_time(b) for a, b in evs]
+        k_ = len(steps_list)
+        totals = [sum(per[r * k_:(r + 1) * k_]) for r in range(reps)]
+        return sum(totals) / reps, max(per)
+
+    one_ms, _ = timed([one], 3)
+    ch_ms, ch_max = timed(chunks, 3)
+    h.check_device("prefill_chunked")
+    tv = torch.tensor([one_ms, ch_ms, ch_max], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+    one_ms, ch_ms, ch_max = tv.tolist()
+    h.close()
+    flops = 4.0 * D * Hq * n * (L * (L + 1) // 2)
+    return {"workload": "prefill_chunked_qwen3_8b_8x8192_budget3000", "q_heads": Hq,
+            "kv_heads": Hkv, "n_seqs": n, "prompt_len": L, "token_budget": budget,
+            "steps": len(chunks), "one_shot_ms": one_ms, "chunked_total_ms": ch_ms,
+            "chunked_max_step_ms": ch_max, "chunked_over_one_shot": ch_ms / one_ms,
+            "one_shot_tflops": flops / (one_ms / 1e3) / 1e12,
+            "chunked_tflops": flops / (ch_ms / 1e3) / 1e12,
+            "note": "store + prefill per step, device time"}
+
+
 def kv_store_roofline(T, hq, hkv, ms, q_out_bytes):
     """Algorithmic bytes of the fused q/k norm + RoPE + K/V store on one GPU:
     read q, k, v (f32) and one RoPE row per token, write q (f32 or bf16) and
@@ -740,6 +846,8 @@ def main():
     ap.add_argument("--no-decode-long", action="store_true",
                     help="skip the secondary decode workloads (32B-shape long context, "
                          "4-sequence small batch)")
+    ap.add_argument("--no-chunked", dest="chunked", action="store_false",
+                    help="skip the chunked-prefill workload")
     ap.add_argument("--no-sample", action="store_true",
                     help="skip the token-sampling workload")
     ap.add_argument("--only-sample", action="store_true",
@@ -768,10 +876,12 @@ def main():
 
     if args.only_prefill:
         res = run_prefills(args, world, rank, device)
+        chunked = bench_prefill_chunked(args, world, rank, device) if args.chunked else None
         if rank == 0:
             first = res[0] if res else {}
             print(json.dumps({"metric": METRIC, "value": first.get("tokens_per_s"),
-                              "unit": "tokens/s", "n_gpus": world, "prefill": res}), flush=True)
+                              "unit": "tokens/s", "n_gpus": world, "prefill": res,
+                              "prefill_chunked": chunked}), flush=True)
         if world > 1:
             dist.destroy_process_group()
         return 0
@@ -971,6 +1081,7 @@ def main():
     decode_long = None if args.no_decode_long else bench_decode_long(args, world, rank, device)
     decode_small = None if args.no_decode_long else bench_decode_small(args, world, rank, device)
     sample = None if args.no_sample else bench_sample(args, world, rank, device)
+    prefill_chunked = bench_prefill_chunked(args, world, rank, device) if args.chunked else None
 
     if rank == 0:
         hbm_peak, _, peak_kind = peaks()
@@ -1007,6 +1118,7 @@ def main():
             "decode_long": decode_long,
             "decode_small": decode_small,
             "sample": sample,
+            "prefill_chunked": prefill_chunked,
             "kv_store": kv_store_roofline(B, hq, hkv, store_ms, q_out_bytes=4),
         }
         if cpu_base is not None:

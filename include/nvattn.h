@@ -172,6 +172,28 @@ NVATTN_API nvattn_status nvattn_plan_decode_device(
     int max_blocks, int32_t* context_lens_dev, int32_t* positions_dev,
     int32_t* slot_mapping_dev, nvattn_stream_t stream);
 
+/* ---- chunked-prefill admission (host only) -------------------------------- */
+
+/* One step's prefill admission with chunking: the reference's
+ * Scheduler::Schedule prefill loop (scheduler.cpp:27-44) admitting parts of
+ * prompts.  Waiting sequences s = 0..n_waiting-1 in FIFO order, each with
+ * prompt_lens[s] tokens of which done[s] (0 <= done < len; a fully cached
+ * prompt passes len - 1) are already in the KV cache and held_blocks[s] KV
+ * blocks already allocated.  Each admitted sequence gets the chunk
+ * [done[s], chunk_end[k]) -- as many of its remaining tokens as the step's
+ * remaining token budget (max_num_batched_tokens, charged with computed
+ * tokens) and the free blocks (free_blocks, charged with new_blocks[k] =
+ * blocks the chunk adds) allow -- at most max_num_seqs sequences; admission
+ * stops at the first sequence that gets no token.  selected[k] = the
+ * sequence index of the k-th admitted sequence, *n_selected = k's count.
+ * Run each chunk as a prefill with num_cached = done[s] and seq_len =
+ * chunk_end[k]; the chunked outputs equal the one-shot prefill's bit for bit.
+ * Host only: no device, no handle. */
+NVATTN_API nvattn_status nvattn_schedule_prefill_chunks(
+    int n_waiting, const int64_t* prompt_lens, const int64_t* done, const int64_t* held_blocks,
+    int block_size, int64_t free_blocks, int max_num_seqs, int64_t max_num_batched_tokens,
+    int32_t* selected, int64_t* chunk_end, int64_t* new_blocks, int* n_selected);
+
 /* ---- token sampling ------------------------------------------------------ */
 
 /* Next-token sampling for a batch: ModelRunner::Sample

@@ -30,7 +30,7 @@ EXPORTED = [
     "nvattn_version", "nvattn_get_error", "nvattn_plan_prefill", "nvattn_plan_decode",
     "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
     "nvattn_paged_decode_noalloc", "nvattn_plan_prefill_device", "nvattn_plan_decode_device",
-    "nvattn_sample",
+    "nvattn_sample", "nvattn_schedule_prefill_chunks",
 ]
 ERR_SCRATCH_LIMIT = 7
 
@@ -94,6 +94,9 @@ def lib():
                                                  _vp, _vp, _vp, _vp]
         L.nvattn_plan_decode_device.argtypes = [_vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp]
         L.nvattn_sample.argtypes = [_vp, _i32, _i32, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp]
+        L.nvattn_schedule_prefill_chunks.argtypes = [_i32, _vp, _vp, _vp, _i32, _i64, _i32,
+                                                     _i64, _vp, _vp, _vp,
+                                                     ctypes.POINTER(_i32)]
         L.nvattn_kv_store_qk_norm_rope.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                                                    _vp, _vp, _i32, _vp, _vp, _vp]
         L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
@@ -301,6 +304,27 @@ def plan_prefill(seq_lens, num_cached, block_tables, block_size=256):
     _check(st, "nvattn_plan_prefill")
     T = int(cu[-1])
     return cu, qs, cl, pos[:T], slot[:T]
+
+
+def schedule_prefill_chunks(prompt_lens, done, held_blocks, free_blocks, max_num_seqs,
+                            max_num_batched_tokens, block_size=256):
+    """nvattn_schedule_prefill_chunks: one step's chunked prefill admission.
+    Returns (selected sequence indices, chunk ends, new blocks per chunk)."""
+    import numpy as np
+    lens = np.ascontiguousarray(prompt_lens, dtype=np.int64)
+    dn = np.ascontiguousarray(done, dtype=np.int64)
+    hb = np.ascontiguousarray(held_blocks, dtype=np.int64)
+    n = lens.shape[0]
+    sel = np.zeros(max(n, 1), np.int32)
+    end = np.zeros(max(n, 1), np.int64)
+    nb = np.zeros(max(n, 1), np.int64)
+    k = _i32()
+    st = lib().nvattn_schedule_prefill_chunks(n, _np_ptr(lens), _np_ptr(dn), _np_ptr(hb),
+                                              block_size, int(free_blocks), int(max_num_seqs),
+                                              int(max_num_batched_tokens), _np_ptr(sel),
+                                              _np_ptr(end), _np_ptr(nb), ctypes.byref(k))
+    _check(st, "nvattn_schedule_prefill_chunks")
+    return sel[:k.value], end[:k.value], nb[:k.value]
 
 
 def plan_decode(seq_lens, block_tables, block_size=256):
