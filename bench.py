@@ -162,11 +162,14 @@ def bench_prefill(kind, args, world, rank, device):
         evs.append((z, a, b))
 
     steps = max(2, args.prefill_steps)
+    clocks = ClockSampler(device.index)
+    clocks.start()
     for _ in range(max(3, min(args.warmup, 5))):
         step()
     torch.cuda.synchronize(device)
     h.check_device(f"prefill warmup {name}")
     evs.clear()
+    mark = clocks.mark()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         import torch.distributed as dist
@@ -176,6 +179,7 @@ def bench_prefill(kind, args, world, rank, device):
         step()
     t1.record(stream)
     torch.cuda.synchronize(device)
+    clk = clocks.stop(mark)
     h.check_device(f"prefill {name}")
     step_ms = t0.elapsed_time(t1) / steps
     pre_ms = sum(a.elapsed_time(b) for _, a, b in evs) / len(evs)
@@ -187,7 +191,8 @@ def bench_prefill(kind, args, world, rank, device):
     fields = {"workload": name, "q_heads": Hq, "kv_heads": Hkv, "n_seqs": len(lens),
               "new_tokens": T, "sum_context": int(cl.sum()), "flops_per_step": flops,
               "steps": steps, "pv_precision": "f16 P x f16 V (V converted in smem)",
-              "kv_store": kv_store_roofline(T, hq, hkv, store_ms, q_out_bytes=2)}
+              "kv_store": kv_store_roofline(T, hq, hkv, store_ms, q_out_bytes=2),
+              "clocks": clk}
     return fields, pre_ms, step_ms
 
 
@@ -681,6 +686,13 @@ def run_prefills(args, world, rank, device):
                          "frac": achieved / tflops_peak, "peak_source": peak_kind,
                          "prefill_ms": pre_ms, "frac_of_2250_nominal": achieved / 2250.0},
         })
+        # the dense BF16 tensor rate at the SM clock sampled during the run
+        # (148 SMs x 8192 FLOP per cycle; 2.25 PFLOP/s is this at ~1.86 GHz)
+        mhz = (fields.get("clocks") or {}).get("sm_mhz")
+        if mhz:
+            at_clock = 148 * 8192 * mhz * 1e6 / 1e12
+            fields["roofline"]["peak_at_sampled_clock"] = at_clock
+            fields["roofline"]["frac_of_peak_at_sampled_clock"] = achieved / at_clock
         results.append(fields)
     return results
 
