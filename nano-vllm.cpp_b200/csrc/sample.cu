@@ -291,6 +291,12 @@ __global__ void __launch_bounds__(kCountThreads, 1) sample_count_kernel(SampleAr
 // Every piece summary below is computed in one fixed order that the finish
 // kernel repeats for the selected piece.
 
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // (max, first arg-max) pair order: a larger value wins, then the smaller index.
 __device__ __forceinline__ void max_combine(float& m, int& am, float m2, int am2) {
   if (am2 == INT_MAX) return;
@@ -384,16 +390,34 @@ __device__ __forceinline__ void piece_max(const float (&x)[kPieceSlabs][4],
                                           int& flags) {
   m = -INFINITY;
   bool nan = false, num = false;
+  if (kFull) {
+    // 3-input max that propagates NaN: without a NaN (the usual case) it is
+    // the maximum; a NaN anywhere falls back to the NaN-skipping loop below
+    float mn = max3_nan(max3_nan(x[0][0], x[0][1], x[0][2]), x[0][3], x[1][0]);
+    mn = max3_nan(mn, x[1][1], x[1][2]);
+    mn = max3_nan(mn, x[1][3], x[2][0]);
+    mn = max3_nan(mn, x[2][1], x[2][2]);
+    mn = max3_nan(mn, x[2][3], x[3][0]);
+    mn = max3_nan(mn, x[3][1], x[3][2]);
+    mn = max3_nan(mn, x[3][3], x[3][3]);
+    nan = isnan(mn);
+    m = mn;
+    num = true;
+  }
+  if (!kFull || __any_sync(0xffffffffu, nan)) {
+    m = -INFINITY;
+    nan = num = false;
 #pragma unroll
-  for (int v = 0; v < kPieceSlabs; ++v)
+    for (int v = 0; v < kPieceSlabs; ++v)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (!kFull && !(valid[v] >> j & 1u)) continue;
-      const bool isn = x[v][j] != x[v][j];
-      nan |= isn;
-      num |= !isn;
-      m = fmaxf(m, x[v][j]);  // fmaxf skips NaN
-    }
+      for (int j = 0; j < 4; ++j) {
+        if (!kFull && !(valid[v] >> j & 1u)) continue;
+        const bool isn = x[v][j] != x[v][j];
+        nan |= isn;
+        num |= !isn;
+        m = fmaxf(m, x[v][j]);  // fmaxf skips NaN
+      }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   flags = __any_sync(0xffffffffu, nan) ? 1 : 0;
