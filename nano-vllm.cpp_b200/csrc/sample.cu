@@ -17,15 +17,16 @@
 //     consumer warps takes one 512-element piece of the chunk, applies the
 //     penalty in shared memory (the reference's v = v < 0 ? v*p : v/p once
 //     per occurrence, bit for bit; the piece's history ids are listed and
-//     spread over the lanes) and writes the piece's maximum, first arg-max, NaN flags
-//     and -- for sampling rows -- the sum of exp((x - piece max)/t) in a
-//     fixed order, with warp shuffles only (no block barrier).
+//     spread over the lanes) and writes the piece's maximum, first arg-max,
+//     NaN flags and -- for sampling rows -- the sum of exp((x - piece max)/t)
+//     in a fixed order, with warp shuffles only (no block barrier).
 //  3. finish -- one CTA per sequence combines the pieces: greedy rows take
 //     the first arg-max; sampling rows scale each piece's sum by
 //     exp((piece max - row max)/t), draw r = u*S, find the piece whose running
 //     total reaches r, and one warp recomputes that piece exactly as pass 2
 //     did and walks slab -> lane -> element.
-// One pass over the logits plus 1/8 of their size in counts: HBM-bound.
+// Traffic: one pass over the logits plus 1/8 of their size in 4-bit counts
+// (the HBM floor; the passes are issue/latency-bound above it).
 //
 // Greedy tokens are bit-exact with the reference (same penalised values,
 // same first-index rule, same NaN outcomes).  Sampled tokens follow the same
@@ -59,13 +60,13 @@ constexpr int kPassSmem = kStages * (kChunk * 4 + kNibBytes);
 constexpr int kPassCtasPerSm = 3;
 constexpr int kCountSmem = 2 * kSegment + kOvSlots * 8;
 
-struct ChunkPartial {
+struct PiecePartial {
   float max;   // maximum of the piece's non-NaN penalised values (-inf if none)
   int argmax;  // first index holding it, INT_MAX if the piece has no non-NaN value
   float sum;   // sampling rows: sum of exp((x - max)/t) in the fixed scan order
   int flags;   // bit 0: a NaN in the piece; bit 1: element 0 of the row is NaN
 };
-static_assert(sizeof(ChunkPartial) == 16, "partial layout");
+static_assert(sizeof(PiecePartial) == 16, "partial layout");
 
 struct SampleArgs {
   int n_seqs, n_vocab, n_chunks;
@@ -80,7 +81,7 @@ struct SampleArgs {
   uint8_t* nib;          // [max_seqs][cap/2] 4-bit counts
   uint32_t* cnt_exact;   // [max_seqs][cap] exact counts of ids with a 4-bit count of 15
   long long cap;         // vocabulary capacity, a multiple of kChunk
-  ChunkPartial* part;    // [max_seqs][kMaxChunks * 8] piece summaries
+  PiecePartial* part;    // [max_seqs][kMaxChunks * 8] piece summaries
   DeviceStatus* status;
 };
 
@@ -479,10 +480,10 @@ __device__ __forceinline__ float k2_of(float temp) { return __fdiv_rn(1.44269504
 
 // Summary of one piece (every lane returns the same value).
 template <bool kFull>
-__device__ __forceinline__ ChunkPartial summarise(float (&x)[kPieceSlabs][4],
+__device__ __forceinline__ PiecePartial summarise(float (&x)[kPieceSlabs][4],
                                                   const unsigned (&valid)[kPieceSlabs], int base,
                                                   int lane, bool greedy, float temp) {
-  ChunkPartial cp;
+  PiecePartial cp;
   piece_max<kFull>(x, valid, base, lane, greedy, cp.max, cp.argmax, cp.flags);
   cp.sum = 0.0f;
   if (!greedy && !(cp.flags & 1) && cp.argmax != INT_MAX && isfinite(cp.max)) {
@@ -556,7 +557,7 @@ struct StageMeta {
 
 // The summary of a piece that crosses the end of the row (one per row), out
 // of line so that only the full-piece version is inlined into the pass.
-__device__ __noinline__ ChunkPartial summarise_partial(float4 q0, float4 q1, float4 q2, float4 q3,
+__device__ __noinline__ PiecePartial summarise_partial(float4 q0, float4 q1, float4 q2, float4 q3,
                                                        uint32_t valid16, int base, int lane,
                                                        bool greedy, float temp) {
   float x[kPieceSlabs][4] = {{q0.x, q0.y, q0.z, q0.w},
@@ -717,7 +718,7 @@ __global__ void __launch_bounds__(kPassThreads, kPassCtasPerSm) sample_pass_kern
     }
     const int p = c * kPiecesPerChunk + warp;
     const bool greedy = temp < 1e-6f;
-    ChunkPartial cp;
+    PiecePartial cp;
     if (full_piece)
       cp = summarise<true>(x, valid, p * kPiece, lane, greedy, temp);
     else
@@ -731,7 +732,7 @@ __global__ void __launch_bounds__(kPassThreads, kPassCtasPerSm) sample_pass_kern
   }
 }
 
-__device__ __forceinline__ double piece_scale(const ChunkPartial& cp, float gm, float temp) {
+__device__ __forceinline__ double piece_scale(const PiecePartial& cp, float gm, float temp) {
   return cp.argmax == INT_MAX || !isfinite(cp.max) ? 0.0 : exp(((double)cp.max - gm) / temp);
 }
 
@@ -752,13 +753,13 @@ __global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
   const int n_p = a.n_chunks * kPiecesPerChunk;
   const int per = (n_p + kThreads - 1) / kThreads;
   const int p0 = min(n_p, tid * per), p1 = min(n_p, p0 + per);
-  const ChunkPartial* parts = a.part + (long long)s * kMaxPieces;
+  const PiecePartial* parts = a.part + (long long)s * kMaxPieces;
 
   // (max, arg-max, flags) over the row
   float m = -INFINITY;
   int am = INT_MAX, fl = 0;
   for (int k = p0; k < p1; ++k) {
-    const ChunkPartial cp = parts[k];
+    const PiecePartial cp = parts[k];
     max_combine(m, am, cp.max, cp.argmax);
     fl |= cp.flags;
   }
@@ -913,7 +914,7 @@ __global__ void __launch_bounds__(kThreads) sample_finish_kernel(SampleArgs a) {
 
 int sample_max_vocab() { return kMaxChunks * kChunk; }
 int sample_vocab_granule() { return kChunk; }
-size_t sample_partial_bytes() { return sizeof(ChunkPartial) * kMaxPieces; }
+size_t sample_partial_bytes() { return sizeof(PiecePartial) * kMaxPieces; }
 
 nvattn_status sample_prepare_device() {
   // large dynamic shared memory: set before the first launch, outside captures
@@ -946,7 +947,7 @@ nvattn_status launch_sample(nvattn_handle* h, int n_seqs, int n_vocab, const flo
   a.nib = h->samp_nib;
   a.cnt_exact = h->samp_exact;
   a.cap = h->samp_cap;
-  a.part = reinterpret_cast<ChunkPartial*>(h->samp_part);
+  a.part = reinterpret_cast<PiecePartial*>(h->samp_part);
   a.status = h->status_dev;
   if (hist != nullptr) sample_count_kernel<<<n_seqs, kCountThreads, kCountSmem, stream>>>(a);
   const bool bulk = (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && row_stride % 4 == 0;
