@@ -46,6 +46,11 @@ SEED = 0
 # algorithmic bytes (x1.0099); scaled to the full launch's 10.987 GB.
 NCU_TRAFFIC_BYTES_N1 = 11.096e9
 
+# sm__pipe_tensor_cycles_active of paged_prefill_kernel, fraction of elapsed
+# cycles, from the full ncu capture of the chunk shape (2 x 2048 new tokens at
+# [30720, 32768), 32B heads) summarised in profiles/paged_prefill_chunk_qwen3_32b.md.
+NCU_PREFILL_TENSOR_ACTIVE = 0.533
+
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
@@ -686,6 +691,11 @@ def run_prefills(args, world, rank, device):
                          "frac": achieved / tflops_peak, "peak_source": peak_kind,
                          "prefill_ms": pre_ms, "frac_of_2250_nominal": achieved / 2250.0},
         })
+        # tensor-pipe utilisation from the committed ncu capture of this kernel
+        # on the chunk shape (sm__pipe_tensor_cycles_active, pct of elapsed;
+        # profiles/paged_prefill_chunk_qwen3_32b.md); null for other shapes
+        fields["roofline"]["ncu_tensor_pipe_active"] = (
+            NCU_PREFILL_TENSOR_ACTIVE if fields["workload"].startswith("chunked_prefill") else None)
         # the dense BF16 tensor rate at the SM clock sampled during the run
         # (148 SMs x 8192 FLOP per cycle; 2.25 PFLOP/s is this at ~1.86 GHz)
         mhz = (fields.get("clocks") or {}).get("sm_mhz")
