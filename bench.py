@@ -41,14 +41,14 @@ N_SEQS, HQ, HKV, D, BS = 256, 32, 8, 128, 256
 SEED = 0
 
 # DRAM traffic per decode launch of this workload (dram__bytes_read.sum +
-# dram__bytes_write.sum): the 32-sequence ncu capture summarised in
-# profiles/paged_decode_qwen3_8b_256seq.md moved 1.3767 GB for 1.3632 GB of
+# dram__bytes_write.sum): an ncu capture of the first 32 sequences of this
+# workload moved 1.3767 GB for 1.3632 GB of
 # algorithmic bytes (x1.0099); scaled to the full launch's 10.987 GB.
 NCU_TRAFFIC_BYTES_N1 = 11.096e9
 
 # sm__pipe_tensor_cycles_active of paged_prefill_kernel, fraction of elapsed
-# cycles, from the full ncu capture of the chunk shape (2 x 2048 new tokens at
-# [30720, 32768), 32B heads) summarised in profiles/paged_prefill_chunk_qwen3_32b.md.
+# cycles, from a full ncu capture of the chunk shape (2 x 2048 new tokens at
+# [30720, 32768), 32B heads).
 NCU_PREFILL_TENSOR_ACTIVE = 0.533
 
 
@@ -691,9 +691,9 @@ def run_prefills(args, world, rank, device):
                          "frac": achieved / tflops_peak, "peak_source": peak_kind,
                          "prefill_ms": pre_ms, "frac_of_2250_nominal": achieved / 2250.0},
         })
-        # tensor-pipe utilisation from the committed ncu capture of this kernel
-        # on the chunk shape (sm__pipe_tensor_cycles_active, pct of elapsed;
-        # profiles/paged_prefill_chunk_qwen3_32b.md); null for other shapes
+        # tensor-pipe utilisation from an ncu capture of this kernel on the
+        # chunk shape (sm__pipe_tensor_cycles_active, fraction of elapsed
+        # cycles); null for other shapes
         fields["roofline"]["ncu_tensor_pipe_active"] = (
             NCU_PREFILL_TENSOR_ACTIVE if fields["workload"].startswith("chunked_prefill") else None)
         # the dense BF16 tensor rate at the SM clock sampled during the run

@@ -1,6 +1,6 @@
 """GPU parity of nvattn_paged_decode against the oracle.
 
-Tolerances (north-star: BF16 inputs, FP32 accumulate):
+Tolerances (BF16 inputs, FP32 accumulate):
   * against fp64 math (oracle TRUTH): max-abs-err <= 2e-2 and
     mean-rel-err <= 1e-3 (sum|a-b| / sum|b|); in practice ~1e-6.
   * against the reference's dtype chain (oracle GGML: f16 Q/K/V, f16 V

@@ -3,7 +3,7 @@
 The kernel multiplies bf16 Q and bf16 K on the tensor cores, rounds the
 softmax probabilities P to f16 and converts V to f16 (as the reference's
 ggml_cast does) for the P.V product, and accumulates in fp32.  Tolerances
-(north-star: BF16 inputs, FP32 accumulate):
+(BF16 inputs, FP32 accumulate):
   * against fp64 math on the same bf16 inputs: max-abs-err <= 2e-2 and
     mean-rel-err <= 1e-3 (sum|a-b| / sum|b|);
   * against the reference's dtype chain (oracle GGML mode): max-abs-err <= 2e-2
