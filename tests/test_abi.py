@@ -60,6 +60,10 @@ def test_create_rejects_bad_config_without_a_device(field, value, status):
 
 def test_null_handle_is_rejected():
     L = nvattn.lib()
+    assert L.nvattn_plan_prefill_device(None, 1, None, None, None, 4, 16, None, None, None, None,
+                                        None, None) == nvattn.ERR_INVALID_ARG
+    assert L.nvattn_plan_decode_device(None, 1, None, None, 4, None, None, None, None) == \
+        nvattn.ERR_INVALID_ARG
     assert L.nvattn_paged_decode(None, 0, 1, None, None, None, None, 1, None, 1, None, None) == \
         nvattn.ERR_INVALID_ARG
     assert L.nvattn_get_error(None, None) == nvattn.ERR_INVALID_ARG
