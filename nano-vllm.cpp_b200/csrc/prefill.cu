@@ -61,7 +61,6 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
   int Hq, Hkv, G, layer, block_size, max_blocks, n_mtiles, pair_heads;
-  int tile_major;  // grid z = (query-tile rank, sequence): longest tiles first overall
   long long n_slots, num_blocks;
   float scale_log2;
   const int32_t* cu_q;
@@ -362,33 +361,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
   // ---- which rows and heads this CTA owns ----
-  // Default grid: x = (tile rank, head pair), y = kv head, z = sequence, so
-  // the CTAs of one (sequence, kv head) run together and share its K/V in
-  // L2.  tile_major grid (small K/V footprints): x = head pair, y = kv head,
-  // z = (tile rank, sequence), so the longest query tiles of every sequence
-  // and kv head start first and the launch ends with short ones.
   Work w;
   w.kvh = blockIdx.y;
-  int rank, gp;  // query-tile rank (0 = longest) and head pair
-  if (prm.tile_major) {
-    const int n_seqs = (int)gridDim.z / (prm.pair_heads ? prm.n_mtiles : (prm.n_mtiles + 1) / 2);
-    w.seq = (int)blockIdx.z % n_seqs;
-    rank = (int)blockIdx.z / n_seqs;
-    gp = (int)blockIdx.x;
-  } else {
-    w.seq = blockIdx.z;
-    const int n_pairs = prm.pair_heads ? prm.G / 2 : 1;
-    rank = (int)(blockIdx.x / n_pairs);
-    gp = (int)(blockIdx.x % n_pairs);
-  }
+  w.seq = blockIdx.z;
   if (prm.pair_heads) {
-    const int mt = prm.n_mtiles - 1 - rank;  // longest tiles first
+    const int n_pairs = prm.G / 2;
+    const int mt = prm.n_mtiles - 1 - (int)(blockIdx.x / n_pairs);  // longest tiles first
+    const int gp = blockIdx.x % n_pairs;
     w.head[0] = w.kvh * prm.G + 2 * gp;
     w.head[1] = w.head[0] + 1;
     w.row0[0] = w.row0[1] = mt * kBM;
   } else {
     const int n_units = (prm.n_mtiles + 1) / 2;
-    const int u = n_units - 1 - rank;
+    const int u = n_units - 1 - (int)blockIdx.x;
     w.head[0] = w.head[1] = w.kvh * prm.G;
     w.row0[0] = 2 * u * kBM;
     w.row0[1] = w.row0[0] + kBM;
@@ -506,25 +491,10 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   prm.out = out;
   prm.status = h->status_dev;
 
-  const long long n_ranks = prm.pair_heads ? prm.n_mtiles : (prm.n_mtiles + 1) / 2;
-  const long long n_pairs = prm.pair_heads ? prm.G / 2 : 1;
-  // K/V of every sequence at the longest context, all kv heads: when it fits
-  // well inside L2 the tile-major order loses no reuse.
-  const long long kv_bytes =
-      (long long)n_seqs * max_blocks * prm.block_size * Hkv * kD * 2 * 2;
-  prm.tile_major = kv_bytes <= (64LL << 20) ? 1 : 0;
-  dim3 grid;
-  if (prm.tile_major) {
-    if (n_pairs > 0x7fffffffLL || Hkv > 65535 || n_ranks * n_seqs > 65535)
-      prm.tile_major = 0;
-    else
-      grid = dim3((unsigned)n_pairs, Hkv, (unsigned)(n_ranks * n_seqs));
-  }
-  if (!prm.tile_major) {
-    const long long gx = n_ranks * n_pairs;
-    if (gx > 0x7fffffffLL || Hkv > 65535 || n_seqs > 65535) return NVATTN_ERR_UNSUPPORTED;
-    grid = dim3((unsigned)gx, Hkv, n_seqs);
-  }
+  const long long gx = prm.pair_heads ? (long long)prm.n_mtiles * (prm.G / 2)
+                                      : (long long)(prm.n_mtiles + 1) / 2;
+  if (gx > 0x7fffffffLL || Hkv > 65535 || n_seqs > 65535) return NVATTN_ERR_UNSUPPORTED;
+  dim3 grid((unsigned)gx, Hkv, n_seqs);
   const size_t smem = sizeof(PrefillSmem) + 1024;
   // The attribute is per device; remember which devices have it.
   static unsigned long long attr_set_mask = 0;
