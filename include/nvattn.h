@@ -213,11 +213,14 @@ NVATTN_API nvattn_status nvattn_schedule_prefill_chunks(
  *    u * sum, n_vocab-1 if none does (a NaN or infinite logit, as in the
  *    reference).  Probabilities are within a few ulp of the reference's.
  * tokens_dev[s] receives the token.  A draw outside [0,1) or unusable
- * history offsets are recorded as NVATTN_ERR_INVALID_ARG (detail = s).
+ * history offsets (decreasing, negative, or 2^30 ids or more for one
+ * sequence) are recorded as NVATTN_ERR_INVALID_ARG (detail = s).
  * n_vocab <= 2,097,152.  The first call for a vocabulary size allocates the
- * handle's sampler workspace (max_seqs * n_vocab * 4 bytes of counts, zero
- * between calls) and cannot be captured (NVATTN_ERR_UNSUPPORTED while the
- * stream captures); later calls are capturable. */
+ * handle's sampler workspace (history count tables of about 4.5 bytes per id
+ * for each of max_seqs rows, plus 64 KiB of piece summaries per row; nothing
+ * in it carries over between calls) and cannot be captured
+ * (NVATTN_ERR_UNSUPPORTED while the stream captures); later calls are
+ * capturable. */
 NVATTN_API nvattn_status nvattn_sample(
     nvattn_handle* h, int n_seqs, int n_vocab, const float* logits_dev, int64_t row_stride,
     const float* temperatures_dev, const float* penalties_dev, const int32_t* history_dev,

@@ -114,12 +114,13 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, 
   }
 }
 
-// History bounds of sequence s, or false if the offsets are unusable.
+// History bounds of sequence s, or false if the offsets are unusable (a
+// history of 2^30 ids or more per sequence included).
 __device__ __forceinline__ bool hist_range(const SampleArgs& a, int s, long long& b,
                                            long long& e) {
   b = a.hist_off[s];
   e = a.hist_off[s + 1];
-  return b >= 0 && e >= b;
+  return b >= 0 && e >= b && e - b < (1LL << 30);
 }
 
 // Rows whose penalty the count kernel prepared.
@@ -219,14 +220,18 @@ __global__ void __launch_bounds__(kCountThreads, 1) sample_count_kernel(SampleAr
     if (threadIdx.x == 0) ov_full = 0;
     __syncthreads();
     constexpr int kBatch = 8;  // independent id loads in flight per thread
-    for (long long j0 = hb; j0 < he; j0 += (long long)kBatch * kCountThreads) {
+    // ids outside [0, n_vocab) are skipped, as the reference does: one
+    // unsigned test covers them and the ids of other segments
+    const uint32_t seg_ids = (uint32_t)min((long long)seg, (long long)a.n_vocab - v0);
+    const int32_t* hs = a.hist + hb;
+    const int n_hist = (int)(he - hb);
+    for (int j0 = 0; j0 < n_hist; j0 += kBatch * kCountThreads) {
       int keys[kBatch];
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
-        const long long j = j0 + (long long)q * kCountThreads + threadIdx.x;
-        const int tok = j < he ? __ldcs(a.hist + j) : -1;
-        // ids outside [0, n_vocab) are skipped, as the reference does
-        keys[q] = tok >= 0 && tok < a.n_vocab && tok >= v0 && tok < v0 + seg ? tok - (int)v0 : -1;
+        const int j = j0 + q * kCountThreads + (int)threadIdx.x;
+        const uint32_t key = j < n_hist ? (uint32_t)(__ldcs(hs + j) - (int)v0) : 0xFFFFFFFFu;
+        keys[q] = key < seg_ids ? (int)key : -1;
       }
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
@@ -262,6 +267,14 @@ __global__ void __launch_bounds__(kCountThreads, 1) sample_count_kernel(SampleAr
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint4 w = src[q];  // ids 32g + 8q .. +7, two per word
+        // The usual group: every count below 15 (the or of the counts below
+        // 16 with a low nibble short of 15): the counts are the low bytes of
+        // the halves.  Otherwise saturate and record exact counts.
+        const uint32_t any = w.x | w.y | w.z | w.w;
+        if (!(any & 0xFFF0FFF0u) && !(((any & 0x000F000Fu) + 0x00010001u) & 0x00100010u)) {
+          out[q] = __byte_perm(w.x, w.y, 0x6420) | (__byte_perm(w.z, w.w, 0x6420) << 4);
+          continue;
+        }
         const uint32_t lo = sat_pair_bytes(w.x) | (sat_pair_bytes(w.y) << 16);
         const uint32_t hi = sat_pair_bytes(w.z) | (sat_pair_bytes(w.w) << 16);
         out[q] = lo | (hi << 4);

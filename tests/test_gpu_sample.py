@@ -68,7 +68,8 @@ def _histories(rng, n, V, max_len, repeat_frac=0.5):
 
 @pytest.mark.parametrize("n,V,stride,seed", [
     (1, QWEN3_VOCAB, None, 0), (37, QWEN3_VOCAB, None, 1), (300, 4097, None, 2),
-    (16, 1000, 1003, 3), (5, 7, None, 4), (8, 4096 * 3, 4096 * 3 + 4, 5)])
+    (16, 1000, 1003, 3), (5, 7, None, 4), (8, 4096 * 3, 4096 * 3 + 4, 5), (3, 1, None, 6),
+    (4, 2, None, 7)])
 def test_greedy_with_penalty_is_bit_exact(n, V, stride, seed):
     rng = np.random.default_rng(seed)
     x = rng.normal(0, 2, (n, V)).astype(np.float32)
@@ -319,3 +320,24 @@ def test_sampler_is_graph_capturable_after_first_call():
         assert h.get_error() == (nvattn.OK, 0)
     finally:
         h.close()
+
+
+@pytest.mark.parametrize("V", [1, 2, 3])
+def test_tiny_vocabularies_sample_like_the_reference(V):
+    """One to three logits per row, temperature rows: with a single finite
+    maximum far above the rest the inverse CDF gives it for any draw."""
+    n = 6
+    x = np.full((n, V), -50.0, np.float32)
+    top = np.arange(n) % V
+    x[np.arange(n), top] = 5.0
+    t = np.full(n, 0.8, np.float32)
+    u = np.linspace(0.05, 0.95, n).astype(np.float32)
+    want = O.sample(x, t, np.ones(n, np.float32), u)
+    h = handle(8, 8, 16)
+    try:
+        got = _run(h, x, t, np.ones(n), u)
+        assert h.get_error() == (nvattn.OK, 0)
+    finally:
+        h.close()
+    np.testing.assert_array_equal(got, want)
+    np.testing.assert_array_equal(got, top)
