@@ -268,7 +268,10 @@ NVATTN_API nvattn_status nvattn_paged_decode(
  * through the block table.  The rows' own K/V must already be stored.
  *   q_dev   [n_tokens][n_q_heads][head_dim] bf16
  *   out_dev [n_tokens][n_q_heads][head_dim] f32
- * max_q_len: host-side upper bound of the per-sequence query count. */
+ * max_q_len: host-side upper bound of the per-sequence query count.
+ * The CTAs take their work from a counter in the handle's workspace, so two
+ * prefill launches on one handle must not run concurrently (issue them on
+ * one stream, as the split-KV workspace of nvattn_paged_decode also needs). */
 NVATTN_API nvattn_status nvattn_paged_prefill(
     nvattn_handle* h, int layer, int n_seqs, int n_tokens,
     const uint16_t* q_dev, const int32_t* cu_q_lens_dev,

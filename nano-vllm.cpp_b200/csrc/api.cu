@@ -187,6 +187,12 @@ nvattn_status nvattn_create(const nvattn_config* cfg, nvattn_handle** out) {
       st = NVATTN_ERR_CUDA;
   }
   if (st == NVATTN_OK) {
+    if (cudaMalloc(&h->prefill_sched_dev, 2 * sizeof(int)) != cudaSuccess)
+      st = NVATTN_ERR_NO_MEMORY;
+    else if (cudaMemset(h->prefill_sched_dev, 0, 2 * sizeof(int)) != cudaSuccess)
+      st = NVATTN_ERR_CUDA;
+  }
+  if (st == NVATTN_OK) {
     // Split-KV workspace: at most 64 splits per (sequence, kv head).
     long long splits = (c.max_context + c.block_size - 1) / c.block_size;
     h->max_splits = (int)(splits < 64 ? splits : 64);
@@ -209,6 +215,7 @@ nvattn_status nvattn_destroy(nvattn_handle* h) {
   DeviceGuard guard(h->cfg.device);
   if (h->rope_table_dev) cudaFree(h->rope_table_dev);
   if (h->status_dev) cudaFree(h->status_dev);
+  if (h->prefill_sched_dev) cudaFree(h->prefill_sched_dev);
   if (h->ws_o) cudaFree(h->ws_o);
   if (h->ws_ml) cudaFree(h->ws_ml);
   if (h->samp_nib) cudaFree(h->samp_nib);

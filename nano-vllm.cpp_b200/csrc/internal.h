@@ -33,6 +33,9 @@ struct nvattn_handle {
 
   float* rope_table_dev = nullptr;  // [max_position][cos x head_dim/2 | sin x head_dim/2]
   nvattn::DeviceStatus* status_dev = nullptr;
+  // prefill work counter: [0] next item, [1] CTAs finished (zero between
+  // launches; the last CTA of each launch zeroes both)
+  int* prefill_sched_dev = nullptr;
 
   // split-KV workspace for decode
   float* ws_o = nullptr;   // [max_seqs][n_kv_heads][max_splits][G][head_dim]

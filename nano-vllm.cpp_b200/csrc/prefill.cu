@@ -15,9 +15,15 @@
 // the F16 V the reference hands to ggml_flash_attn_ext (qwen3.cpp:388-393,
 // including its overflow above 65504).  Accumulation is f32.
 //
-// One CTA owns two 128-row query tiles that read the same keys: the two GQA
+// A work item is two 128-row query tiles that read the same keys: the two GQA
 // heads of a pair (same rows, same kv head), or, when a kv head serves one q
-// head, two consecutive row tiles.  Keys come in 128-key tiles.
+// head, two consecutive row tiles.  Keys come in 128-key tiles.  The kernel
+// is persistent (one CTA per SM): the producer takes items in launch order
+// (query tiles of one sequence and kv head together, longest first) from a
+// counter in the handle's workspace and hands each to the other roles
+// through a 2-slot work ring in shared memory, so the next item's Q, first K
+// tile and first S MMAs overlap the current item's last softmax and epilogue,
+// and items without rows cost one counter step instead of a CTA launch.
 //   warp 0       TMA producer: both Q tiles once, then K(j), V(j), K(j+1) ...
 //                through a ring of 5 x 32 KiB slots (two 64-column boxes per
 //                tile, 128-byte swizzle).
@@ -61,6 +67,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
   int Hq, Hkv, G, layer, block_size, max_blocks, n_mtiles, pair_heads;
+  int gx, n_items;  // items per (sequence, kv head); items in all
   long long n_slots, num_blocks;
   float scale_log2;
   const int32_t* cu_q;
@@ -69,6 +76,14 @@ struct PrefillParams {
   const int32_t* block_tables;
   float* out;
   DeviceStatus* status;
+  int* sched;  // [0] next work item, [1] CTAs finished; the last CTA zeroes both
+};
+
+// One work item (written by the producer, read by every role).  valid == 0
+// ends the CTA's loop.
+struct Work {
+  int valid, seq, kvh, q0, q_start, ctx, n_kv, p_last0;
+  int head[2], row0[2], rows[2];
 };
 
 struct __align__(1024) PrefillSmem {
@@ -79,107 +94,221 @@ struct __align__(1024) PrefillSmem {
   uint64_t s_full[2], p_full[2];
   uint64_t v_ready[2], v_consumed[2];  // by key-tile parity
   uint64_t o_final;
+  uint64_t q_empty;                      // the item's last S MMAs have read Q
+  uint64_t work_full[2], work_empty[2];  // the work ring
+  Work work[2];
   uint32_t tmem_base;
   int abort_flag;  // raised by the first wait that times out
 };
 
-// What one CTA works on (computed identically by every thread).
-struct Work {
-  int seq, kvh, q0, q_start, ctx, n_kv, p_last0;
-  int head[2], row0[2], rows[2];
-};
+// Dynamic shared memory (+1 KiB for the 1024-byte alignment) within the
+// 227 KiB a CTA may use.
+static_assert(sizeof(PrefillSmem) + 1024 <= 227 * 1024, "prefill shared memory");
+
+// Arrivals that release a work-ring slot: the MMA lane, the 4 converter warps
+// and the 8 softmax warps.
+constexpr int kWorkReaders = 1 + 4 + 8;
 
 __device__ __forceinline__ int ring_slot(int idx) { return idx % kSlots; }
 __device__ __forceinline__ uint32_t ring_parity(int idx) { return (uint32_t)(idx / kSlots) & 1u; }
 
+// ---------------------------------------------------------------- work items
+// Item `item` in launch order: x fastest, then kv head, then sequence, as a
+// gx x Hkv x n_seqs grid.  Returns false for an item without query rows or
+// with invalid metadata (the latter recorded in the status word).  The items
+// without rows of a (sequence, kv head) are its first x values (longest
+// tiles first); for one of them `skip_to` is the group's first item with rows
+// (or the next group), so the caller can move the counter past the rest.
+__device__ __forceinline__ bool decode_item(const PrefillParams& prm, int item, Work& w,
+                                            int& skip_to) {
+  const int x = item % prm.gx;
+  const int yz = item / prm.gx;
+  w.kvh = yz % prm.Hkv;
+  w.seq = yz / prm.Hkv;
+  if (prm.pair_heads) {
+    const int n_pairs = prm.G / 2;
+    const int mt = prm.n_mtiles - 1 - x / n_pairs;  // longest tiles first
+    const int gp = x % n_pairs;
+    w.head[0] = w.kvh * prm.G + 2 * gp;
+    w.head[1] = w.head[0] + 1;
+    w.row0[0] = w.row0[1] = mt * kBM;
+  } else {
+    const int n_units = (prm.n_mtiles + 1) / 2;
+    const int u = n_units - 1 - x;
+    w.head[0] = w.head[1] = w.kvh * prm.G;
+    w.row0[0] = 2 * u * kBM;
+    w.row0[1] = w.row0[0] + kBM;
+  }
+  w.q0 = prm.cu_q[w.seq];
+  const int n_q = prm.cu_q[w.seq + 1] - w.q0;
+  if (n_q > prm.n_mtiles * kBM && x == 0 && w.kvh == 0)
+    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 21, n_q);
+  skip_to = item + 1;
+  if (w.row0[0] >= n_q) {
+    int x_first = prm.gx;
+    if (n_q > 0)
+      x_first = prm.pair_heads
+                    ? (prm.n_mtiles - 1 - (n_q - 1) / kBM) * (prm.G / 2)
+                    : (prm.n_mtiles + 1) / 2 - 1 - (n_q - 1) / (2 * kBM);
+    skip_to = item - x + max(x_first, x + 1);
+    return false;
+  }
+  w.q_start = prm.q_starts[w.seq];
+  w.rows[0] = min(kBM, n_q - w.row0[0]);
+  w.rows[1] = max(0, min(kBM, n_q - w.row0[1]));
+  w.p_last0 = w.q_start + w.row0[0] + w.rows[0] - 1;
+  const int p_last =
+      w.rows[1] > 0 ? max(w.p_last0, w.q_start + w.row0[1] + w.rows[1] - 1) : w.p_last0;
+  if (w.q_start < 0 || (long long)p_last >= (long long)prm.max_blocks * prm.block_size) {
+    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 22, p_last);
+    return false;
+  }
+  w.ctx = prm.context_lens[w.seq];
+  if (w.ctx <= p_last) {
+    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 23, w.ctx);
+    w.ctx = p_last + 1;
+  }
+  w.n_kv = p_last / kBN + 1;
+  w.valid = 1;
+  return true;
+}
+
+// Every role runs the same sequence of items, so each keeps the CTA-wide
+// count of key tiles before the current item (`tb`): key tile j of the item
+// is tile gj = tb + j, its K and V are ring loads 2*gj and 2*gj + 1, and the
+// per-tile barriers are in phase gj.
+
 // ---------------------------------------------------------------- producer
 __device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap* tm_q,
                                               const CUtensorMap* tm_k, const CUtensorMap* tm_v,
-                                              const PrefillParams& prm, const Work& w) {
+                                              const PrefillParams& prm) {
   volatile int* abort_flag = &sm.abort_flag;
   tma_prefetch_desc(tm_q);
   tma_prefetch_desc(tm_k);
   tma_prefetch_desc(tm_v);
-  mbar_arrive_expect_tx(&sm.q_full, 4 * kHalfBytes);
-  for (int t = 0; t < 2; ++t) {
-    tma_load_3d(sm.q[t][0], tm_q, &sm.q_full, 0, w.head[t], w.q0 + w.row0[t]);
-    tma_load_3d(sm.q[t][1], tm_q, &sm.q_full, 64, w.head[t], w.q0 + w.row0[t]);
-  }
-  const int n_loads = 2 * w.n_kv;
-  long long bid = 0;
-  for (int idx = 0; idx < n_loads; ++idx) {
-    const int slot = ring_slot(idx);
-    if (idx >= kSlots)
-      mbar_wait(&sm.empty[slot], ring_parity(idx) ^ 1u, prm.status, abort_flag, 30);
-    const int key0 = (idx >> 1) * kBN;
-    if ((idx & 1) == 0) {
-      bid = prm.block_tables[(long long)w.seq * prm.max_blocks + key0 / prm.block_size];
-      if (bid < 0 || bid >= prm.num_blocks) {
-        record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 24, bid);
-        bid = 0;
-      }
+  int g = 0;  // ring loads issued so far
+  for (int k = 0;; ++k) {
+    const int ws = k & 1;
+    if (k >= 2 && !mbar_wait(&sm.work_empty[ws], ((k >> 1) - 1) & 1, prm.status, abort_flag, 45))
+      break;
+    Work& w = sm.work[ws];
+    w.valid = 0;
+    // An earlier launch that timed out leaves its status: take no work then.
+    while (!*abort_flag && !timeout_recorded(prm.status)) {
+      const int item = atomicAdd(prm.sched, 1);
+      int skip_to;
+      if (item >= prm.n_items || decode_item(prm, item, w, skip_to)) break;
+      // Items in (item, skip_to) are empty: nobody needs to take them.
+      if (skip_to > item + 1) atomicMax(prm.sched, skip_to);
     }
-    const int row = (int)((long long)prm.layer * prm.n_slots + bid * prm.block_size +
-                          key0 % prm.block_size);
-    const CUtensorMap* map = (idx & 1) ? tm_v : tm_k;
-    mbar_arrive_expect_tx(&sm.full[slot], 2 * kHalfBytes);
-    tma_load_3d(sm.kv[slot][0], map, &sm.full[slot], 0, w.kvh, row);
-    tma_load_3d(sm.kv[slot][1], map, &sm.full[slot], 64, w.kvh, row);
+    mbar_arrive(&sm.work_full[ws]);
+    if (!w.valid) break;
+    // Q of the previous item is free once its last S MMAs have completed.
+    if (k >= 1) mbar_wait(&sm.q_empty, (k - 1) & 1, prm.status, abort_flag, 46);
+    mbar_arrive_expect_tx(&sm.q_full, 4 * kHalfBytes);
+    for (int t = 0; t < 2; ++t) {
+      tma_load_3d(sm.q[t][0], tm_q, &sm.q_full, 0, w.head[t], w.q0 + w.row0[t]);
+      tma_load_3d(sm.q[t][1], tm_q, &sm.q_full, 64, w.head[t], w.q0 + w.row0[t]);
+    }
+    const int n_loads = 2 * w.n_kv;
+    long long bid = 0;
+    for (int i = 0; i < n_loads; ++i) {
+      const int idx = g + i;
+      const int slot = ring_slot(idx);
+      if (idx >= kSlots)
+        mbar_wait(&sm.empty[slot], ring_parity(idx) ^ 1u, prm.status, abort_flag, 30);
+      const int key0 = (i >> 1) * kBN;
+      if ((i & 1) == 0) {
+        bid = prm.block_tables[(long long)w.seq * prm.max_blocks + key0 / prm.block_size];
+        if (bid < 0 || bid >= prm.num_blocks) {
+          record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 24, bid);
+          bid = 0;
+        }
+      }
+      const int row = (int)((long long)prm.layer * prm.n_slots + bid * prm.block_size +
+                            key0 % prm.block_size);
+      const CUtensorMap* map = (i & 1) ? tm_v : tm_k;
+      mbar_arrive_expect_tx(&sm.full[slot], 2 * kHalfBytes);
+      tma_load_3d(sm.kv[slot][0], map, &sm.full[slot], 0, w.kvh, row);
+      tma_load_3d(sm.kv[slot][1], map, &sm.full[slot], 64, w.kvh, row);
+    }
+    g += n_loads;
   }
   // Drain: the last load of every slot has landed before the CTA can exit
   // (immediate in normal operation; bounded after an abort).
-  for (int idx = max(0, n_loads - kSlots); idx < n_loads; ++idx)
+  for (int idx = max(0, g - kSlots); idx < g; ++idx)
     mbar_wait(&sm.full[ring_slot(idx)], ring_parity(idx), prm.status, 40);
 }
 
+// Takes the next item from the work ring (every lane of a warp calls it; lane
+// 0 releases the slot).  Returns false when the CTA's work is over.
+__device__ __forceinline__ bool next_work(PrefillSmem& sm, const PrefillParams& prm, int k,
+                                          int lane, Work& w, int site) {
+  const int ws = k & 1;
+  if (!mbar_wait(&sm.work_full[ws], (k >> 1) & 1, prm.status, &sm.abort_flag, site)) return false;
+  w = sm.work[ws];
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&sm.work_empty[ws]);
+  return w.valid != 0;
+}
+
 // ---------------------------------------------------------------- V converters
-// Tile j is converted only after P.V of tile j-2 has finished, so each
+// Tile gj is converted only after P.V of tile gj-2 has finished, so each
 // barrier of a parity pair runs at most one phase ahead of its waiter.
-__device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillParams& prm,
-                                               const Work& w, int c) {
+__device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillParams& prm, int c) {
   volatile int* abort_flag = &sm.abort_flag;
   const int lane = c & 31;
-  for (int j = 0; j < w.n_kv; ++j) {
-    const int b = j & 1;
-    if (j >= 2) mbar_wait(&sm.v_consumed[b], ((j >> 1) - 1) & 1, prm.status, abort_flag, 43);
-    const int vidx = 2 * j + 1;
-    const int slot = ring_slot(vidx);
-    mbar_wait(&sm.full[slot], ring_parity(vidx), prm.status, abort_flag, 44);
-    const int key0 = j * kBN;
-    // 2048 16-byte chunks: half h = f / 1024, key row = (f % 1024) / 8.
-    // Consecutive threads touch consecutive chunks (no bank conflicts).
-#pragma unroll 4
-    for (int f = c; f < 2 * 128 * 8; f += kConvThreads) {
-      const int half = f >> 10, key = (f & 1023) >> 3;
-      uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.kv[slot][half]) +
-                                          (f & 1023) * 16);
-      uint4 v = *p;
-      if (key0 + key < w.ctx) {
-        v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
-        v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
-        v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
-        v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
-      } else {
-        v = make_uint4(0, 0, 0, 0);
-      }
-      *p = v;
-    }
-    fence_proxy_async_smem();
+  int tb = 0;
+  for (int k = 0;; ++k) {
+    // Only the key count and the context length are needed here.
+    const int ws = k & 1;
+    if (!mbar_wait(&sm.work_full[ws], (k >> 1) & 1, prm.status, abort_flag, 49)) break;
+    const int valid = sm.work[ws].valid, n_kv = sm.work[ws].n_kv, ctx = sm.work[ws].ctx;
     __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.v_ready[b]);
+    if (lane == 0) mbar_arrive(&sm.work_empty[ws]);
+    if (!valid) break;
+    for (int j = 0; j < n_kv; ++j) {
+      const int gj = tb + j;
+      const int b = gj & 1;
+      if (gj >= 2) mbar_wait(&sm.v_consumed[b], ((gj >> 1) - 1) & 1, prm.status, abort_flag, 43);
+      const int vidx = 2 * gj + 1;
+      const int slot = ring_slot(vidx);
+      mbar_wait(&sm.full[slot], ring_parity(vidx), prm.status, abort_flag, 44);
+      const int key0 = j * kBN;
+      // 2048 16-byte chunks: half h = f / 1024, key row = (f % 1024) / 8.
+      // Consecutive threads touch consecutive chunks (no bank conflicts).
+#pragma unroll 4
+      for (int f = c; f < 2 * 128 * 8; f += kConvThreads) {
+        const int half = f >> 10, key = (f & 1023) >> 3;
+        uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.kv[slot][half]) +
+                                            (f & 1023) * 16);
+        uint4 v = *p;
+        if (key0 + key < ctx) {
+          v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
+          v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
+          v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
+          v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
+        } else {
+          v = make_uint4(0, 0, 0, 0);
+        }
+        *p = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.v_ready[b]);
+    }
+    tb += n_kv;
   }
 }
 
 // ---------------------------------------------------------------- MMA issuer
 __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
-                                         const PrefillParams& prm, const Work& w) {
+                                         const PrefillParams& prm) {
   volatile int* abort_flag = &sm.abort_flag;
   constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kBM, kBN, 0, 0);
   constexpr uint32_t idesc_o = umma_idesc_f16_f32(kBM, kD, 0, 1);
-  const int n_kv = w.n_kv;
-  mbar_wait(&sm.q_full, 0, prm.status, abort_flag, 31);
-  auto issue_s = [&](int t, int j) {
-    const int slot = ring_slot(2 * j);
+  auto issue_s = [&](int t, int gj) {
+    const int slot = ring_slot(2 * gj);
 #pragma unroll
     for (int k = 0; k < kD / 16; ++k) {
       const uint32_t koff = (uint32_t)(k & 3) * 32;
@@ -188,54 +317,70 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
       umma_bf16(tmem + t * 256, a, b, idesc_s, k > 0 ? 1u : 0u);
     }
   };
-  auto issue_pv = [&](int t, int j) {
-    const uint32_t vbase = smem_u32(sm.kv[ring_slot(2 * j + 1)][0]);
+  auto issue_pv = [&](int t, int gj, bool accumulate) {
+    const uint32_t vbase = smem_u32(sm.kv[ring_slot(2 * gj + 1)][0]);
 #pragma unroll
     for (int k = 0; k < kBN / 16; ++k) {
       const uint64_t b = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kHalfBytes, 1024);
       umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, b, idesc_o,
-                   (j > 0 || k > 0) ? 1u : 0u);
+                   (accumulate || k > 0) ? 1u : 0u);
     }
   };
-  mbar_wait(&sm.full[ring_slot(0)], ring_parity(0), prm.status, abort_flag, 32);
-  tc_fence_after();
-  issue_s(0, 0);
-  umma_commit(&sm.s_full[0]);
-  issue_s(1, 0);
-  umma_commit(&sm.s_full[1]);
-  umma_commit(&sm.empty[ring_slot(0)]);
-  for (int j = 0; j < n_kv; ++j) {
-    const int vidx = 2 * j + 1, kidx = 2 * j + 2;
-    mbar_wait(&sm.v_ready[j & 1], (j >> 1) & 1, prm.status, abort_flag, 33);
-    mbar_wait(&sm.p_full[0], j & 1, prm.status, abort_flag, 34);
+  int tb = 0, k = 0;
+  for (;; ++k) {
+    const int ws = k & 1;
+    if (!mbar_wait(&sm.work_full[ws], (k >> 1) & 1, prm.status, abort_flag, 48)) break;
+    const int valid = sm.work[ws].valid, n_kv = sm.work[ws].n_kv;
+    mbar_arrive(&sm.work_empty[ws]);
+    if (!valid) break;
+    mbar_wait(&sm.q_full, k & 1, prm.status, abort_flag, 31);
+    mbar_wait(&sm.full[ring_slot(2 * tb)], ring_parity(2 * tb), prm.status, abort_flag, 32);
     tc_fence_after();
-    issue_pv(0, j);
-    if (j + 1 < n_kv) {
-      mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 35);
+    // S_t(0) overwrites the S/P columns of the previous item: its P.V MMAs
+    // were issued before and execute first.  Its O columns are rewritten by
+    // the first P.V below, which waits for P_t(0), i.e. for the softmax warps
+    // to have read the previous O out in their epilogue.
+    issue_s(0, tb);
+    umma_commit(&sm.s_full[0]);
+    issue_s(1, tb);
+    umma_commit(&sm.s_full[1]);
+    umma_commit(&sm.empty[ring_slot(2 * tb)]);
+    if (n_kv == 1) umma_commit(&sm.q_empty);
+    for (int j = 0; j < n_kv; ++j) {
+      const int gj = tb + j;
+      const int vidx = 2 * gj + 1, kidx = 2 * gj + 2;
+      mbar_wait(&sm.v_ready[gj & 1], (gj >> 1) & 1, prm.status, abort_flag, 33);
+      mbar_wait(&sm.p_full[0], gj & 1, prm.status, abort_flag, 34);
       tc_fence_after();
-      issue_s(0, j + 1);
-      umma_commit(&sm.s_full[0]);
+      issue_pv(0, gj, j > 0);
+      if (j + 1 < n_kv) {
+        mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 35);
+        tc_fence_after();
+        issue_s(0, gj + 1);
+        umma_commit(&sm.s_full[0]);
+      }
+      mbar_wait(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
+      tc_fence_after();
+      issue_pv(1, gj, j > 0);
+      umma_commit(&sm.v_consumed[gj & 1]);
+      umma_commit(&sm.empty[ring_slot(vidx)]);
+      if (j + 1 < n_kv) {
+        issue_s(1, gj + 1);
+        umma_commit(&sm.s_full[1]);
+        umma_commit(&sm.empty[ring_slot(kidx)]);
+        if (j + 2 == n_kv) umma_commit(&sm.q_empty);
+      }
     }
-    mbar_wait(&sm.p_full[1], j & 1, prm.status, abort_flag, 36);
-    tc_fence_after();
-    issue_pv(1, j);
-    umma_commit(&sm.v_consumed[j & 1]);
-    umma_commit(&sm.empty[ring_slot(vidx)]);
-    if (j + 1 < n_kv) {
-      issue_s(1, j + 1);
-      umma_commit(&sm.s_full[1]);
-      umma_commit(&sm.empty[ring_slot(kidx)]);
-    }
+    umma_commit(&sm.o_final);
+    tb += n_kv;
   }
-  umma_commit(&sm.o_final);
   // Drain: every MMA has completed before TMEM is released.
-  mbar_wait(&sm.o_final, 0, prm.status, 42);
+  if (k > 0) mbar_wait(&sm.o_final, (k - 1) & 1, prm.status, 42);
 }
 
 // ---------------------------------------------------------------- softmax
 __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
-                                             const PrefillParams& prm, const Work& w, int warp,
-                                             int lane) {
+                                             const PrefillParams& prm, int warp, int lane) {
   volatile int* abort_flag = &sm.abort_flag;
   const int t = (warp - 4) >> 2;  // query tile
   const int quad = warp & 3;      // TMEM lanes [32*quad, 32*quad+32)
@@ -243,111 +388,120 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
   const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
   const uint32_t s_col = tmem + lane_off + t * 256;
   const uint32_t o_col = s_col + 128;
-  const int my_rows = t ? w.rows[1] : w.rows[0];
-  const int my_row0 = t ? w.row0[1] : w.row0[0];
-  const int my_head = t ? w.head[1] : w.head[0];
-  // Rows past the end of the sequence mimic a real row (never stored).
-  const int pos_row = my_rows > 0 ? w.q_start + my_row0 + min(row, my_rows - 1) : w.p_last0;
-  const int vis_last = min(pos_row, w.ctx - 1);  // last visible key
   const float sc = prm.scale_log2;
   const uint64_t sc2 = pack2(sc, sc);
-  float m_used = -INFINITY;
-  float l = 0.0f;
+  int tb = 0;
+  Work w;
+  for (int k = 0; next_work(sm, prm, k, lane, w, 47); ++k) {
+    const int my_rows = t ? w.rows[1] : w.rows[0];
+    const int my_row0 = t ? w.row0[1] : w.row0[0];
+    const int my_head = t ? w.head[1] : w.head[0];
+    // Rows past the end of the sequence mimic a real row (never stored).
+    const int pos_row = my_rows > 0 ? w.q_start + my_row0 + min(row, my_rows - 1) : w.p_last0;
+    const int vis_last = min(pos_row, w.ctx - 1);  // last visible key
+    float* dst = prm.out + ((long long)(w.q0 + my_row0 + row) * prm.Hq + my_head) * kD;
+    const int n_kv = w.n_kv, tb0 = tb;
+    tb += n_kv;
+    float m_used = -INFINITY;
+    float l = 0.0f;
 
-  for (int j = 0; j < w.n_kv; ++j) {
-    mbar_wait(&sm.s_full[t], j & 1, prm.status, abort_flag, 37);
+    for (int j = 0; j < n_kv; ++j) {
+      const int gj = tb0 + j;
+      mbar_wait(&sm.s_full[t], gj & 1, prm.status, abort_flag, 37);
+      tc_fence_after();
+      uint32_t sr[kBN];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      tmem_wait_ld();
+
+      const int lim = vis_last - j * kBN;  // keys c <= lim are visible
+      // Warp-uniform: the paths below end in tcgen05.st, a warp-collective
+      // instruction that every lane of the warp must execute together.
+      const bool masked = __any_sync(0xffffffffu, lim < kBN - 1);
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < kBN; ++c)
+          if (c > lim) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float mx[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) mx[a] = __uint_as_float(sr[a]);
+#pragma unroll
+      for (int c = 4; c < kBN; c += 2)
+        mx[(c >> 1) & 3] =
+            fmax3(mx[(c >> 1) & 3], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+      const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sc;
+      const float m_new = fmaxf(m_used, tile_max);
+      float alpha = 1.0f;
+      bool rescale = false;
+      if (m_new > m_used + kRescaleThreshold) {
+        alpha = fast_exp2(m_used - m_new);
+        rescale = j > 0;
+        m_used = m_new;
+      }
+      // p = 2^(s*sc - m) in f32 pairs (ex2.approx on the XU port), stored as
+      // f16.  An FMA-pipe polynomial for a share of the pairs was measured
+      // slower: the softmax is issue-bound, and the polynomial costs about six
+      // issue slots per element against one.
+      const uint64_t nm2 = pack2(-m_used, -m_used);
+      uint64_t sum2 = pack2(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 packed columns
+        uint32_t ph[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c * 32 + 2 * i]),
+                                          __uint_as_float(sr[c * 32 + 2 * i + 1])),
+                                    sc2, nm2);
+          float x0, x1;
+          unpack2(x2, x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          sum2 = fadd2(sum2, pack2(p0, p1));
+          ph[i] = cvt_f16x2(p0, p1);
+        }
+        tmem_st16(s_col + c * 16, ph);
+      }
+      float s0, s1;
+      unpack2(sum2, s0, s1);
+      l = l * alpha + (s0 + s1);
+
+      // O_t: the completion of S_t(j) implies PV_t(j-1) has completed.
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_col + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_col + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[t]);
+    }
+
+    // ---- epilogue: O_t / l.  The next item's first P.V (which rewrites O_t)
+    // is issued only after this warp's next P_t arrival, i.e. after these
+    // loads have completed.
+    mbar_wait(&sm.o_final, k & 1, prm.status, abort_flag, 39);
     tc_fence_after();
-    uint32_t sr[kBN];
+    const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
-      tmem_ld32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-    tmem_wait_ld();
-
-    const int lim = vis_last - j * kBN;  // keys c <= lim are visible
-    // Warp-uniform: the paths below end in tcgen05.st, a warp-collective
-    // instruction that every lane of the warp must execute together.
-    const bool masked = __any_sync(0xffffffffu, lim < kBN - 1);
-    if (masked) {
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      tmem_ld32(o_col + c * 32, o);
+      tmem_wait_ld();
+      if (row < my_rows) {
 #pragma unroll
-      for (int c = 0; c < kBN; ++c)
-        if (c > lim) sr[c] = __float_as_uint(-INFINITY);
-    }
-    float mx[4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a) mx[a] = __uint_as_float(sr[a]);
-#pragma unroll
-    for (int c = 4; c < kBN; c += 2)
-      mx[(c >> 1) & 3] =
-          fmax3(mx[(c >> 1) & 3], __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
-    const float tile_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sc;
-    const float m_new = fmaxf(m_used, tile_max);
-    float alpha = 1.0f;
-    bool rescale = false;
-    if (m_new > m_used + kRescaleThreshold) {
-      alpha = fast_exp2(m_used - m_new);
-      rescale = j > 0;
-      m_used = m_new;
-    }
-    // p = 2^(s*sc - m) in f32 pairs (ex2.approx on the XU port), stored as
-    // f16.  An FMA-pipe polynomial for a share of the pairs was measured
-    // slower: the softmax is issue-bound, and the polynomial costs about six
-    // issue slots per element against one.
-    const uint64_t nm2 = pack2(-m_used, -m_used);
-    uint64_t sum2 = pack2(0.0f, 0.0f);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 packed columns
-      uint32_t ph[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c * 32 + 2 * i]),
-                                        __uint_as_float(sr[c * 32 + 2 * i + 1])),
-                                  sc2, nm2);
-        float x0, x1;
-        unpack2(x2, x0, x1);
-        const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-        sum2 = fadd2(sum2, pack2(p0, p1));
-        ph[i] = cvt_f16x2(p0, p1);
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(dst + c * 32 + i) =
+              make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
+                          __uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
       }
-      tmem_st16(s_col + c * 16, ph);
-    }
-    float s0, s1;
-    unpack2(sum2, s0, s1);
-    l = l * alpha + (s0 + s1);
-
-    // O_t: the completion of S_t(j) implies PV_t(j-1) has completed.
-    if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(o_col + c * 32, o);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-        tmem_st32(o_col + c * 32, o);
-      }
-    }
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.p_full[t]);
-  }
-
-  // ---- epilogue ----
-  mbar_wait(&sm.o_final, 0, prm.status, abort_flag, 39);
-  tc_fence_after();
-  const float inv_l = l > 0.0f ? 1.0f / l : 0.0f;
-  float* dst = prm.out + ((long long)(w.q0 + my_row0 + row) * prm.Hq + my_head) * kD;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t o[32];
-    tmem_ld32(o_col + c * 32, o);
-    tmem_wait_ld();
-    if (row < my_rows) {
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(dst + c * 32 + i) =
-            make_float4(__uint_as_float(o[i]) * inv_l, __uint_as_float(o[i + 1]) * inv_l,
-                        __uint_as_float(o[i + 2]) * inv_l, __uint_as_float(o[i + 3]) * inv_l);
     }
   }
 }
@@ -360,50 +514,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
-  // ---- which rows and heads this CTA owns ----
-  Work w;
-  w.kvh = blockIdx.y;
-  w.seq = blockIdx.z;
-  if (prm.pair_heads) {
-    const int n_pairs = prm.G / 2;
-    const int mt = prm.n_mtiles - 1 - (int)(blockIdx.x / n_pairs);  // longest tiles first
-    const int gp = blockIdx.x % n_pairs;
-    w.head[0] = w.kvh * prm.G + 2 * gp;
-    w.head[1] = w.head[0] + 1;
-    w.row0[0] = w.row0[1] = mt * kBM;
-  } else {
-    const int n_units = (prm.n_mtiles + 1) / 2;
-    const int u = n_units - 1 - (int)blockIdx.x;
-    w.head[0] = w.head[1] = w.kvh * prm.G;
-    w.row0[0] = 2 * u * kBM;
-    w.row0[1] = w.row0[0] + kBM;
-  }
-  w.q0 = prm.cu_q[w.seq];
-  const int n_q = prm.cu_q[w.seq + 1] - w.q0;
-  if (n_q > prm.n_mtiles * kBM && threadIdx.x == 0 && blockIdx.x == 0 && w.kvh == 0)
-    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 21, n_q);
-  if (w.row0[0] >= n_q) return;  // whole CTA: nothing to do
-  if (timeout_recorded(prm.status)) return;
-  w.q_start = prm.q_starts[w.seq];
-  w.rows[0] = min(kBM, n_q - w.row0[0]);
-  w.rows[1] = max(0, min(kBM, n_q - w.row0[1]));
-  w.p_last0 = w.q_start + w.row0[0] + w.rows[0] - 1;
-  const int p_last =
-      w.rows[1] > 0 ? max(w.p_last0, w.q_start + w.row0[1] + w.rows[1] - 1) : w.p_last0;
-  if (w.q_start < 0 || (long long)p_last >= (long long)prm.max_blocks * prm.block_size) {
-    if (threadIdx.x == 0) record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 22, p_last);
-    return;
-  }
-  w.ctx = prm.context_lens[w.seq];
-  if (w.ctx <= p_last) {
-    if (threadIdx.x == 0) record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 23, w.ctx);
-    w.ctx = p_last + 1;
-  }
-  w.n_kv = p_last / kBN + 1;
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
@@ -413,6 +527,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.p_full[t], 4);
       mbar_init(&sm.v_ready[t], kConvThreads / 32);
       mbar_init(&sm.v_consumed[t], 1);
+      mbar_init(&sm.work_full[t], 1);
+      mbar_init(&sm.work_empty[t], kWorkReaders);
     }
     mbar_init(&sm.o_final, 1);
     sm.abort_flag = 0;
@@ -428,18 +544,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
   // 512 threads x 128 registers at launch: warpgroup 0 (TMA, MMA) gives back
-  // down to 88, warpgroup 3 (converters) to 40, the two softmax warpgroups
-  // take 192 each (128*88 + 128*40 + 256*192 = 65536 = 512*128).
+  // down to 96, warpgroup 3 (converters) to 40, the two softmax warpgroups
+  // take 184 each (128*96 + 128*40 + 256*184 = 64512 <= 65536 = 512*128).
   if (warp < 4) {
-    regs_dec<88>();
-    if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm, w);
-    if (warp == 1 && lane == 0) mma_role(sm, tmem, prm, w);
+    regs_dec<96>();
+    if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm);
+    if (warp == 1 && lane == 0) mma_role(sm, tmem, prm);
   } else if (warp >= 12) {
     regs_dec<40>();
-    converter_role(sm, prm, w, threadIdx.x - 384);
+    converter_role(sm, prm, threadIdx.x - 384);
   } else {
-    regs_inc<192>();
-    softmax_role(sm, tmem, prm, w, warp, lane);
+    regs_inc<184>();
+    softmax_role(sm, tmem, prm, warp, lane);
   }
 
   tc_fence_before();
@@ -447,6 +563,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+  // The last CTA to finish zeroes the work counter for the next launch
+  // (every CTA has taken its last item before it counts itself finished).
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&prm.sched[1], 1) == (int)gridDim.x - 1) {
+      atomicExch(&prm.sched[0], 0);
+      atomicExch(&prm.sched[1], 0);
+    }
   }
 }
 
@@ -490,11 +615,18 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   prm.block_tables = block_tables;
   prm.out = out;
   prm.status = h->status_dev;
+  prm.sched = h->prefill_sched_dev;
 
   const long long gx = prm.pair_heads ? (long long)prm.n_mtiles * (prm.G / 2)
                                       : (long long)(prm.n_mtiles + 1) / 2;
-  if (gx > 0x7fffffffLL || Hkv > 65535 || n_seqs > 65535) return NVATTN_ERR_UNSUPPORTED;
-  dim3 grid((unsigned)gx, Hkv, n_seqs);
+  const long long n_items = gx * Hkv * (long long)n_seqs;
+  if (n_items <= 0) return NVATTN_OK;
+  // The counter overshoots n_items by at most one step per CTA.
+  if (n_items > 0x7fffffffLL - h->sm_count) return NVATTN_ERR_UNSUPPORTED;
+  prm.gx = (int)gx;
+  prm.n_items = (int)n_items;
+  // Persistent: one CTA per SM (the shared-memory footprint allows no more).
+  const int grid = (int)std::min<long long>(n_items, h->sm_count);
   const size_t smem = sizeof(PrefillSmem) + 1024;
   // The attribute is per device; remember which devices have it.
   static unsigned long long attr_set_mask = 0;
