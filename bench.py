@@ -49,7 +49,7 @@ NCU_TRAFFIC_BYTES_N1 = 11.096e9
 # sm__pipe_tensor_cycles_active of paged_prefill_kernel, fraction of elapsed
 # cycles, from a full ncu capture of the chunk shape (2 x 2048 new tokens at
 # [30720, 32768), 32B heads).
-NCU_PREFILL_TENSOR_ACTIVE = 0.533
+NCU_PREFILL_TENSOR_ACTIVE = 0.543
 
 
 def log(*a):
