@@ -24,9 +24,10 @@
 // through a 2-slot work ring in shared memory, so the next item's Q, first K
 // tile and first S MMAs overlap the current item's last softmax and epilogue,
 // and items without rows cost one counter step instead of a CTA launch.
-//   warp 0       TMA producer: both Q tiles once, then K(j), V(j), K(j+1) ...
-//                through a ring of 5 x 32 KiB slots (two 64-column boxes per
-//                tile, 128-byte swizzle).
+//   warp 0       work items from the counter; TMA producer: per item both Q
+//                tiles, then K(j), V(j), K(j+1) ... through a ring of
+//                5 x 32 KiB slots (two 64-column boxes per tile, 128-byte
+//                swizzle) that runs on across items.
 //   warp 1       TMEM allocation; one lane issues the MMAs, interleaving the
 //                two tiles so the tensor core works on one tile while the
 //                other tile's softmax runs:
