@@ -47,9 +47,10 @@ SEED = 0
 NCU_TRAFFIC_BYTES_N1 = 11.096e9
 
 # sm__pipe_tensor_cycles_active of paged_prefill_kernel, fraction of elapsed
-# cycles, from a full ncu capture of the chunk shape (2 x 2048 new tokens at
-# [30720, 32768), 32B heads).
+# cycles, from full ncu captures: the chunk shape (2 x 2048 new tokens at
+# [30720, 32768), 32B heads) and the prefix-hit workload itself.
 NCU_PREFILL_TENSOR_ACTIVE = 0.543
+NCU_PREFIX_HIT_TENSOR_ACTIVE = 0.366
 
 
 def log(*a):
@@ -691,11 +692,13 @@ def run_prefills(args, world, rank, device):
                          "frac": achieved / tflops_peak, "peak_source": peak_kind,
                          "prefill_ms": pre_ms, "frac_of_2250_nominal": achieved / 2250.0},
         })
-        # tensor-pipe utilisation from an ncu capture of this kernel on the
-        # chunk shape (sm__pipe_tensor_cycles_active, fraction of elapsed
-        # cycles); null for other shapes
+        # tensor-pipe utilisation from an ncu capture of this kernel
+        # (sm__pipe_tensor_cycles_active, fraction of elapsed cycles) on the
+        # chunk shape or the prefix-hit workload; null for other shapes
+        wl = fields["workload"]
         fields["roofline"]["ncu_tensor_pipe_active"] = (
-            NCU_PREFILL_TENSOR_ACTIVE if fields["workload"].startswith("chunked_prefill") else None)
+            NCU_PREFILL_TENSOR_ACTIVE if wl.startswith("chunked_prefill")
+            else NCU_PREFIX_HIT_TENSOR_ACTIVE if wl.startswith("prefill_prefix_hit") else None)
         # the dense BF16 tensor rate at the SM clock sampled during the run
         # (148 SMs x 8192 FLOP per cycle; 2.25 PFLOP/s is this at ~1.86 GHz)
         mhz = (fields.get("clocks") or {}).get("sm_mhz")
