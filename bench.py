@@ -193,12 +193,33 @@ def bench_prefill(kind, args, world, rank, device):
     # algorithmic causal FLOPs (whole job, all heads): 4*d*Hq per visible (q, k) pair
     pairs = sum(int(((np.arange(qs[s], cl[s]) + 1)).sum()) for s in range(len(lens)))
     flops = 4.0 * D * Hq * pairs
+    cpu = None
+    if kind == "prefix_hit" and world == 1 and rank == 0 and not args.no_cpu_baseline:
+        # the same prefill (the cache as the last step left it) on the host
+        # cores: the oracle's restatement of the reference's dtype chain
+        # (bf16 K -> f16, f32 scores and softmax, f16 V accumulator)
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        cores = os.cpu_count() or 1
+        p = O.params(n_q_heads=hq, n_kv_heads=hkv, n_slots=n_slots, n_threads=cores)
+        kh = kc16.cpu().numpy().view(np.uint16)[None]
+        vh = vc16.cpu().numpy().view(np.uint16)[None]
+        qh = qb.float().cpu().numpy()
+        t_cpu = time.perf_counter()
+        O.paged_prefill(p, O.MODE_GGML, 0, qh, cu.astype(np.int32), qs.astype(np.int32),
+                        cl.astype(np.int32), bt_np, kh, vh)
+        t_cpu = time.perf_counter() - t_cpu
+        cpu = {"cores": cores, "kind": "port", "ms": t_cpu * 1e3,
+               "tflops": flops / world / t_cpu / 1e12,
+               "sample": "the whole workload, once (oracle GGML-mode paged prefill)"}
     h.close()
     fields = {"workload": name, "q_heads": Hq, "kv_heads": Hkv, "n_seqs": len(lens),
               "new_tokens": T, "sum_context": int(cl.sum()), "flops_per_step": flops,
               "steps": steps, "pv_precision": "f16 P x f16 V (V converted in smem)",
               "kv_store": kv_store_roofline(T, hq, hkv, store_ms, q_out_bytes=2),
               "clocks": clk}
+    if cpu is not None:
+        fields["cpu"] = cpu
     return fields, pre_ms, step_ms
 
 
