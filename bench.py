@@ -209,9 +209,18 @@ def bench_prefill(kind, args, world, rank, device):
         O.paged_prefill(p, O.MODE_GGML, 0, qh, cu.astype(np.int32), qs.astype(np.int32),
                         cl.astype(np.int32), bt_np, kh, vh)
         t_cpu = time.perf_counter() - t_cpu
+        # the reference's own prefill algorithm on the same host cores: the
+        # batch's new tokens concatenated, masked attention over the padded
+        # buffer; it attends no cached prefix, so it does less work than the
+        # path above (timing only; the f32 rows are the store's inputs)
+        t_ref = time.perf_counter()
+        O.concat_prefill_ggml(p, qh, cu.astype(np.int32), k.cpu().numpy(), v.cpu().numpy())
+        t_ref = time.perf_counter() - t_ref
         cpu = {"cores": cores, "kind": "port", "ms": t_cpu * 1e3,
                "tflops": flops / world / t_cpu / 1e12,
-               "sample": "the whole workload, once (oracle GGML-mode paged prefill)"}
+               "reference_concat_ms": t_ref * 1e3,
+               "sample": "the whole workload, once (oracle GGML-mode paged prefill; and the "
+                         "reference's concat-all prefill, which ignores the cached prefix)"}
     h.close()
     fields = {"workload": name, "q_heads": Hq, "kv_heads": Hkv, "n_seqs": len(lens),
               "new_tokens": T, "sum_context": int(cl.sum()), "flops_per_step": flops,

@@ -661,6 +661,73 @@ void orc_concat_decode_ggml(const orc_params* p, int layer, int n_seqs,
 }
 
 /* ------------------------------------------------------------------------ */
+/* the reference's prefill attention (GGML mode)                             */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  const orc_params* p;
+  int n_seqs;
+  int64_t n_tokens, n_kv_pad, rows_per_item;
+  const int32_t* cu_q;
+  const float *q, *kh, *vh; /* kh/vh: [Hkv][n_kv_pad][d], f16-rounded */
+  float* out;
+} concat_prefill_ctx;
+
+/* one item = (kv head, block of query rows); each row scans its whole mask
+ * row, as the masked attention over the padded buffer does */
+static void concat_prefill_item(void* vctx, int64_t item) {
+  concat_prefill_ctx* c = (concat_prefill_ctx*)vctx;
+  const orc_params* p = c->p;
+  const int Hq = p->n_q_heads, Hkv = p->n_kv_heads, d = p->head_dim;
+  const int G = Hq / Hkv;
+  const int kvh = (int)(item % Hkv);
+  const int64_t r0 = (item / Hkv) * c->rows_per_item;
+  int64_t r1 = r0 + c->rows_per_item;
+  if (r1 > c->n_tokens) r1 = c->n_tokens;
+  key_set ks = {(float*)c->kh + (int64_t)kvh * c->n_kv_pad * d,
+                (float*)c->vh + (int64_t)kvh * c->n_kv_pad * d, c->n_kv_pad};
+  int64_t* idx = (int64_t*)malloc(sizeof(int64_t) * (size_t)(c->n_kv_pad + 1));
+  int s = 0;
+  for (int64_t r = r0; r < r1; ++r) {
+    while (s + 1 < c->n_seqs && c->cu_q[s + 1] <= r) ++s;
+    /* FillCausalMask: column j is 0 (attend) for cu_q[s] <= j <= r, -inf
+     * elsewhere, padded columns included; -inf columns are skipped */
+    int64_t n = 0;
+    for (int64_t j = 0; j < c->n_kv_pad; ++j)
+      if (j >= c->cu_q[s] && j <= r) idx[n++] = j;
+    for (int g = 0; g < G; ++g) {
+      const int64_t row = r * Hq + (int64_t)kvh * G + g;
+      attend_row(ORC_MODE_GGML, d, p->scale, c->q + row * d, &ks, idx, n, c->out + row * d);
+    }
+  }
+  free(idx);
+}
+
+void orc_concat_prefill_ggml(const orc_params* p, int n_seqs, const int32_t* cu_q,
+                             const float* q, const float* new_k, const float* new_v,
+                             float* out) {
+  const int Hkv = p->n_kv_heads, d = p->head_dim;
+  const int64_t T = cu_q[n_seqs];
+  const int64_t T_pad = (T + 255) / 256 * 256; /* qwen3.cpp:461 */
+  /* ggml_pad with zeros (qwen3.cpp:524-527), then ggml_cast to F16
+   * (:388-393); one contiguous [n_kv_pad][d] plane per kv head */
+  float* kh = (float*)calloc((size_t)(Hkv * T_pad * d), sizeof(float));
+  float* vh = (float*)calloc((size_t)(Hkv * T_pad * d), sizeof(float));
+  for (int h = 0; h < Hkv; ++h)
+    for (int64_t j = 0; j < T; ++j) {
+      memcpy(kh + ((int64_t)h * T_pad + j) * d, new_k + (j * Hkv + h) * d, sizeof(float) * d);
+      memcpy(vh + ((int64_t)h * T_pad + j) * d, new_v + (j * Hkv + h) * d, sizeof(float) * d);
+    }
+  ROUND_F16(kh, (int64_t)Hkv * T_pad * d);
+  ROUND_F16(vh, (int64_t)Hkv * T_pad * d);
+  concat_prefill_ctx c = {p, n_seqs, T, T_pad, 16, cu_q, q, kh, vh, out};
+  parallel_for(p->n_threads, ((T + c.rows_per_item - 1) / c.rows_per_item) * Hkv,
+               concat_prefill_item, &c);
+  free(kh);
+  free(vh);
+}
+
+/* ------------------------------------------------------------------------ */
 /* token sampling (model_runner.cpp:417-489)                                */
 /* ------------------------------------------------------------------------ */
 

@@ -127,6 +127,17 @@ void orc_concat_decode_ggml(const orc_params* p, int layer, int n_seqs,
                             const int32_t* context_lens, const float* new_k,
                             const float* new_v, float* out);
 
+/* ---- the reference's own prefill attention (GGML mode only) ----
+ * The batch's new tokens concatenated (sequence s owns rows [cu_q[s],
+ * cu_q[s+1])), their f32 K/V zero-padded to a multiple of 256 and cast to
+ * F16, and masked attention over the whole buffer with FillCausalMask's
+ * block-diagonal causal mask (model_runner.cpp:188-217; qwen3.cpp:461-531,
+ * 377-405).  A cached prefix is not attended: the reference's prefill sees
+ * only the batch's tokens.  O(T * PAD(T, 256)) mask work per kv head. */
+void orc_concat_prefill_ggml(const orc_params* p, int n_seqs, const int32_t* cu_q,
+                             const float* q, const float* new_k, const float* new_v,
+                             float* out);
+
 /* ---- token sampling (ModelRunner::Sample, model_runner.cpp:417-489) ----
  * Row s of logits (n_vocab f32 at logits + s*row_stride):
  *  - penalty[s] > 1: every occurrence of a history id t in [0, n_vocab)

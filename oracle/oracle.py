@@ -154,6 +154,20 @@ def concat_decode_ggml(p, layer, q, k_cache, v_cache, block_tables, context_lens
     return out
 
 
+def concat_prefill_ggml(p, q, cu_q, new_k, new_v):
+    """The reference's prefill attention over the batch's concatenated new
+    tokens (FillCausalMask, model_runner.cpp:188-217; qwen3.cpp:461-531)."""
+    T = int(cu_q[-1])
+    out = np.empty((T, p.n_q_heads, p.head_dim), dtype=np.float32)
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    new_k = np.ascontiguousarray(new_k, dtype=np.float32)
+    new_v = np.ascontiguousarray(new_v, dtype=np.float32)
+    cu_q = np.ascontiguousarray(cu_q, dtype=np.int32)
+    lib().orc_concat_prefill_ggml(ctypes.byref(p), ctypes.c_int(len(cu_q) - 1), _p(cu_q), _p(q),
+                                  _p(new_k), _p(new_v), _p(out))
+    return out
+
+
 def _hist_args(history, history_offsets):
     if history is None:
         return None, None, None

@@ -162,6 +162,40 @@ def test_reference_concat_decode_is_bit_identical_to_paged_restatement():
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+def test_reference_concat_prefill_is_bit_identical_to_paged_restatement():
+    """The reference's prefill (the batch's new tokens concatenated, f32 K/V
+    padded and cast to F16, FillCausalMask's block-diagonal causal mask over
+    the whole buffer) visits a row's keys in the same order as the paged
+    restatement given the same f32 new rows; without a cached prefix the two
+    agree bit for bit."""
+    rng = np.random.default_rng(8)
+    lens = [300, 1, 129, 700]
+    c = cases.prefill_case(8, 16, 8, lens, [0, 0, 0, 0])
+    p = cases.oracle_params(16, 8, c.cache)
+    T = int(c.cu_q[-1])
+    nk = rng.standard_normal((T, 8, 128), dtype=np.float32)
+    nv = rng.standard_normal((T, 8, 128), dtype=np.float32)
+    a = O.concat_prefill_ggml(p, c.q, c.cu_q, nk, nv)
+    b = O.paged_prefill(p, O.MODE_GGML, 0, c.q, c.cu_q, c.q_starts, c.seq_lens, c.block_tables,
+                        c.cache.k, c.cache.v, nk, nv)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_reference_concat_prefill_ignores_a_cached_prefix():
+    """With a cached prefix the reference's prefill attends only the batch's
+    own tokens; the paged restatement (and the kernel) attend the prefix too,
+    so the rows differ (by design, not a tolerance question)."""
+    rng = np.random.default_rng(9)
+    c = cases.prefill_case(9, 2, 1, [600], [256])
+    p = cases.oracle_params(2, 1, c.cache)
+    nk = rng.standard_normal((344, 1, 128), dtype=np.float32)
+    nv = rng.standard_normal((344, 1, 128), dtype=np.float32)
+    a = O.concat_prefill_ggml(p, c.q, c.cu_q, nk, nv)
+    b = O.paged_prefill(p, O.MODE_GGML, 0, c.q, c.cu_q, c.q_starts, c.seq_lens, c.block_tables,
+                        c.cache.k, c.cache.v, nk, nv)
+    assert np.abs(a - b).max() > 1e-2
+
+
 def test_block_permutation_invariance():
     c = cases.decode_case(7, 8, 4, [700, 129], num_blocks=12)
     p = cases.oracle_params(8, 4, c.cache)
