@@ -2,6 +2,7 @@
 #include "attention_runner.h"
 
 #include <algorithm>
+#include <limits>
 #include <stdexcept>
 
 namespace nvattn_host {
@@ -16,7 +17,8 @@ bool grow(T** ptr, size_t n) {
 }
 }  // namespace
 
-AttentionRunner::AttentionRunner(const nvattn_config& cfg) : cfg_(cfg) {
+AttentionRunner::AttentionRunner(const nvattn_config& cfg, uint32_t sample_seed)
+    : cfg_(cfg), rng_(sample_seed) {
   const nvattn_status st = nvattn_create(&cfg_, &handle_);
   if (st != NVATTN_OK)
     throw std::runtime_error(std::string("nvattn_create failed: ") + nvattn_status_string(st));
@@ -28,7 +30,65 @@ AttentionRunner::~AttentionRunner() {
   for (int32_t* b : bufs)
     if (b) cudaFree(b);
   if (d_q_bf16_) cudaFree(d_q_bf16_);
+  void* sbufs[] = {d_temps_, d_pens_, d_uniforms_, d_tokens_, d_hist_offsets_, d_history_};
+  for (void* b : sbufs)
+    if (b) cudaFree(b);
   nvattn_destroy(handle_);
+}
+
+std::vector<int> AttentionRunner::Sample(const float* logits_dev, int n_vocab,
+                                         const std::vector<float>& temperatures,
+                                         const std::vector<float>& penalties,
+                                         const std::vector<std::vector<int32_t>>& histories,
+                                         cudaStream_t stream) {
+  const size_t n = temperatures.size();
+  if (n == 0 || n > (size_t)cfg_.max_seqs || penalties.size() != n || histories.size() != n ||
+      n_vocab <= 0)
+    return {};
+  // the draws, as the reference's loop takes them: one per sampled row
+  uniforms_.assign(n, 0.0f);
+  for (size_t s = 0; s < n; ++s)
+    if (!(temperatures[s] < 1e-6f))
+      uniforms_[s] = std::generate_canonical<float, std::numeric_limits<float>::digits>(rng_);
+  std::vector<int64_t> offsets(n + 1, 0);
+  for (size_t s = 0; s < n; ++s) offsets[s + 1] = offsets[s] + (int64_t)histories[s].size();
+  std::vector<int32_t> ids;
+  ids.reserve((size_t)offsets[n]);
+  for (const auto& h : histories) ids.insert(ids.end(), h.begin(), h.end());
+
+  bool ok = true;
+  if (n > cap_sample_rows_) {
+    ok = grow(&d_temps_, n) && grow(&d_pens_, n) && grow(&d_uniforms_, n) &&
+         grow(&d_tokens_, n) && grow(&d_hist_offsets_, n + 1);
+    cap_sample_rows_ = ok ? n : 0;
+  }
+  if (ok && ids.size() > cap_history_) {
+    ok = grow(&d_history_, ids.size());
+    cap_history_ = ok ? ids.size() : 0;
+  }
+  if (!ok) return {};
+  auto up = [&](void* dst, const void* src, size_t bytes) {
+    return bytes == 0 ||
+           cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream) == cudaSuccess;
+  };
+  if (!up(d_temps_, temperatures.data(), n * sizeof(float)) ||
+      !up(d_pens_, penalties.data(), n * sizeof(float)) ||
+      !up(d_uniforms_, uniforms_.data(), n * sizeof(float)) ||
+      !up(d_hist_offsets_, offsets.data(), (n + 1) * sizeof(int64_t)) ||
+      !up(d_history_, ids.data(), ids.size() * sizeof(int32_t)))
+    return {};
+  if (nvattn_sample(handle_, (int)n, n_vocab, logits_dev, n_vocab, d_temps_, d_pens_,
+                    ids.empty() ? nullptr : d_history_, ids.empty() ? nullptr : d_hist_offsets_,
+                    d_uniforms_, d_tokens_, stream) != NVATTN_OK)
+    return {};
+  std::vector<int32_t> tok(n);
+  if (cudaMemcpyAsync(tok.data(), d_tokens_, n * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                      stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return {};
+  int64_t detail = 0;
+  if (nvattn_get_error(handle_, &detail) != NVATTN_OK) return {};
+  return std::vector<int>(tok.begin(), tok.end());
 }
 
 bool AttentionRunner::Reserve(size_t n_tokens, size_t n_seqs, size_t max_blocks) {

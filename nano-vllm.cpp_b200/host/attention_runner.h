@@ -21,6 +21,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <random>
 #include <string>
 #include <vector>
 
@@ -38,7 +39,10 @@ struct SequenceView {
 
 class AttentionRunner {
  public:
-  explicit AttentionRunner(const nvattn_config& cfg);
+  // sample_seed seeds the runner's std::mt19937 for temperature sampling
+  // (the reference seeds its own from std::random_device).
+  explicit AttentionRunner(const nvattn_config& cfg,
+                           uint32_t sample_seed = std::mt19937::default_seed);
   ~AttentionRunner();
   AttentionRunner(const AttentionRunner&) = delete;
   AttentionRunner& operator=(const AttentionRunner&) = delete;
@@ -58,6 +62,22 @@ class AttentionRunner {
                          const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                          uint16_t* k_cache, uint16_t* v_cache, float* out,
                          cudaStream_t stream);
+
+  // ModelRunner::Sample (model_runner.cpp:417-489) on the device.
+  // logits_dev: [n_seqs][n_vocab] f32 (the graph's output rows);
+  // temperatures, penalties and histories (prompt ids, then completion ids)
+  // per sequence.  Each row with temperature >= 1e-6 takes one draw, in row
+  // order, from the runner's mt19937 as the reference's
+  // uniform_real_distribution<float> does.  Returns the tokens after
+  // synchronising the stream, or {} on invalid input, a failed call or an
+  // error in the handle's status word (read and cleared here).
+  std::vector<int> Sample(const float* logits_dev, int n_vocab,
+                          const std::vector<float>& temperatures,
+                          const std::vector<float>& penalties,
+                          const std::vector<std::vector<int32_t>>& histories,
+                          cudaStream_t stream);
+  // The draws the last Sample call used (0 for greedy rows).
+  const std::vector<float>& LastUniforms() const { return uniforms_; }
 
   int NumTokens() const { return n_tokens_; }
   int NumSeqs() const { return n_seqs_; }
@@ -86,6 +106,17 @@ class AttentionRunner {
   int32_t* d_cu_q_ = nullptr;
   int32_t* d_q_starts_ = nullptr;
   uint16_t* d_q_bf16_ = nullptr;
+
+  // sampling
+  std::mt19937 rng_;
+  std::vector<float> uniforms_;
+  size_t cap_sample_rows_ = 0, cap_history_ = 0;
+  float* d_temps_ = nullptr;
+  float* d_pens_ = nullptr;
+  float* d_uniforms_ = nullptr;
+  int32_t* d_tokens_ = nullptr;
+  int64_t* d_hist_offsets_ = nullptr;
+  int32_t* d_history_ = nullptr;
 };
 
 }  // namespace nvattn_host

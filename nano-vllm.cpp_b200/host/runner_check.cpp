@@ -7,6 +7,10 @@
 //   prefill: sequence A, 300 new tokens; sequence B, 600 tokens of which the
 //            first 512 (two blocks) are a prefix-cache hit; sequence C, 37.
 //   decode:  each sequence appends one token.
+//   sample:  two Sample calls on the same 3 x 5003 logits (unaligned rows):
+//            greedy rows with and without a repetition penalty (histories
+//            include ids past the vocabulary) and a temperature row with one
+//            dominant logit, so every token is determined.
 // Usage: runner_check <out_dir> [seed]
 // Output: <out_dir>/manifest.txt lines "name dtype d0 d1 ..." and one raw
 // little-endian <name>.bin per array.
@@ -220,6 +224,41 @@ int main(int argc, char** argv) {
       cudaFree(d_v);
       cudaFree(d_out);
     }
+
+    // ---- sampling: the next token of each sequence ----
+    const int V = 5003;
+    std::vector<float> logits((size_t)3 * V);
+    for (auto& x : logits) x = 2.0f * rng.normal();
+    logits[(size_t)1 * V + 4321] = 40.0f;  // row 1 samples this id whatever the draw
+    const std::vector<float> temps = {0.0f, 0.7f, 0.0f}, pens = {1.3f, 1.2f, 1.0f};
+    std::vector<std::vector<int32_t>> hist(3);
+    for (int i = 0; i < 200; ++i) hist[0].push_back((int32_t)(rng.next() % (V + 50)));
+    for (int i = 0; i < 50; ++i) hist[1].push_back((int32_t)(rng.next() % V));
+    float* d_logits = upload(logits);
+    if (!d_logits) return 1;
+    std::vector<int32_t> tokens, offsets = {0}, flat;
+    std::vector<float> draws;
+    for (int call = 0; call < 2; ++call) {
+      const std::vector<int> t = runner.Sample(d_logits, V, temps, pens, hist, nullptr);
+      if (t.size() != 3) {
+        std::fprintf(stderr, "Sample failed (call %d)\n", call);
+        return 1;
+      }
+      tokens.insert(tokens.end(), t.begin(), t.end());
+      draws.insert(draws.end(), runner.LastUniforms().begin(), runner.LastUniforms().end());
+    }
+    for (const auto& h : hist) {
+      flat.insert(flat.end(), h.begin(), h.end());
+      offsets.push_back((int32_t)flat.size());
+    }
+    out.put("sample_logits", "f32", logits, {(size_t)3, (size_t)V});
+    out.put("sample_temperatures", "f32", temps, {(size_t)3});
+    out.put("sample_penalties", "f32", pens, {(size_t)3});
+    out.put("sample_history", "i32", flat, {flat.size()});
+    out.put("sample_history_offsets", "i32", offsets, {(size_t)4});
+    out.put("sample_uniforms", "f32", draws, {(size_t)2, (size_t)3});
+    out.put("sample_tokens", "i32", tokens, {(size_t)2, (size_t)3});
+    cudaFree(d_logits);
   } catch (const std::exception& e) {
     std::fprintf(stderr, "%s\n", e.what());
     return 1;

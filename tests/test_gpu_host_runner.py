@@ -2,11 +2,13 @@
 the ModelRunner-shaped caller of the C ABI (model_runner.cpp:25-186).
 
 nano-vllm.cpp_b200/bin/runner_check drives AttentionRunner through one prefill
-step (three sequences, one with a two-block prefix-cache hit) and one decode
-step on layer 1 of a 2-layer cache and dumps every input and output; this test
-recomputes them with the oracle: the runner's positions and slot mapping equal
-the planner's, the stored K/V rows are bit-exact, and the attention outputs
-meet the attention tolerances."""
+step (three sequences, one with a two-block prefix-cache hit), one decode
+step on layer 1 of a 2-layer cache, and two Sample calls, and dumps every
+input and output; this test recomputes them with the oracle: the runner's
+positions and slot mapping equal the planner's, the stored K/V rows are
+bit-exact, the attention outputs meet the attention tolerances, the draws
+are the reference's mt19937 draws and the sampled tokens equal
+ModelRunner::Sample's."""
 import os
 import subprocess
 
@@ -78,3 +80,22 @@ def test_host_runner_prefill_then_decode(cuda, tmp_path):
     ref = O.paged_decode(p, O.MODE_TRUTH, layer, oq, kc, vc, bt, cl)
     mx, mr = O.err_stats(a["decode_out"], ref)
     assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+
+    # ---- sampling: AttentionRunner::Sample, twice on the same logits ----
+    logits = a["sample_logits"]
+    temps, pens = a["sample_temperatures"], a["sample_penalties"]
+    offs = a["sample_history_offsets"].astype(np.int64)
+    hist = a["sample_history"]
+    # the draws are the reference's: one generate_canonical<float> of the
+    # runner's mt19937 (default seed 5489) per temperature row, in row order
+    bg = np.random.MT19937()
+    bg._legacy_seeding(5489)
+    raw = bg.random_raw(2)
+    u = a["sample_uniforms"]
+    assert u[0, 0] == u[0, 2] == u[1, 0] == u[1, 2] == 0.0
+    assert u[0, 1] == np.float32(O.canonical_float(int(raw[0])))
+    assert u[1, 1] == np.float32(O.canonical_float(int(raw[1])))
+    for call in range(2):
+        want = O.sample(logits, temps, pens, u[call], hist, offs)
+        np.testing.assert_array_equal(a["sample_tokens"][call], want)
+    assert a["sample_tokens"][0, 1] == 4321
