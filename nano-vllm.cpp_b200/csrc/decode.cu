@@ -29,6 +29,8 @@
 //               the UMMA operand layout.
 // A split writes either the final row (single split) or its (m, l, O)
 // partial, which paged_decode_combine_kernel merges.
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -408,14 +410,15 @@ nvattn_status launch_g(const CUtensorMap* tk, const CUtensorMap* tv, const Decod
                        int n_seqs, int max_context_len, cudaStream_t stream) {
   const size_t smem = sizeof(DecodeSmem<G>) + 1024;
   // The attribute is per device; remember which devices have it.
-  static unsigned long long attr_set_mask = 0;
+  // (atomic: handles on different threads may launch at the same time)
+  static std::atomic<unsigned long long> attr_set_mask{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
-  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
+  if (dev >= 64 || !(attr_set_mask.load(std::memory_order_relaxed) & (1ull << dev))) {
     if (cudaFuncSetAttribute(paged_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return NVATTN_ERR_CUDA;
-    if (dev < 64) attr_set_mask |= 1ull << dev;
+    if (dev < 64) attr_set_mask.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
   const int n_splits_max = max_context_len > 0
                                ? (max_context_len + prm.split_tokens - 1) / prm.split_tokens

@@ -40,6 +40,7 @@
 //    (non-finite input, or norm weights of magnitude >= 2^120) takes ggml's
 //    bit rule instead, which keeps the NaN payload.
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "internal.h"
@@ -615,15 +616,16 @@ StagedPlan plan_staged(int n_tokens, int Hq, int Hkv) {
 template <bool kQOutBf16>
 nvattn_status launch_staged(const KvStoreParams& p, const StagedPlan& plan, int sm_count,
                             cudaStream_t stream) {
-  static unsigned long long attr_set_mask = 0;
+  // (atomic: handles on different threads may launch at the same time)
+  static std::atomic<unsigned long long> attr_set_mask{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
-  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
+  if (dev >= 64 || !(attr_set_mask.load(std::memory_order_relaxed) & (1ull << dev))) {
     if (cudaFuncSetAttribute(kv_store_staged_kernel<kQOutBf16>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kStageSmemBudget) != cudaSuccess)
       return NVATTN_ERR_CUDA;
-    if (dev < 64) attr_set_mask |= 1ull << dev;
+    if (dev < 64) attr_set_mask.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
   const int grid = std::min(sm_count, plan.n_chunks);
   const size_t smem = kStageHeader + (size_t)plan.n_stages * plan.stage_bytes;

@@ -49,6 +49,8 @@
 // implies PV(j) is done (its O may then be rescaled).
 // TMEM columns: tile t uses [256t, 256t+128) for S/P and [256t+128, 256t+256)
 // for O.
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -630,14 +632,15 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   const int grid = (int)std::min<long long>(n_items, h->sm_count);
   const size_t smem = sizeof(PrefillSmem) + 1024;
   // The attribute is per device; remember which devices have it.
-  static unsigned long long attr_set_mask = 0;
+  // (atomic: handles on different threads may launch at the same time)
+  static std::atomic<unsigned long long> attr_set_mask{0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
-  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
+  if (dev >= 64 || !(attr_set_mask.load(std::memory_order_relaxed) & (1ull << dev))) {
     if (cudaFuncSetAttribute(paged_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return NVATTN_ERR_CUDA;
-    if (dev < 64) attr_set_mask |= 1ull << dev;
+    if (dev < 64) attr_set_mask.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
   paged_prefill_kernel<<<grid, kThreads, smem, stream>>>(tm_q, *tk, *tv, prm);
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
