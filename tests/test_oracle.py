@@ -1,5 +1,6 @@
 """CPU tests of the oracle itself: known answers, IEEE edge cases, the
-reference's concat-all decode algorithm, and the committed golden fixtures.
+reference's concat-all decode and prefill algorithms, and the committed
+golden fixtures.
 
 Parity against the reference is unpinned (no reference tests exist and ggml
 is not vendored); these tests pin the restatement instead.
@@ -162,19 +163,20 @@ def test_reference_concat_decode_is_bit_identical_to_paged_restatement():
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-def test_reference_concat_prefill_is_bit_identical_to_paged_restatement():
+@pytest.mark.parametrize("Hq,Hkv,lens", [(16, 8, [300, 1, 129, 700]), (32, 8, [257, 511]),
+                                         (8, 8, [1, 2, 3, 640]), (2, 1, [1000])])
+def test_reference_concat_prefill_is_bit_identical_to_paged_restatement(Hq, Hkv, lens):
     """The reference's prefill (the batch's new tokens concatenated, f32 K/V
     padded and cast to F16, FillCausalMask's block-diagonal causal mask over
     the whole buffer) visits a row's keys in the same order as the paged
     restatement given the same f32 new rows; without a cached prefix the two
     agree bit for bit."""
-    rng = np.random.default_rng(8)
-    lens = [300, 1, 129, 700]
-    c = cases.prefill_case(8, 16, 8, lens, [0, 0, 0, 0])
-    p = cases.oracle_params(16, 8, c.cache)
+    rng = np.random.default_rng(8 + Hq)
+    c = cases.prefill_case(8 + Hq, Hq, Hkv, lens, [0] * len(lens))
+    p = cases.oracle_params(Hq, Hkv, c.cache)
     T = int(c.cu_q[-1])
-    nk = rng.standard_normal((T, 8, 128), dtype=np.float32)
-    nv = rng.standard_normal((T, 8, 128), dtype=np.float32)
+    nk = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    nv = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
     a = O.concat_prefill_ggml(p, c.q, c.cu_q, nk, nv)
     b = O.paged_prefill(p, O.MODE_GGML, 0, c.q, c.cu_q, c.q_starts, c.seq_lens, c.block_tables,
                         c.cache.k, c.cache.v, nk, nv)
