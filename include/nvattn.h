@@ -269,6 +269,9 @@ NVATTN_API nvattn_status nvattn_paged_decode(
  *   q_dev   [n_tokens][n_q_heads][head_dim] bf16
  *   out_dev [n_tokens][n_q_heads][head_dim] f32
  * max_q_len: host-side upper bound of the per-sequence query count.
+ * A sequence whose rows [cu_q_lens[s], cu_q_lens[s+1]) do not lie inside
+ * [0, n_tokens) is skipped and reported as NVATTN_ERR_OUT_OF_RANGE (detail =
+ * cu_q_lens[s+1]); nothing is read or written for it.
  * The CTAs take their work from a counter in the handle's workspace, so two
  * prefill launches on one handle must not run concurrently (issue them on
  * one stream, as the split-KV workspace of nvattn_paged_decode also needs). */

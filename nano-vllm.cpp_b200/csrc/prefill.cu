@@ -71,6 +71,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 struct PrefillParams {
   int Hq, Hkv, G, layer, block_size, max_blocks, n_mtiles, pair_heads;
   int gx, n_items;  // items per (sequence, kv head); items in all
+  int n_tokens;     // rows of q and out
   long long n_slots, num_blocks;
   float scale_log2;
   const int32_t* cu_q;
@@ -143,7 +144,14 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& prm, int item, 
     w.row0[1] = w.row0[0] + kBM;
   }
   w.q0 = prm.cu_q[w.seq];
-  const int n_q = prm.cu_q[w.seq + 1] - w.q0;
+  const int q1 = prm.cu_q[w.seq + 1];
+  if (w.q0 < 0 || q1 < w.q0 || q1 > prm.n_tokens) {
+    // rows outside q / out: the sequence is skipped (all its items)
+    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 25, q1);
+    skip_to = item - x + prm.gx;
+    return false;
+  }
+  const int n_q = q1 - w.q0;
   if (n_q > prm.n_mtiles * kBM && x == 0 && w.kvh == 0)
     record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 21, n_q);
   skip_to = item + 1;
@@ -628,6 +636,7 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   if (n_items > 0x7fffffffLL - h->sm_count) return NVATTN_ERR_UNSUPPORTED;
   prm.gx = (int)gx;
   prm.n_items = (int)n_items;
+  prm.n_tokens = n_tokens;
   // Persistent: one CTA per SM (the shared-memory footprint allows no more).
   const int grid = (int)std::min<long long>(n_items, h->sm_count);
   const size_t smem = sizeof(PrefillSmem) + 1024;

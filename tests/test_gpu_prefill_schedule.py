@@ -5,13 +5,15 @@ zeroes the counter.  These tests target that machinery: batches where most
 items are empty (one long prompt among one-token ones, a max_q_len bound far
 above the longest prompt), CUDA-graph replays (the counter must be back at
 zero before every replay, with no host-side reset), and launches of
-different shapes back to back on one handle.  Outputs are checked against
+different shapes back to back on one handle; and query rows named outside
+q and out, which are reported and skipped.  Outputs are checked against
 the oracle's fp64 attention (max-abs 2e-2, mean-rel 1e-3) and, across
 launches, bit for bit against each other."""
 import numpy as np
 import pytest
 
 import cases
+import nvattn
 import oracle as O
 from gpu_util import dev, handle
 
@@ -137,3 +139,28 @@ def test_back_to_back_launches_of_different_shapes(cuda):
     for oa, ob in zip(outs_a, outs_b):
         np.testing.assert_array_equal(oa.cpu().numpy().view(np.uint32), first_a.view(np.uint32))
         np.testing.assert_array_equal(ob.cpu().numpy().view(np.uint32), first_b.view(np.uint32))
+
+
+def test_rows_outside_q_are_reported_not_written(cuda):
+    """cu_q_lens naming rows past the n_tokens rows of q and out: that
+    sequence is skipped and reported (NVATTN_ERR_OUT_OF_RANGE, detail = the
+    offending end row); the other sequence is computed as usual.  The output
+    buffer has spare rows past n_tokens, which must stay untouched."""
+    import torch
+    c = cases.prefill_case(930, 16, 8, [300, 200], [0, 0])
+    x = Inputs(c)
+    T = c.q.shape[0]
+    bad_cu = c.cu_q.copy()
+    bad_cu[2] = T + 20
+    out = torch.full((T + 64, 16, 128), float("nan"), device="cuda")
+    h = handle(16, 8, c.cache.num_blocks, max_seqs=2)
+    try:
+        h.prefill(c.layer, x.q, dev(bad_cu), x.qs, x.cl, x.bt, 320, x.k, x.v, out)
+        torch.cuda.synchronize()
+        st, detail = h.get_error()
+    finally:
+        h.close()
+    assert st == nvattn.ERR_OUT_OF_RANGE and detail == T + 20
+    got = out.cpu().numpy()
+    assert np.isnan(got[300:]).all()
+    check(got[:300], truth(c)[:300])
