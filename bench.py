@@ -148,7 +148,7 @@ def bench_prefill(kind, args, world, rank, device):
     v = torch.randn((T, hkv, D), generator=gen, device=device)
     qw = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16)
     kw = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16)
-    qb = torch.empty((T, hq, D), dtype=torch.bfloat16, device=device)
+    qb = torch.empty((T, hq, D), dtype=torch.float16, device=device)
     out = torch.empty((T, hq, D), device=device)
     d = {n: torch.from_numpy(a).to(device) for n, a in
          (("cu", cu), ("qs", qs), ("cl", cl), ("pos", pos_np), ("slot", slot_np), ("bt", bt_np))}
@@ -274,7 +274,7 @@ def bench_prefill_chunked(args, world, rank, device):
         idx = torch.from_numpy(rows).to(device)
         t = {"q": q.index_select(0, idx), "k": k.index_select(0, idx),
              "v": v.index_select(0, idx)}
-        t["qb"] = torch.empty(t["q"].shape, dtype=torch.bfloat16, device=device)
+        t["qb"] = torch.empty(t["q"].shape, dtype=torch.float16, device=device)
         t["out"] = torch.empty(t["q"].shape, device=device)
         for name, arr in (("cu", cu), ("qs", qs), ("cl", cl), ("pos", pos), ("slot", slot),
                           ("bt", np.ascontiguousarray(bt_np[seqs]))):
@@ -481,7 +481,7 @@ def bench_decode_small(args, world, rank, device):
            "lens": lens.tolist(), "steps": steps, "step_us": step_ms * 1e3,
            "graph_step_us": graph_us, "graph_step_device_planned_us": planned_us,
            "decode_us": dec_ms * 1e3,
-           "roofline": {"bound": "hbm", "kernel": "paged_decode (main + split combine)",
+           "roofline": {"bound": "hbm", "kernel": "paged_decode (split-KV, merged in-kernel by the last split)",
                         "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
                         "frac": gbs / hbm_peak, "peak_source": kind, "algorithmic_bytes": alg,
                         "frac_of_8tbs": gbs / 8000.0}}
@@ -599,7 +599,7 @@ def bench_decode_long(args, world, rank, device):
     return {"workload": "decode_qwen3_32b_attn_16seq_ctx131104", "q_heads": Hq, "kv_heads": Hkv,
             "n_seqs": B, "context": L, "steps": steps, "ms_per_step": step_ms,
             "tokens_per_s": B / (step_ms / 1e3),
-            "roofline": {"bound": "hbm", "kernel": "paged_decode (main + split combine)",
+            "roofline": {"bound": "hbm", "kernel": "paged_decode (split-KV, merged in-kernel by the last split)",
                          "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": gbs / hbm_peak, "peak_source": kind, "decode_ms": dec_ms,
                          "algorithmic_bytes": alg, "frac_of_8tbs": gbs / 8000.0}}
@@ -736,8 +736,110 @@ def run_prefills(args, world, rank, device):
             at_clock = 148 * 8192 * mhz * 1e6 / 1e12
             fields["roofline"]["peak_at_sampled_clock"] = at_clock
             fields["roofline"]["frac_of_peak_at_sampled_clock"] = achieved / at_clock
+        fields["kind"] = kind
+        fields["roofline"]["flops_per_step"] = fields["flops_per_step"]
         results.append(fields)
     return results
+
+
+def allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq, lens, bt_np, kc,
+                   vc, q):
+    """Second timed loop at N > 1: every step is the store + decode step
+    followed by NCCL's all-gather of the [B][Hq/N][128] head outputs into
+    [N][B][Hq/N][128] (the head-concatenated attention output o_proj needs).
+    Then rank 0 checks the gathered output of the two shortest sequences
+    against the oracle (exact math over all heads): every rank hands over
+    those sequences' cache rows and normed q for its heads, and rank 0
+    reassembles them.  Every rank runs the same collectives in the same
+    order."""
+    import torch
+    import torch.distributed as dist
+    gathered = torch.empty((world * B, hq, D), device=device_of(out))
+    ev = []
+
+    def gstep():
+        step()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        dist.all_gather_into_tensor(gathered, out)
+        b.record(stream)
+        ev.append((a, b))
+
+    for _ in range(3):
+        gstep()
+    dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    ev.clear()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        gstep()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[local_rank])
+    tv = torch.tensor([t0.elapsed_time(t1) / 1e3,
+                       sum(a.elapsed_time(b) for a, b in ev) / len(ev)],
+                      dtype=torch.float64, device=device_of(out))
+    dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+    elapsed, ag_ms = tv.tolist()
+
+    # sharded parity: the gathered output holds the last step's attention
+    full = gathered.view(world, B, hq, D).permute(1, 0, 2, 3).reshape(B, world * hq, D)
+    sel = np.argsort(lens, kind="stable")[:2]
+    need = (lens[sel] + BS - 1) // BS
+    ids = np.concatenate([bt_np[s, :need[i]] for i, s in enumerate(sel)])
+    rows = (torch.from_numpy(ids.astype(np.int64)).to(kc.device)[:, None] * BS
+            + torch.arange(BS, device=kc.device)[None]).reshape(-1)
+    mine = torch.cat([kc.index_select(0, rows).view(torch.int16),
+                      vc.index_select(0, rows).view(torch.int16)], 0).contiguous()
+    theirs = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype, device=mine.device)
+    dist.all_gather_into_tensor(theirs, mine)
+    qs = q[torch.from_numpy(sel).to(q.device)].contiguous()
+    q_all = torch.empty((world,) + tuple(qs.shape), dtype=qs.dtype, device=qs.device)
+    dist.all_gather_into_tensor(q_all, qs)
+    res = {"allgather_ms": ag_ms, "steps": args.steps, "ms_per_step": 1e3 * elapsed / args.steps,
+           "e2e_with_gather": {"value": B * args.steps / elapsed, "unit": "tokens/s"},
+           "bytes_per_rank": B * hq * D * 4}
+    if rank == 0:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        k_full, v_full, q_full, btc = reassemble_shards(
+            theirs.cpu().numpy().view(np.uint16), q_all.cpu().numpy(), need)
+        p = O.params(n_q_heads=world * hq, n_kv_heads=k_full.shape[2],
+                     n_slots=k_full.shape[1], n_threads=0)
+        ref = O.paged_decode(p, O.MODE_TRUTH, 0, q_full, k_full, v_full, btc,
+                             lens[sel].astype(np.int32))
+        got = full[torch.from_numpy(sel).to(full.device)].cpu().numpy()
+        mx, mr = O.err_stats(got, ref)
+        res["sharded_parity"] = {"seqs": [int(s) for s in sel], "max_abs": mx, "mean_rel": mr,
+                                 "ok": bool(mx <= 2e-2 and mr <= 1e-3),
+                                 "against": "oracle TRUTH over all heads"}
+    return res
+
+
+def reassemble_shards(kv_ranks, q_ranks, need):
+    """Rebuilds all heads from per-rank pieces (rank r owns kv heads
+    [r*Hkv/N, (r+1)*Hkv/N) and their q heads, consecutively): kv_ranks
+    [N][2n][Hkv/N][D] = each rank's K rows then V rows of the sampled
+    sequences' blocks (n rows, blocks in sequence order), q_ranks
+    [N][S][Hq/N][D].  Returns a one-layer K and V cache [1][n][Hkv][D], the
+    queries [S][Hq][D] and a block table numbering the blocks in order."""
+    world = kv_ranks.shape[0]
+    n = kv_ranks.shape[1] // 2
+    k_full = np.concatenate([kv_ranks[r, :n] for r in range(world)], axis=1)[None]
+    v_full = np.concatenate([kv_ranks[r, n:] for r in range(world)], axis=1)[None]
+    q_full = np.concatenate([q_ranks[r] for r in range(world)], axis=1)
+    btc = np.full((len(need), int(max(need))), -1, np.int32)
+    off = 0
+    for i, nb in enumerate(need):
+        btc[i, :nb] = np.arange(off, off + nb)
+        off += int(nb)
+    return (np.ascontiguousarray(k_full), np.ascontiguousarray(v_full),
+            np.ascontiguousarray(q_full), btc)
+
+
+def device_of(t):
+    return t.device
 
 
 def peaks():
@@ -890,8 +992,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--allgather", action="store_true",
-                    help="all-gather the head-sharded outputs every step (NCCL)")
+    ap.add_argument("--no-allgather", action="store_true",
+                    help="with N > 1 GPUs, skip the second timed loop that all-gathers the "
+                         "head-sharded outputs every step (NCCL) and checks them")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seqs", type=int, default=N_SEQS,
                     help="use the first SEQS sequences only (smaller case for profiling)")
@@ -980,7 +1083,6 @@ def main():
     w = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16)
     q = torch.empty_like(q0)
     out = torch.empty((B, hq, D), device=device)
-    gathered = torch.empty((world, B, hq, D), device=device) if args.allgather else None
     stream = torch.cuda.current_stream(device)
     kc16, vc16, w16 = kc.view(torch.int16), vc.view(torch.int16), w.view(torch.int16)
 
@@ -991,8 +1093,6 @@ def main():
         ev_a.record(stream)
         h.decode(0, q, kc16, vc16, bt, ctx, max_ctx, out, stream=stream)
         ev_b.record(stream)
-        if gathered is not None:
-            dist.all_gather_into_tensor(gathered, out)
 
     def barrier():
         if world > 1:
@@ -1106,6 +1206,12 @@ def main():
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     elapsed, e2e_elapsed, dec_ms = times.tolist()
 
+    # ---- N > 1: the step plus the all-gather of the head-sharded outputs ----
+    allgather = None
+    if world > 1 and not args.no_allgather:
+        allgather = allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq,
+                                   lens, bt_np, kc, vc, q)
+
     # CPU baseline (rank 0, one GPU): the oracle's ggml-chain decode on the
     # host cores over the workload's first sequences, with this run's K/V.
     cpu_base = None
@@ -1145,7 +1251,6 @@ def main():
         alg_bytes = (kv_bytes + B * hq * D * 4 * 2 + int(((lens + BS - 1) // BS).sum()) * 4
                      + B * 4)
         achieved = alg_bytes / (dec_ms / 1e3) / 1e9
-        splits = 1
         line = {
             "metric": METRIC, "value": n_tok / elapsed, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -1158,8 +1263,8 @@ def main():
                        "kv_gb_per_gpu": round(kv_bytes / 1e9, 3),
                        "parallelism": f"kv-head shard x{world}",
                        "l2": "inputs larger than L2 (KV cache >> 126 MB), no flush",
-                       "allgather": bool(args.allgather)},
-            "roofline": {"bound": "hbm", "kernel": "paged_decode (main + split combine)",
+                       "allgather": allgather is not None},
+            "roofline": {"bound": "hbm", "kernel": "paged_decode (split-KV, merged in-kernel by the last split)",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_kind,
                          "traffic": NCU_TRAFFIC_BYTES_N1 if world == 1 else None,
@@ -1167,15 +1272,18 @@ def main():
                          "frac_of_8tbs": achieved / 8000.0},
             "e2e": {"value": n_tok / e2e_elapsed, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * (2 + splits),
+            "gpu_launches": args.steps * 2,  # fused store + decode per step
             "clocks": clk,
-            "prefill": prefill_results,
             "decode_long": decode_long,
             "decode_small": decode_small,
             "sample": sample,
             "prefill_chunked": prefill_chunked,
             "kv_store": kv_store_roofline(B, hq, hkv, store_ms, q_out_bytes=4),
         }
+        for res in prefill_results:
+            line["prefill_" + res["kind"]] = res
+        if allgather is not None:
+            line["allgather"] = allgather
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)

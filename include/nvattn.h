@@ -54,7 +54,7 @@ extern "C" {
 #endif
 
 #define NVATTN_VERSION_MAJOR 0
-#define NVATTN_VERSION_MINOR 1
+#define NVATTN_VERSION_MINOR 2
 
 typedef enum nvattn_status {
   NVATTN_OK = 0,
@@ -70,7 +70,8 @@ typedef enum nvattn_status {
 
 typedef enum nvattn_dtype {
   NVATTN_DTYPE_F32 = 0,
-  NVATTN_DTYPE_BF16 = 1
+  NVATTN_DTYPE_BF16 = 1,
+  NVATTN_DTYPE_F16 = 2
 } nvattn_dtype;
 
 /* Same type as cudaStream_t, without pulling in CUDA headers. */
@@ -236,7 +237,9 @@ NVATTN_API nvattn_status nvattn_sample(
  *   k_dev, v_dev [n_tokens][n_kv_heads][head_dim] f32
  *   q_norm_w_dev, k_norm_w_dev [head_dim] bf16
  *   q_out_dev [n_tokens][n_q_heads][head_dim] in q_out_dtype (may alias q_dev
- *            when f32)
+ *            when f32); f16 is the query type nvattn_paged_prefill takes
+ *            (round to nearest even, as ggml_fp32_to_fp16, which the
+ *            reference's flash attention applies to Q)
  *   k_cache_dev, v_cache_dev: cache base (all layers).
  * The stored K/V bytes equal ggml_fp32_to_bf16_row of the reference's f32
  * graph outputs (round to nearest even). */
@@ -254,6 +257,7 @@ NVATTN_API nvattn_status nvattn_kv_store_qk_norm_rope(
  *   q_dev   [n_seqs][n_q_heads][head_dim] f32
  *   out_dev [n_seqs][n_q_heads][head_dim] f32
  * max_context_len: host-side upper bound of context_lens (sizes the grid).
+ * n_seqs <= 65535 (INVALID_ARG above).
  * Split-KV partial results go to the handle's workspace. */
 NVATTN_API nvattn_status nvattn_paged_decode(
     nvattn_handle* h, int layer, int n_seqs, const float* q_dev,
@@ -266,7 +270,11 @@ NVATTN_API nvattn_status nvattn_paged_decode(
  * s owns query rows [cu_q_lens[s], cu_q_lens[s+1]) at positions
  * q_starts[s] + i; a row at position P attends keys [0, P] of layer `layer`
  * through the block table.  The rows' own K/V must already be stored.
- *   q_dev   [n_tokens][n_q_heads][head_dim] bf16
+ *   q_dev   [n_tokens][n_q_heads][head_dim] f16 (q_out of
+ *           nvattn_kv_store_qk_norm_rope with NVATTN_DTYPE_F16)
+ * Scores multiply f16 Q with the cache's K converted to f16 and P.V uses f16
+ * probabilities and V -- the F16 Q/K/V of the reference's
+ * ggml_flash_attn_ext -- with f32 accumulation.
  *   out_dev [n_tokens][n_q_heads][head_dim] f32
  * max_q_len: host-side upper bound of the per-sequence query count.
  * A sequence whose rows [cu_q_lens[s], cu_q_lens[s+1]) do not lie inside
@@ -305,11 +313,15 @@ typedef struct nvattn_device_status {
  * every input and output, and the split-KV partial results go to a fixed
  * 32 MiB device array inside the library (held by every GPU that loads the
  * library until the process exits).  A call whose partials do not fit
- * (n_seqs * n_q_heads * splits * 520 bytes > 32 MiB, splits chosen as for a
- * handle created from cfg) returns NVATTN_ERR_SCRATCH_LIMIT.
+ * (n_seqs * n_q_heads * splits * 520 bytes plus n_seqs * n_kv_heads * 4
+ * bytes of split counters > 32 MiB, splits chosen as for a handle created
+ * from cfg) returns NVATTN_ERR_SCRATCH_LIMIT; a call that splits clears the
+ * counters first (cudaMemsetAsync on the stream, no allocation).
+ * n_seqs <= 65535 (INVALID_ARG above).
  * It runs on the caller's current device, which must be cfg->device.  The
- * first call on a device looks up the array's device address; make that
- * first call before any stream capture.  All calls share the one array and
+ * first call on a device looks up the array's device address and the SM
+ * count (once per device, safe when several threads make that first call
+ * together); make that first call before any stream capture.  All calls share the one array and
  * it keeps the last call's contents: calls whose kernels overlap on the GPU
  * (other streams, other threads) race on it, so serialise them.
  * status_dev (nullable) receives errors the kernels detect; results equal

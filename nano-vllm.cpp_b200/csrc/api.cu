@@ -56,28 +56,29 @@ namespace nvattn {
 
 nvattn_status encode_tensor_map_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
                                    uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
-                                   uint32_t box0, uint32_t box1, uint32_t box2, int swizzle) {
+                                   uint32_t box0, uint32_t box1, uint32_t box2, int swizzle,
+                                   CUtensorMapDataType dtype) {
   EncodeTiledFn fn = encode_tiled_fn();
   if (fn == nullptr) return NVATTN_ERR_CUDA;
   const cuuint64_t dims[3] = {d0, d1, d2};
   const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
   const cuuint32_t box[3] = {box0, box1, box2};
   const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+  CUresult r = fn(map, dtype, 3, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 
 nvattn_status get_cache_tensor_map(nvattn_handle* h, const void* base, int box_d, int box_rows,
-                                   int swizzle, const CUtensorMap** out) {
-  for (auto& e : h->maps) {
+                                   int swizzle, CUtensorMap* out) {
+  for (int i = 0; i < h->n_maps; ++i) {
+    const NvattnTensorMapEntry& e = h->maps[i];
     if (e.base == base && e.box_d == box_d && e.box_rows == box_rows && e.swizzle == swizzle) {
-      *out = &e.map;
+      *out = e.map;
       return NVATTN_OK;
     }
   }
-  if (h->maps.size() >= 16) h->maps.erase(h->maps.begin());
   NvattnTensorMapEntry e;
   e.base = base;
   e.box_d = box_d;
@@ -89,8 +90,15 @@ nvattn_status get_cache_tensor_map(nvattn_handle* h, const void* base, int box_d
                                           Hkv * D * 2, (uint32_t)box_d, 1, (uint32_t)box_rows,
                                           swizzle);
   if (st != NVATTN_OK) return st;
-  h->maps.push_back(e);
-  *out = &h->maps.back().map;
+  int slot;
+  if (h->n_maps < nvattn_handle::kMapCacheSize) {
+    slot = h->n_maps++;
+  } else {
+    slot = h->next_map;
+    h->next_map = (h->next_map + 1) % nvattn_handle::kMapCacheSize;
+  }
+  h->maps[slot] = e;
+  *out = e.map;
   return NVATTN_OK;
 }
 
@@ -197,9 +205,13 @@ nvattn_status nvattn_create(const nvattn_config* cfg, nvattn_handle** out) {
     long long splits = (c.max_context + c.block_size - 1) / c.block_size;
     h->max_splits = (int)(splits < 64 ? splits : 64);
     const size_t rows = (size_t)c.max_seqs * c.n_q_heads * h->max_splits;
+    const size_t tickets = (size_t)c.max_seqs * c.n_kv_heads * sizeof(int);
     if (cudaMalloc(&h->ws_o, rows * c.head_dim * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&h->ws_ml, rows * 2 * sizeof(float)) != cudaSuccess)
+        cudaMalloc(&h->ws_ml, rows * 2 * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&h->decode_tickets, tickets) != cudaSuccess)
       st = NVATTN_ERR_NO_MEMORY;
+    else if (cudaMemset(h->decode_tickets, 0, tickets) != cudaSuccess)
+      st = NVATTN_ERR_CUDA;
   }
   if (st != NVATTN_OK) {
     cudaGetLastError();  // clear a sticky allocation error
@@ -218,6 +230,7 @@ nvattn_status nvattn_destroy(nvattn_handle* h) {
   if (h->prefill_sched_dev) cudaFree(h->prefill_sched_dev);
   if (h->ws_o) cudaFree(h->ws_o);
   if (h->ws_ml) cudaFree(h->ws_ml);
+  if (h->decode_tickets) cudaFree(h->decode_tickets);
   if (h->samp_nib) cudaFree(h->samp_nib);
   if (h->samp_exact) cudaFree(h->samp_exact);
   if (h->samp_part) cudaFree(h->samp_part);
@@ -235,6 +248,11 @@ nvattn_status nvattn_get_error(nvattn_handle* h, int64_t* detail) {
   if (cudaMemcpy(&st, h->status_dev, sizeof(st), cudaMemcpyDeviceToHost) != cudaSuccess)
     return NVATTN_ERR_CUDA;
   if (st.code != 0 && cudaMemset(h->status_dev, 0, sizeof(st)) != cudaSuccess)
+    return NVATTN_ERR_CUDA;
+  // A decode launch cut short by a timeout may leave split tickets taken.
+  if (st.code == NVATTN_ERR_TIMEOUT &&
+      cudaMemset(h->decode_tickets, 0,
+                 (size_t)h->cfg.max_seqs * h->cfg.n_kv_heads * sizeof(int)) != cudaSuccess)
     return NVATTN_ERR_CUDA;
   if (detail) *detail = st.detail;
   return (nvattn_status)st.code;
@@ -390,7 +408,8 @@ nvattn_status nvattn_kv_store_qk_norm_rope(nvattn_handle* h, int layer, int n_to
                                            uint16_t* v_cache_dev, nvattn_stream_t stream) {
   if (h == nullptr || layer < 0 || layer >= h->cfg.n_layer || n_tokens < 0)
     return NVATTN_ERR_INVALID_ARG;
-  if (q_out_dtype != NVATTN_DTYPE_F32 && q_out_dtype != NVATTN_DTYPE_BF16)
+  if (q_out_dtype != NVATTN_DTYPE_F32 && q_out_dtype != NVATTN_DTYPE_BF16 &&
+      q_out_dtype != NVATTN_DTYPE_F16)
     return NVATTN_ERR_INVALID_ARG;
   if (n_tokens == 0) return NVATTN_OK;
   const void* ptrs[] = {q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev, q_out_dev,
@@ -412,8 +431,8 @@ nvattn_status nvattn_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
                                   const int32_t* context_lens_dev, int max_context_len,
                                   float* out_dev, nvattn_stream_t stream) {
   if (h == nullptr || layer < 0 || layer >= h->cfg.n_layer || n_seqs < 0 ||
-      n_seqs > h->cfg.max_seqs || max_blocks <= 0 || max_context_len < 0 ||
-      max_context_len > h->cfg.max_context ||
+      n_seqs > h->cfg.max_seqs || n_seqs > nvattn::kMaxDecodeSeqs || max_blocks <= 0 ||
+      max_context_len < 0 || max_context_len > h->cfg.max_context ||
       (long long)max_context_len > (long long)max_blocks * h->cfg.block_size)
     return NVATTN_ERR_INVALID_ARG;
   if (n_seqs == 0) return NVATTN_OK;

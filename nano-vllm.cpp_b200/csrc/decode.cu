@@ -28,8 +28,12 @@
 //               sums reduced once per split, P^T written to shared memory in
 //               the UMMA operand layout.
 // A split writes either the final row (single split) or its (m, l, O)
-// partial, which paged_decode_combine_kernel merges.
+// partial; the last split CTA of a (sequence, kv head) to finish -- found by
+// an atomic ticket per (sequence, kv head), which that CTA re-arms to zero --
+// merges the partials and writes the rows, so a decode is one launch.
 #include <atomic>
+#include <functional>
+#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
@@ -58,6 +62,7 @@ struct DecodeParams {
   float* out;
   float* ws_o;
   float* ws_ml;
+  int* tickets;  // [n_seqs][Hkv] split tickets, zero between launches
   DeviceStatus* status;
 };
 
@@ -72,6 +77,7 @@ struct __align__(1024) DecodeSmem {
   uint64_t q_ready, s_full[2], p_full, o_done;
   uint32_t tmem_base;
   int abort_flag;  // raised by the first wait that times out
+  int last_split;  // this CTA merges the (sequence, kv head)'s partials
 };
 
 __device__ __forceinline__ int ring_slot(int idx) { return idx % kSlots; }
@@ -107,10 +113,18 @@ __global__ void __launch_bounds__(kThreads, 2)
     ctx = ctx < 0 ? 0 : prm.max_context;
   }
   if (t_begin >= ctx && split > 0) return;  // nothing for this split
-  if (timeout_recorded(prm.status)) return;
+  const int n_splits = ctx > 0 ? (ctx + prm.split_tokens - 1) / prm.split_tokens : 1;
+  if (timeout_recorded(prm.status)) {
+    // An earlier launch timed out: skip the work, but keep the ticket count
+    // right so the last split still re-arms it.
+    if (threadIdx.x == 0 && n_splits > 1) {
+      int* tk = prm.tickets + (long long)seq * prm.Hkv + kvh;
+      if (atomicAdd(tk, 1) == n_splits - 1) atomicExch(tk, 0);
+    }
+    return;
+  }
   const int t_end = min(ctx, t_begin + prm.split_tokens);
   const int n_tiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
-  const int n_splits = ctx > 0 ? (ctx + prm.split_tokens - 1) / prm.split_tokens : 1;
   volatile int* abort_flag = &sm.abort_flag;
 
   if (threadIdx.x == 0) {
@@ -358,19 +372,51 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int n = 0; n < 16; ++n) ov[n] = 0u;
     }
+    if (n_splits == 1) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float o = __uint_as_float(ov[g]) + __uint_as_float(ov[G + g]);
-      const int h = kvh * G + g;
-      if (n_splits == 1) {
-        prm.out[((long long)seq * prm.Hq + h) * kD + r] = l_tot[g] > 0.0f ? o / l_tot[g] : 0.0f;
-      } else {
-        const long long pidx =
-            ((long long)(seq * prm.Hkv + kvh) * prm.max_splits + split) * G + g;
-        prm.ws_o[pidx * kD + r] = o;
+      for (int g = 0; g < G; ++g) {
+        const float o = __uint_as_float(ov[g]) + __uint_as_float(ov[G + g]);
+        prm.out[((long long)seq * prm.Hq + kvh * G + g) * kD + r] =
+            l_tot[g] > 0.0f ? o / l_tot[g] : 0.0f;
+      }
+    } else {
+      const long long base = (long long)(seq * prm.Hkv + kvh) * prm.max_splits;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const long long pidx = (base + split) * G + g;
+        prm.ws_o[pidx * kD + r] = __uint_as_float(ov[g]) + __uint_as_float(ov[G + g]);
         if (r == 0) {
           prm.ws_ml[pidx * 2 + 0] = m_used[g];
           prm.ws_ml[pidx * 2 + 1] = l_tot[g];
+        }
+      }
+      // Publish the partial, then take a ticket: the CTA that takes the
+      // last one sees every other split's partial (fence, atomic, fence).
+      __threadfence();
+      named_barrier_sync(1, 128);
+      if (r == 0) {
+        int* tk = prm.tickets + (long long)seq * prm.Hkv + kvh;
+        const int last = atomicAdd(tk, 1) == n_splits - 1;
+        if (last) atomicExch(tk, 0);  // re-armed for the next launch
+        sm.last_split = last;
+      }
+      named_barrier_sync(1, 128);
+      if (sm.last_split) {
+        __threadfence();
+        // merge: thread r = head dim r, every split in order
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float M = -INFINITY;
+          for (int i = 0; i < n_splits; ++i)
+            M = fmaxf(M, __ldcg(prm.ws_ml + ((base + i) * G + g) * 2));
+          float L = 0.0f, O = 0.0f;
+          for (int i = 0; i < n_splits; ++i) {
+            const long long pidx = (base + i) * G + g;
+            const float w = fast_exp2(__ldcg(prm.ws_ml + pidx * 2) - M);
+            L = fmaf(__ldcg(prm.ws_ml + pidx * 2 + 1), w, L);
+            O = fmaf(__ldcg(prm.ws_o + pidx * kD + r), w, O);
+          }
+          prm.out[((long long)seq * prm.Hq + kvh * G + g) * kD + r] = L > 0.0f ? O / L : 0.0f;
         }
       }
     }
@@ -382,27 +428,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
-}
-
-// Merges the split partials of one (sequence, q head); one thread per dim.
-__global__ void __launch_bounds__(kD) paged_decode_combine_kernel(DecodeParams prm, int G) {
-  const int h = blockIdx.x, seq = blockIdx.y, d = threadIdx.x;
-  const int ctx = min(prm.context_lens[seq], prm.max_context);
-  if (ctx <= 0) return;
-  const int n = (ctx + prm.split_tokens - 1) / prm.split_tokens;
-  if (n <= 1) return;
-  const int kvh = h / G, g = h % G;
-  const long long base = (long long)(seq * prm.Hkv + kvh) * prm.max_splits;
-  float M = -INFINITY;
-  for (int i = 0; i < n; ++i) M = fmaxf(M, prm.ws_ml[((base + i) * G + g) * 2]);
-  float L = 0.0f, O = 0.0f;
-  for (int i = 0; i < n; ++i) {
-    const long long pidx = (base + i) * G + g;
-    const float w = fast_exp2(prm.ws_ml[pidx * 2] - M);
-    L = fmaf(prm.ws_ml[pidx * 2 + 1], w, L);
-    O = fmaf(prm.ws_o[pidx * kD + d], w, O);
-  }
-  prm.out[((long long)seq * prm.Hq + h) * kD + d] = L > 0.0f ? O / L : 0.0f;
 }
 
 template <int G>
@@ -425,10 +450,6 @@ nvattn_status launch_g(const CUtensorMap* tk, const CUtensorMap* tv, const Decod
                                : 1;
   dim3 grid(n_splits_max, prm.Hkv, n_seqs);
   paged_decode_kernel<G><<<grid, kThreads, smem, stream>>>(*tk, *tv, prm);
-  if (n_splits_max > 1) {
-    dim3 cgrid(prm.Hq, n_seqs);
-    paged_decode_combine_kernel<<<cgrid, kD, 0, stream>>>(prm, G);
-  }
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 
@@ -468,8 +489,7 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
                                   const int32_t* context_lens, int max_context_len,
                                   float* out, cudaStream_t stream) {
   if (n_seqs == 0) return NVATTN_OK;
-  const CUtensorMap* tk = nullptr;
-  const CUtensorMap* tv = nullptr;
+  CUtensorMap tk, tv;
   nvattn_status st = get_cache_tensor_map(h, k_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
   if (st != NVATTN_OK) return st;
   st = get_cache_tensor_map(h, v_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tv);
@@ -493,12 +513,13 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
   prm.out = out;
   prm.ws_o = h->ws_o;
   prm.ws_ml = h->ws_ml;
+  prm.tickets = h->decode_tickets;
   prm.status = h->status_dev;
   switch (prm.Hq / prm.Hkv) {
-    case 1: return launch_g<1>(tk, tv, prm, n_seqs, max_context_len, stream);
-    case 2: return launch_g<2>(tk, tv, prm, n_seqs, max_context_len, stream);
-    case 4: return launch_g<4>(tk, tv, prm, n_seqs, max_context_len, stream);
-    case 8: return launch_g<8>(tk, tv, prm, n_seqs, max_context_len, stream);
+    case 1: return launch_g<1>(&tk, &tv, prm, n_seqs, max_context_len, stream);
+    case 2: return launch_g<2>(&tk, &tv, prm, n_seqs, max_context_len, stream);
+    case 4: return launch_g<4>(&tk, &tv, prm, n_seqs, max_context_len, stream);
+    case 8: return launch_g<8>(&tk, &tv, prm, n_seqs, max_context_len, stream);
     default: return NVATTN_ERR_UNSUPPORTED;
   }
 }
@@ -518,8 +539,31 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 namespace {
 constexpr int kMaxDevices = 64;
-void* g_noalloc_scratch_addr[kMaxDevices];  // device address per device (set once)
-int g_noalloc_sm_count[kMaxDevices];
+// Per-device set-up, done once under std::call_once: the scratch's device
+// address and the SM count.  call_once publishes both to every thread that
+// later passes the same flag, so no caller can see the address without the
+// SM count that chooses its splits.
+struct NoAllocDevice {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  void* scratch = nullptr;
+  int sm_count = 0;
+};
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+
+// Runs on the current device `dev` (the caller made it current).
+void noalloc_setup(NoAllocDevice& d, int dev) {
+  void* addr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+  int sms = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess && (addr == nullptr || sms <= 0)) e = cudaErrorInvalidValue;
+  d.err = e;
+  if (e == cudaSuccess) {
+    d.scratch = addr;
+    d.sm_count = sms;
+  }
+}
 }  // namespace
 
 }  // namespace nvattn
@@ -542,7 +586,8 @@ extern "C" NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
     return NVATTN_ERR_UNSUPPORTED;
   const long long n_slots = c.num_blocks * (long long)c.block_size;
   if ((long long)c.n_layer * n_slots >= (1LL << 31)) return NVATTN_ERR_UNSUPPORTED;
-  if (layer < 0 || layer >= c.n_layer || n_seqs < 0 || max_blocks <= 0 || max_context_len < 0 ||
+  if (layer < 0 || layer >= c.n_layer || n_seqs < 0 || n_seqs > kMaxDecodeSeqs ||
+      max_blocks <= 0 || max_context_len < 0 ||
       max_context_len > c.max_context ||
       (long long)max_context_len > (long long)max_blocks * c.block_size)
     return NVATTN_ERR_INVALID_ARG;
@@ -556,26 +601,24 @@ extern "C" NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
   if (dev != c.device || dev < 0 || dev >= kMaxDevices) return NVATTN_ERR_INVALID_ARG;
-  // One-time set-up on this device: the scratch's device address and the SM
-  // count (neither allocates).
-  if (g_noalloc_scratch_addr[dev] == nullptr) {
-    void* addr = nullptr;
-    if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || addr == nullptr)
-      return NVATTN_ERR_CUDA;
-    int sms = 0;
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return NVATTN_ERR_CUDA;
-    g_noalloc_sm_count[dev] = sms;
-    g_noalloc_scratch_addr[dev] = addr;
-  }
+  // One-time set-up on this device (allocates nothing).  A failure is kept
+  // and returned by every later call on the device.
+  NoAllocDevice& nd = g_noalloc_dev[dev];
+  std::call_once(nd.once, noalloc_setup, std::ref(nd), dev);
+  if (nd.err != cudaSuccess) return NVATTN_ERR_CUDA;
 
   // Same split rule as a handle created from this config, so the result
   // equals nvattn_paged_decode's.
-  const int split = split_tokens_for(g_noalloc_sm_count[dev], c.block_size, c.n_kv_heads,
+  const int split = split_tokens_for(nd.sm_count, c.block_size, c.n_kv_heads,
                                      workspace_max_splits(c), n_seqs, max_context_len);
   const int n_splits = max_context_len > 0 ? (max_context_len + split - 1) / split : 1;
   const size_t rows = n_splits > 1 ? (size_t)n_seqs * c.n_q_heads * n_splits : 0;
-  if (rows * (kD + 2) * sizeof(float) > kNoAllocScratchBytes) return NVATTN_ERR_SCRATCH_LIMIT;
+  // scratch layout: split tickets (n_seqs x n_kv_heads ints, padded to 256 B),
+  // then the partial rows' O (rows x 128 f32) and (m, l) (rows x 2 f32)
+  const size_t ticket_bytes =
+      n_splits > 1 ? ((size_t)n_seqs * c.n_kv_heads * sizeof(int) + 255) / 256 * 256 : 0;
+  if (ticket_bytes + rows * (kD + 2) * sizeof(float) > kNoAllocScratchBytes)
+    return NVATTN_ERR_SCRATCH_LIMIT;
 
   CUtensorMap tk, tv;
   nvattn_status st = encode_tensor_map_3d(&tk, k_cache_dev, kD, (uint64_t)c.n_kv_heads,
@@ -589,7 +632,13 @@ extern "C" NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
                             CU_TENSOR_MAP_SWIZZLE_128B);
   if (st != NVATTN_OK) return st;
 
-  float* scratch = static_cast<float*>(g_noalloc_scratch_addr[dev]);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int* tickets = static_cast<int*>(nd.scratch);
+  float* scratch = reinterpret_cast<float*>(static_cast<char*>(nd.scratch) + ticket_bytes);
+  // The tickets must start at zero: the array keeps whatever the last call
+  // (possibly one cut short by a timeout) left there.
+  if (ticket_bytes > 0 && cudaMemsetAsync(tickets, 0, ticket_bytes, s) != cudaSuccess)
+    return NVATTN_ERR_CUDA;
   DecodeParams prm;
   prm.Hq = c.n_q_heads;
   prm.Hkv = c.n_kv_heads;
@@ -608,8 +657,8 @@ extern "C" NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
   prm.out = out_dev;
   prm.ws_o = scratch;
   prm.ws_ml = scratch + rows * kD;
+  prm.tickets = tickets;
   prm.status = reinterpret_cast<DeviceStatus*>(status_dev);
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (G) {
     case 1: return launch_g<1>(&tk, &tv, prm, n_seqs, max_context_len, s);
     case 2: return launch_g<2>(&tk, &tv, prm, n_seqs, max_context_len, s);

@@ -40,9 +40,15 @@ struct nvattn_handle {
   // split-KV workspace for decode
   float* ws_o = nullptr;   // [max_seqs][n_kv_heads][max_splits][G][head_dim]
   float* ws_ml = nullptr;  // [max_seqs][n_kv_heads][max_splits][G][2]
+  int* decode_tickets = nullptr;  // [max_seqs][n_kv_heads], zero between launches
   int max_splits = 0;
 
-  std::vector<NvattnTensorMapEntry> maps;
+  // TMA descriptor cache: fixed storage, replaced round-robin once full, so
+  // an entry never moves while the handle lives.
+  static constexpr int kMapCacheSize = 16;
+  NvattnTensorMapEntry maps[kMapCacheSize] = {};
+  int n_maps = 0;
+  int next_map = 0;  // slot the next new descriptor replaces once full
 
   // sampler workspace (sample.cu), allocated by the first nvattn_sample call
   // for a vocabulary size; no contents survive between calls
@@ -54,16 +60,22 @@ struct nvattn_handle {
 
 namespace nvattn {
 
-// Returns a TMA descriptor over a whole K or V cache (all layers):
-// dims {head_dim, n_kv_heads, n_layer*n_slots}, bf16, box {box_d, 1, box_rows}.
-nvattn_status get_cache_tensor_map(nvattn_handle* h, const void* base, int box_d,
-                                   int box_rows, int swizzle, const CUtensorMap** out);
+// Largest n_seqs of one decode launch (the grid's z extent).
+constexpr int kMaxDecodeSeqs = 65535;
 
-// Generic 3-D bf16 tensor map (used for Q in prefill).
+// Copies into *out a TMA descriptor over a whole K or V cache (all layers):
+// dims {head_dim, n_kv_heads, n_layer*n_slots}, bf16, box {box_d, 1, box_rows}.
+// Encoded descriptors are cached per handle; the copy keeps the caller's
+// descriptor valid whatever later lookups do to the cache.
+nvattn_status get_cache_tensor_map(nvattn_handle* h, const void* base, int box_d,
+                                   int box_rows, int swizzle, CUtensorMap* out);
+
+// Generic 3-D tensor map of 16-bit elements (bf16 caches; f16 Q in prefill).
 nvattn_status encode_tensor_map_3d(CUtensorMap* map, const void* base, uint64_t d0,
                                    uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
                                    uint64_t stride2_bytes, uint32_t box0, uint32_t box1,
-                                   uint32_t box2, int swizzle);
+                                   uint32_t box2, int swizzle,
+                                   CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
 
 nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const float* q,
                               const float* k, const float* v, const uint16_t* qw,

@@ -210,6 +210,16 @@ __device__ __forceinline__ void norm_rope(float (&x)[2 * kPer], float scale,
   }
 }
 
+// q_out element types (template argument of the row kernels).
+constexpr int kQOutF32 = 0, kQOutBf16 = 1, kQOutF16 = 2;
+
+// Eight floats -> f16, round to nearest even (ggml_fp32_to_fp16's rounding
+// for every finite value; overflow gives inf, as there).
+__device__ __forceinline__ uint4 pack8_f16(const float* y) {
+  return make_uint4(cvt_f16x2(y[0], y[1]), cvt_f16x2(y[2], y[3]), cvt_f16x2(y[4], y[5]),
+                    cvt_f16x2(y[6], y[7]));
+}
+
 __device__ __forceinline__ uint4 pack8_bf16(const float* y, bool nan_rule) {
   uint4 a;
   if (!nan_rule) {
@@ -228,16 +238,20 @@ __device__ __forceinline__ uint4 pack8_bf16(const float* y, bool nan_rule) {
 
 // Writes the finished row: q rows to q_out, k/v rows to slot_mapping[t] of
 // the cache (slot < 0: not stored; slot >= n_slots: reported).
-template <bool kQOutBf16>
+template <int kQOut>
 __device__ __forceinline__ void store_row(const KvStoreParams& p, const float (&x)[2 * kPer],
                                           int t, int rr, int kind, int slot, bool nan_rule,
                                           int l8) {
   if (kind == 0) {
     const long long off = ((long long)t * p.Hq + rr) * kD + kPer * l8;
-    if (kQOutBf16) {
+    if (kQOut == kQOutBf16) {
       uint16_t* o = static_cast<uint16_t*>(p.q_out) + off;
       *reinterpret_cast<uint4*>(o) = pack8_bf16(x, nan_rule);
       *reinterpret_cast<uint4*>(o + kHalf) = pack8_bf16(x + kPer, nan_rule);
+    } else if (kQOut == kQOutF16) {
+      uint16_t* o = static_cast<uint16_t*>(p.q_out) + off;
+      *reinterpret_cast<uint4*>(o) = pack8_f16(x);
+      *reinterpret_cast<uint4*>(o + kHalf) = pack8_f16(x + kPer);
     } else {
       float* o = static_cast<float*>(p.q_out) + off;
 #pragma unroll
@@ -265,7 +279,7 @@ __device__ __forceinline__ void store_row(const KvStoreParams& p, const float (&
 // calls this, `active` false for padding rows).  get_w(w) and get_cs(c, sn)
 // supply the lane's norm weights and cos/sin values; they run after the
 // norm's dependency chain so the values are live only where they are used.
-template <bool kQOutBf16, class GetW, class GetCs>
+template <int kQOut, class GetW, class GetCs>
 __device__ __forceinline__ void finish_row(const KvStoreParams& p, float (&x)[2 * kPer],
                                            bool active, int t, int rr, int kind, int pos,
                                            bool pos_ok, int slot, GetW get_w, bool w_tame,
@@ -285,7 +299,7 @@ __device__ __forceinline__ void finish_row(const KvStoreParams& p, float (&x)[2 
     norm_rope(x, scale, w, c, sn);
     nan_rule = nan_rule || !w_tame;
   }
-  store_row<kQOutBf16>(p, x, t, rr, kind, slot, nan_rule, l8);
+  store_row<kQOut>(p, x, t, rr, kind, slot, nan_rule, l8);
 }
 
 // Input row of flattened row (t, rr): q, k or v head row.
@@ -308,7 +322,7 @@ __device__ __forceinline__ void load_row(const float* src, int l8, float (&x)[2 
   }
 }
 
-template <bool kQOutBf16>
+template <int kQOut>
 __global__ void __launch_bounds__(kThreads, 2) kv_store_rows_kernel(KvStoreParams p) {
   const int l8 = threadIdx.x & 7;  // lane within the row's 8-lane group
   const int rows_per_token = p.Hq + 2 * p.Hkv;
@@ -360,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 2) kv_store_rows_kernel(KvStoreParam
       load_weights(kind == 0 ? p.qw : p.kw, l8, lw);
     }
     const int slot = (valid && kind != 0) ? p.slots[t_row] : 0;
-    finish_row<kQOutBf16>(p, x, valid, t_row, rr_row, kind, pos, pos_ok, slot,
+    finish_row<kQOut>(p, x, valid, t_row, rr_row, kind, pos, pos_ok, slot,
                           [&](float (&w)[2 * kPer]) {
 #pragma unroll
                             for (int e = 0; e < kPer; ++e) {
@@ -417,7 +431,7 @@ __device__ __forceinline__ int lane_weight_slot(int el) {
 // The header holds the ring's barriers and, per stage, the chunk's positions
 // and slots (written by the producer warp before it arms the stage, so the
 // consumers never wait on a global load).
-template <bool kQOutBf16>
+template <int kQOut>
 __global__ void __launch_bounds__(kStageMaxThreads, 1)
     kv_store_staged_kernel(KvStoreParams p, StagedPlan plan) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -560,7 +574,7 @@ __global__ void __launch_bounds__(kStageMaxThreads, 1)
       const bool pos_ok = pos >= 0 && pos < p.max_position;
       const float4* cs4 = reinterpret_cast<const float4*>(st + (stage_rows + g.tl) * kRowBytes);
       const float4* w4 = reinterpret_cast<const float4*>(wsm + (g.kind == 0 ? 0 : kD)) + l8;
-      finish_row<kQOutBf16>(
+      finish_row<kQOut>(
           p, x, active, t0 + g.tl, g.rr, g.kind, pos, pos_ok, mslot[g.tl],
           [&](float (&w)[2 * kPer]) {
 #pragma unroll
@@ -613,7 +627,7 @@ StagedPlan plan_staged(int n_tokens, int Hq, int Hkv) {
   return s;
 }
 
-template <bool kQOutBf16>
+template <int kQOut>
 nvattn_status launch_staged(const KvStoreParams& p, const StagedPlan& plan, int sm_count,
                             cudaStream_t stream) {
   // (atomic: handles on different threads may launch at the same time)
@@ -621,7 +635,7 @@ nvattn_status launch_staged(const KvStoreParams& p, const StagedPlan& plan, int 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
   if (dev >= 64 || !(attr_set_mask.load(std::memory_order_relaxed) & (1ull << dev))) {
-    if (cudaFuncSetAttribute(kv_store_staged_kernel<kQOutBf16>,
+    if (cudaFuncSetAttribute(kv_store_staged_kernel<kQOut>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kStageSmemBudget) != cudaSuccess)
       return NVATTN_ERR_CUDA;
@@ -629,7 +643,7 @@ nvattn_status launch_staged(const KvStoreParams& p, const StagedPlan& plan, int 
   }
   const int grid = std::min(sm_count, plan.n_chunks);
   const size_t smem = kStageHeader + (size_t)plan.n_stages * plan.stage_bytes;
-  kv_store_staged_kernel<kQOutBf16>
+  kv_store_staged_kernel<kQOut>
       <<<grid, (plan.consumer_warps + 1) * 32, smem, stream>>>(p, plan);
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
@@ -661,7 +675,9 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
   const long long rows = (long long)n_tokens * (p.Hq + 2 * p.Hkv);
   if (rows > 0x7fffffffLL - kMaxRowsPerGroup * kGroupsPerBlock) return NVATTN_ERR_INVALID_ARG;
   p.total_rows = (int)rows;
-  const bool bf16_q = q_out_dtype == NVATTN_DTYPE_BF16;
+  const int q_kind = q_out_dtype == NVATTN_DTYPE_BF16  ? kQOutBf16
+                     : q_out_dtype == NVATTN_DTYPE_F16 ? kQOutF16
+                                                       : kQOutF32;
 
   // Large batches: bulk-copy staging (at least four stages per CTA so the
   // ring pipelines).  Small batches: the register-row kernel, which spreads
@@ -669,8 +685,11 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
   const StagedPlan plan = plan_staged(n_tokens, p.Hq, p.Hkv);
   if (plan.n_stages >= 3 && plan.n_chunks >= 4 * h->sm_count) {
     p.rows_per_group = 0;
-    return bf16_q ? launch_staged<true>(p, plan, h->sm_count, stream)
-                  : launch_staged<false>(p, plan, h->sm_count, stream);
+    switch (q_kind) {
+      case kQOutBf16: return launch_staged<kQOutBf16>(p, plan, h->sm_count, stream);
+      case kQOutF16: return launch_staged<kQOutF16>(p, plan, h->sm_count, stream);
+      default: return launch_staged<kQOutF32>(p, plan, h->sm_count, stream);
+    }
   }
   // Enough groups for about four resident blocks per SM; beyond that each
   // group takes more rows so the per-token loads are shared.
@@ -678,10 +697,16 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
   p.rows_per_group = (int)std::max(1LL, std::min<long long>(kMaxRowsPerGroup, rows / per_wave));
   const long long groups = (rows + p.rows_per_group - 1) / p.rows_per_group;
   const long long blocks = (groups + kGroupsPerBlock - 1) / kGroupsPerBlock;
-  if (bf16_q)
-    kv_store_rows_kernel<true><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
-  else
-    kv_store_rows_kernel<false><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+  switch (q_kind) {
+    case kQOutBf16:
+      kv_store_rows_kernel<kQOutBf16><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+      break;
+    case kQOutF16:
+      kv_store_rows_kernel<kQOutF16><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+      break;
+    default:
+      kv_store_rows_kernel<kQOutF32><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+  }
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 

@@ -9,11 +9,14 @@
 // position P attends keys [0, P] of its sequence through the block table,
 // which covers prefix-cache hits and chunked prefill alike.
 //
-// Precision: S = Q K^T multiplies bf16 Q with the bf16 cache K.  For P.V the
-// softmax probabilities are rounded to f16 (11 significant bits, vs 8 for
-// bf16) and each V tile is converted bf16 -> f16 in shared memory, exactly
-// the F16 V the reference hands to ggml_flash_attn_ext (qwen3.cpp:388-393,
-// including its overflow above 65504).  Accumulation is f32.
+// Precision: the reference's flash attention runs on F16 Q, K and V
+// (ggml_cast of K/V, qwen3.cpp:388-393, and the F16 conversion of Q inside
+// ggml_flash_attn_ext).  Here Q arrives as f16 (the fused store's f16 q
+// output), each K and V tile is converted bf16 -> f16 in shared memory (exact
+// in f16's range; overflow above 65504 as in ggml_cast), S = Q K^T multiplies
+// f16 operands, P is rounded to f16 for P.V, and accumulation is f32.  (A bf16
+// Q, 8 significant bits, put the output ~1.4e-3 mean-rel from exact math on
+// f32 queries; f16 Q, 11 bits, ~2e-4.)
 //
 // A work item is two 128-row query tiles that read the same keys: the two GQA
 // heads of a pair (same rows, same kv head), or, when a kv head serves one q
@@ -32,12 +35,14 @@
 //                two tiles so the tensor core works on one tile while the
 //                other tile's softmax runs:
 //                  PV0(j), S0(j+1), PV1(j), S1(j+1), ...
-//                S_t = Q_t K^T (M=128, N=128, K=128; A and B K-major, smem)
+//                S_t = Q_t K^T (M=128, N=128, K=128; f16 A and B K-major, smem)
 //                O_t += P_t V  (A = P from TMEM, B = V MN-major from smem)
-//   warps 12-15  V converters (one per SM sub-partition, so the conversion
-//                work does not fall on the sub-partitions of only some softmax
-//                warps): bf16 -> f16 in place, rows past the context zeroed (a
-//                cache slot past a sequence's end may hold NaN bits).
+//   warps 12-15  K/V converters (one per SM sub-partition, so the
+//                conversion work does not fall on the sub-partitions of only
+//                some softmax warps): bf16 -> f16 in place, K(j) then V(j);
+//                V rows past the context zeroed (a cache slot past a
+//                sequence's end may hold NaN bits; masked K columns never
+//                reach P).
 //   warps 2-3    idle.
 //   warps 4-7    softmax of tile 0; warps 8-11 softmax of tile 1: thread =
 //                query row = TMEM lane.  Causal mask, online softmax in the
@@ -63,6 +68,7 @@ constexpr int kBN = 128;  // keys per tile
 constexpr int kSlots = 5;
 constexpr int kThreads = 16 * 32;
 constexpr int kConvThreads = 128;         // warps 12-15
+constexpr int kConvAhead = 4;             // converter lead, in key tiles (barrier sets)
 constexpr int kHalfBytes = 128 * 64 * 2;  // one 128-row x 64-column 16-bit box: 16 KiB
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -96,7 +102,9 @@ struct __align__(1024) PrefillSmem {
   uint64_t q_full;
   uint64_t full[kSlots], empty[kSlots];
   uint64_t s_full[2], p_full[2];
-  uint64_t v_ready[2], v_consumed[2];  // by key-tile parity
+  // per key tile gj, indexed gj % kConvAhead: converted K / V ready for the
+  // MMAs, and P.V of the tile done (its V slot no longer read)
+  uint64_t k_ready[4], v_ready[4], v_consumed[4];
   uint64_t o_final;
   uint64_t q_empty;                      // the item's last S MMAs have read Q
   uint64_t work_full[2], work_empty[2];  // the work ring
@@ -263,9 +271,37 @@ __device__ __forceinline__ bool next_work(PrefillSmem& sm, const PrefillParams& 
   return w.valid != 0;
 }
 
-// ---------------------------------------------------------------- V converters
-// Tile gj is converted only after P.V of tile gj-2 has finished, so each
-// barrier of a parity pair runs at most one phase ahead of its waiter.
+// ---------------------------------------------------------------- K/V converters
+// Converts one 128-key tile (two 64-column halves, 2048 16-byte chunks) from
+// bf16 to f16 in place; with zero_from >= 0, keys at or past zero_from are
+// zeroed instead.  Consecutive threads touch consecutive chunks (no bank
+// conflicts).
+__device__ __forceinline__ void convert_tile(uint16_t (&tile)[2][kBN * 64], int c, int zero_from) {
+#pragma unroll 4
+  for (int f = c; f < 2 * 128 * 8; f += kConvThreads) {
+    const int half = f >> 10, key = (f & 1023) >> 3;
+    uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(tile[half]) + (f & 1023) * 16);
+    uint4 v = *p;
+    if (zero_from < 0 || key < zero_from) {
+      v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
+      v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
+      v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
+      v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
+    } else {
+      v = make_uint4(0, 0, 0, 0);
+    }
+    *p = v;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+}
+
+// The converters run ahead of the MMAs as far as the TMA ring lets them
+// (K(gj) and V(gj) as soon as they land), so the conversion stays off the
+// S -> softmax -> P.V chain.  Their barriers come in sets of kConvAhead, one
+// per key tile mod kConvAhead; tile gj waits for P.V of tile gj-kConvAhead
+// (which has waited k_ready / v_ready of that tile), so no barrier runs more
+// than one phase ahead of its waiter.
 __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillParams& prm, int c) {
   volatile int* abort_flag = &sm.abort_flag;
   const int lane = c & 31;
@@ -280,32 +316,16 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
     if (!valid) break;
     for (int j = 0; j < n_kv; ++j) {
       const int gj = tb + j;
-      const int b = gj & 1;
-      if (gj >= 2) mbar_wait(&sm.v_consumed[b], ((gj >> 1) - 1) & 1, prm.status, abort_flag, 43);
-      const int vidx = 2 * gj + 1;
-      const int slot = ring_slot(vidx);
-      mbar_wait(&sm.full[slot], ring_parity(vidx), prm.status, abort_flag, 44);
+      const int b = gj % kConvAhead;
+      const uint32_t ph = (uint32_t)(gj / kConvAhead) & 1u;
+      if (gj >= kConvAhead) mbar_wait(&sm.v_consumed[b], ph ^ 1u, prm.status, abort_flag, 43);
+      const int kidx = 2 * gj, vidx = 2 * gj + 1;
+      mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 50);
+      convert_tile(sm.kv[ring_slot(kidx)], c, -1);
+      if (lane == 0) mbar_arrive(&sm.k_ready[b]);
+      mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 44);
       const int key0 = j * kBN;
-      // 2048 16-byte chunks: half h = f / 1024, key row = (f % 1024) / 8.
-      // Consecutive threads touch consecutive chunks (no bank conflicts).
-#pragma unroll 4
-      for (int f = c; f < 2 * 128 * 8; f += kConvThreads) {
-        const int half = f >> 10, key = (f & 1023) >> 3;
-        uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.kv[slot][half]) +
-                                            (f & 1023) * 16);
-        uint4 v = *p;
-        if (key0 + key < ctx) {
-          v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
-          v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
-          v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
-          v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
-        } else {
-          v = make_uint4(0, 0, 0, 0);
-        }
-        *p = v;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
+      convert_tile(sm.kv[ring_slot(vidx)], c, ctx - key0 < kBN ? max(ctx - key0, 0) : -1);
       if (lane == 0) mbar_arrive(&sm.v_ready[b]);
     }
     tb += n_kv;
@@ -316,7 +336,7 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
 __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
                                          const PrefillParams& prm) {
   volatile int* abort_flag = &sm.abort_flag;
-  constexpr uint32_t idesc_s = umma_idesc_bf16_f32(kBM, kBN, 0, 0);
+  constexpr uint32_t idesc_s = umma_idesc_f16_f32(kBM, kBN, 0, 0);
   constexpr uint32_t idesc_o = umma_idesc_f16_f32(kBM, kD, 0, 1);
   auto issue_s = [&](int t, int gj) {
     const int slot = ring_slot(2 * gj);
@@ -345,7 +365,8 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
     mbar_arrive(&sm.work_empty[ws]);
     if (!valid) break;
     mbar_wait(&sm.q_full, k & 1, prm.status, abort_flag, 31);
-    mbar_wait(&sm.full[ring_slot(2 * tb)], ring_parity(2 * tb), prm.status, abort_flag, 32);
+    mbar_wait(&sm.k_ready[tb % kConvAhead], (uint32_t)(tb / kConvAhead) & 1u, prm.status,
+              abort_flag, 32);
     tc_fence_after();
     // S_t(0) overwrites the S/P columns of the previous item: its P.V MMAs
     // were issued before and execute first.  Its O columns are rewritten by
@@ -360,12 +381,14 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
     for (int j = 0; j < n_kv; ++j) {
       const int gj = tb + j;
       const int vidx = 2 * gj + 1, kidx = 2 * gj + 2;
-      mbar_wait(&sm.v_ready[gj & 1], (gj >> 1) & 1, prm.status, abort_flag, 33);
+      mbar_wait(&sm.v_ready[gj % kConvAhead], (uint32_t)(gj / kConvAhead) & 1u, prm.status,
+                abort_flag, 33);
       mbar_wait(&sm.p_full[0], gj & 1, prm.status, abort_flag, 34);
       tc_fence_after();
       issue_pv(0, gj, j > 0);
       if (j + 1 < n_kv) {
-        mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 35);
+        mbar_wait(&sm.k_ready[(gj + 1) % kConvAhead], (uint32_t)((gj + 1) / kConvAhead) & 1u,
+                  prm.status, abort_flag, 35);
         tc_fence_after();
         issue_s(0, gj + 1);
         umma_commit(&sm.s_full[0]);
@@ -373,7 +396,7 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
       mbar_wait(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
       tc_fence_after();
       issue_pv(1, gj, j > 0);
-      umma_commit(&sm.v_consumed[gj & 1]);
+      umma_commit(&sm.v_consumed[gj % kConvAhead]);
       umma_commit(&sm.empty[ring_slot(vidx)]);
       if (j + 1 < n_kv) {
         issue_s(1, gj + 1);
@@ -533,11 +556,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], 1);
     }
+    for (int i = 0; i < kConvAhead; ++i) {
+      mbar_init(&sm.k_ready[i], kConvThreads / 32);
+      mbar_init(&sm.v_ready[i], kConvThreads / 32);
+      mbar_init(&sm.v_consumed[i], 1);
+    }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.p_full[t], 4);
-      mbar_init(&sm.v_ready[t], kConvThreads / 32);
-      mbar_init(&sm.v_consumed[t], 1);
       mbar_init(&sm.work_full[t], 1);
       mbar_init(&sm.work_empty[t], kWorkReaders);
     }
@@ -599,10 +625,10 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   CUtensorMap tm_q;
   nvattn_status st =
       encode_tensor_map_3d(&tm_q, q, kD, (uint64_t)Hq, (uint64_t)n_tokens, kD * 2,
-                           (uint64_t)Hq * kD * 2, 64, 1, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
+                           (uint64_t)Hq * kD * 2, 64, 1, kBM, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
   if (st != NVATTN_OK) return st;
-  const CUtensorMap* tk = nullptr;
-  const CUtensorMap* tv = nullptr;
+  CUtensorMap tk, tv;
   st = get_cache_tensor_map(h, k_cache, 64, kBN, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
   if (st != NVATTN_OK) return st;
   st = get_cache_tensor_map(h, v_cache, 64, kBN, CU_TENSOR_MAP_SWIZZLE_128B, &tv);
@@ -651,7 +677,7 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
       return NVATTN_ERR_CUDA;
     if (dev < 64) attr_set_mask.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
-  paged_prefill_kernel<<<grid, kThreads, smem, stream>>>(tm_q, *tk, *tv, prm);
+  paged_prefill_kernel<<<grid, kThreads, smem, stream>>>(tm_q, tk, tv, prm);
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 

@@ -29,7 +29,7 @@ AttentionRunner::~AttentionRunner() {
                      d_q_starts_};
   for (int32_t* b : bufs)
     if (b) cudaFree(b);
-  if (d_q_bf16_) cudaFree(d_q_bf16_);
+  if (d_q_f16_) cudaFree(d_q_f16_);
   void* sbufs[] = {d_temps_, d_pens_, d_uniforms_, d_tokens_, d_hist_offsets_, d_history_};
   for (void* b : sbufs)
     if (b) cudaFree(b);
@@ -96,7 +96,7 @@ bool AttentionRunner::Reserve(size_t n_tokens, size_t n_seqs, size_t max_blocks)
   if (n_tokens > cap_tokens_) {
     const size_t cap = std::max(n_tokens, cap_tokens_ * 2);
     ok = ok && grow(&d_positions_, cap) && grow(&d_slots_, cap) &&
-         grow(&d_q_bf16_, cap * (size_t)cfg_.n_q_heads * cfg_.head_dim);
+         grow(&d_q_f16_, cap * (size_t)cfg_.n_q_heads * cfg_.head_dim);
     cap_tokens_ = ok ? cap : 0;
   }
   if (n_seqs > cap_seqs_ || max_blocks > cap_blocks_) {
@@ -180,10 +180,10 @@ bool AttentionRunner::RunAttentionLayer(int layer, float* q, const float* k, con
   auto* s = reinterpret_cast<nvattn_stream_t>(stream);
   if (is_prefill_) {
     if (nvattn_kv_store_qk_norm_rope(handle_, layer, n_tokens_, q, k, v, q_norm_w, k_norm_w,
-                                     d_positions_, d_slots_, d_q_bf16_, NVATTN_DTYPE_BF16,
+                                     d_positions_, d_slots_, d_q_f16_, NVATTN_DTYPE_F16,
                                      k_cache, v_cache, s) != NVATTN_OK)
       return false;
-    return nvattn_paged_prefill(handle_, layer, n_seqs_, n_tokens_, d_q_bf16_, d_cu_q_,
+    return nvattn_paged_prefill(handle_, layer, n_seqs_, n_tokens_, d_q_f16_, d_cu_q_,
                                 d_q_starts_, d_context_lens_, d_block_tables_, max_blocks_,
                                 max_q_len_, k_cache, v_cache, out, s) == NVATTN_OK;
   }

@@ -105,7 +105,7 @@ class AttentionRunner {
   int32_t* d_context_lens_ = nullptr;
   int32_t* d_cu_q_ = nullptr;
   int32_t* d_q_starts_ = nullptr;
-  uint16_t* d_q_bf16_ = nullptr;
+  uint16_t* d_q_f16_ = nullptr;
 
   // sampling
   std::mt19937 rng_;

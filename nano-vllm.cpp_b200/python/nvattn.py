@@ -24,6 +24,7 @@ ERR_NO_MEMORY = 6
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+DTYPE_F16 = 2
 
 EXPORTED = [
     "nvattn_config_init_qwen3", "nvattn_create", "nvattn_destroy", "nvattn_status_string",
@@ -223,7 +224,7 @@ class Handle:
     def kv_store(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, q_out, k_cache,
                  v_cache, stream=None, check=True):
         import torch
-        dt = DTYPE_BF16 if q_out.dtype == torch.bfloat16 else DTYPE_F32
+        dt = {torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}.get(q_out.dtype, DTYPE_F32)
         st = lib().nvattn_kv_store_qk_norm_rope(
             self._h, layer, positions.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm_w),
             _ptr(k_norm_w), _ptr(positions), _ptr(slots), _ptr(q_out), dt, _ptr(k_cache),

@@ -484,7 +484,7 @@ static void decode_item(void* vctx, int64_t item) {
   const int s = (int)(item / Hkv), kvh = (int)(item % Hkv);
   const int64_t L = c->cl[s];
   key_set ks;
-  const int use_new = c->nk && c->mode == ORC_MODE_GGML;
+  const int use_new = c->nk != NULL;
   if (gather_keys(p, c->mode, c->layer, c->kc, c->vc, c->bt + (int64_t)s * c->max_blocks, L,
                   kvh, use_new ? c->nk + ((int64_t)s * Hkv + kvh) * d : NULL,
                   use_new ? c->nv + ((int64_t)s * Hkv + kvh) * d : NULL, L - 1, 0, &ks) == 0) {
@@ -535,7 +535,7 @@ static void prefill_item(void* vctx, int64_t item) {
   if (r1 > c->cu_q[s + 1]) r1 = c->cu_q[s + 1];
   if (r0 >= r1) return;
   const int64_t P_last = c->q_start[s] + (r1 - 1 - c->cu_q[s]);
-  const int use_new = c->nk && c->mode == ORC_MODE_GGML;
+  const int use_new = c->nk != NULL;
   key_set ks;
   if (gather_keys(p, c->mode, c->layer, c->kc, c->vc, c->bt + (int64_t)s * c->max_blocks,
                   P_last + 1, kvh,

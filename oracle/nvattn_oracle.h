@@ -93,9 +93,11 @@ void orc_qk_norm_rope_store(const orc_params* p, int layer, int n_tokens,
 
 /* ---- paged decode: one query token per sequence, keys [0, context_len) ----
  * q [B][Hq][d] f32, out [B][Hq][d] f32.  block_tables [B][max_blocks].
- * new_k/new_v (nullable, [B][Hkv][d] f32): in GGML mode the newest key
- * (index context_len-1) is taken from these f32 rows (cast to f16) instead of
- * the bf16 cache, as in the reference's decode graph concat. */
+ * new_k/new_v (nullable, [B][Hkv][d] f32): the newest key (index
+ * context_len-1) is taken from these f32 rows instead of the bf16 cache, as
+ * in the reference's decode graph concat (model_runner.cpp:116-124,
+ * qwen3.cpp:648-661); GGML mode casts them to f16, TRUTH uses them as they
+ * are (exact math on the reference's graph values). */
 void orc_paged_decode(const orc_params* p, int mode, int layer, int n_seqs,
                       const float* q, const uint16_t* k_cache,
                       const uint16_t* v_cache, const int32_t* block_tables,
@@ -106,7 +108,8 @@ void orc_paged_decode(const orc_params* p, int mode, int layer, int n_seqs,
  * Sequence s owns query rows [cu_q[s], cu_q[s+1]) at positions
  * q_start[s] + i; a row at position P attends keys [0, P].  Keys come from the
  * cache through the block table.  new_k/new_v (nullable, [T][Hkv][d] f32):
- * in GGML mode keys at positions >= q_start[s] use these f32 rows. */
+ * keys at positions >= q_start[s] use these f32 rows (the reference's graph
+ * rows; GGML mode casts them to f16, TRUTH uses them as they are). */
 void orc_paged_prefill(const orc_params* p, int mode, int layer, int n_seqs,
                        const float* q, const int32_t* cu_q,
                        const int32_t* q_start, const int32_t* context_lens,

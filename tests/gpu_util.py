@@ -24,3 +24,11 @@ def dev(a, device="cuda:0"):
 def host_bits(t):
     """Device int16 tensor of bf16 bits -> numpy uint16."""
     return t.cpu().numpy().view(np.uint16)
+
+
+def prefill_q(q, device="cuda:0"):
+    """Query rows for nvattn_paged_prefill: f16 on the device (round to
+    nearest even; the test cases' bf16-exact values are f16-exact except
+    magnitudes below 2^-17)."""
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(q, dtype=np.float32).astype(np.float16)).to(device)

@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_version_and_status_strings():
-    assert nvattn.version() == (0, 1)
+    assert nvattn.version() == (0, 2)
     for s in range(7):
         assert nvattn.status_string(s)
     assert nvattn.status_string(99) == "unknown status"
@@ -119,3 +119,15 @@ def test_plan_decode_matches_append_decode_kv():
     cl, pos, slot = nvattn.plan_decode([513, 256], bt)
     assert cl.tolist() == [513, 256] and pos.tolist() == [512, 255]
     assert slot.tolist() == [2 * 256 + 0, 1 * 256 + 255]
+
+
+def test_decode_rejects_more_sequences_than_one_launch_holds():
+    """A decode launch covers at most 65535 sequences (its grid's z extent);
+    both decode entry points reject more as an argument error before they
+    touch a device."""
+    cfg = nvattn.qwen3_config(n_layer=1, max_seqs=70000)
+    dummy = ctypes.c_void_p(1 << 20)  # aligned, never dereferenced
+    L = nvattn.lib()
+    st = L.nvattn_paged_decode_noalloc(ctypes.byref(cfg), 0, 65536, dummy, dummy, dummy, dummy, 4,
+                                       dummy, 1024, dummy, None, None)
+    assert st == nvattn.ERR_INVALID_ARG

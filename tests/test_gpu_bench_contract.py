@@ -36,6 +36,6 @@ def test_bench_prints_the_contract_line():
     e2e = d["e2e"]
     assert e2e["value"] > 0 and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] > 0 and e2e["d2h_bytes_per_step"] > 0
-    assert d["gpu_launches"] == 3 * d["steps"]
+    assert d["gpu_launches"] == 2 * d["steps"]
     for key in ("sm_mhz", "sm_max_mhz", "reasons"):
         assert key in d["clocks"], key

@@ -9,7 +9,7 @@ import pytest
 import cases
 import nvattn
 import oracle as O
-from gpu_util import dev, handle
+from gpu_util import dev, handle, prefill_q
 
 pytestmark = pytest.mark.gpu
 
@@ -26,7 +26,7 @@ def prefill_rows(h, c, seqs, starts, ends):
     q = np.concatenate(q_rows)
     out = torch.full((q.shape[0], c.Hq, 128), float("nan"), device="cuda")
     bt = np.ascontiguousarray(c.block_tables[np.asarray(seqs)])
-    h.prefill(c.layer, dev(O.f32_to_bf16(q)), dev(np.asarray(cu, np.int32)),
+    h.prefill(c.layer, prefill_q(q), dev(np.asarray(cu, np.int32)),
               dev(np.asarray(starts, np.int32)), dev(np.asarray(ends, np.int32)), dev(bt),
               int(max(b - a for a, b in zip(starts, ends))), dev(c.cache.k), dev(c.cache.v), out)
     torch.cuda.synchronize()

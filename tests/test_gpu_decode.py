@@ -146,3 +146,76 @@ def test_host_validation(cuda):
     st = h.decode(1, dev(c.q), dev(c.cache.k), dev(c.cache.v), dev(c.block_tables), dev(c.lens),
                   10, out, check=False)
     assert st == nvattn.ERR_INVALID_ARG
+
+
+def test_descriptor_cache_with_more_cache_buffers_than_it_holds(cuda):
+    """One handle decodes over 20 distinct K/V buffer pairs (40 bases, more
+    than the 16 TMA descriptors a handle caches), twice over in different
+    orders and once with K and V swapped: every launch must read the buffers
+    it was given."""
+    import torch
+    Hq, Hkv, nb = 16, 8, 8
+    h = handle(Hq, Hkv, nb, max_seqs=3)
+    cs = [cases.decode_case(600 + i, Hq, Hkv, [300, 1, 900], num_blocks=nb) for i in range(20)]
+    bufs = [(dev(c.cache.k), dev(c.cache.v)) for c in cs]
+    p = cases.oracle_params(Hq, Hkv, cs[0].cache)
+    order = list(range(20)) + [19 - i for i in range(20)] + [3, 17, 3, 0]
+    for n, i in enumerate(order):
+        c = cs[i]
+        kd, vd = bufs[i]
+        swap = n == len(order) - 1
+        if swap:
+            kd, vd = vd, kd
+        out = torch.full((3, Hq, 128), float("nan"), device="cuda")
+        h.decode(0, dev(c.q), kd, vd, dev(c.block_tables), dev(c.lens), 900, out)
+        torch.cuda.synchronize()
+        kh, vh = (c.cache.v, c.cache.k) if swap else (c.cache.k, c.cache.v)
+        ref = O.paged_decode(p, O.MODE_TRUTH, 0, c.q, kh, vh, c.block_tables, c.lens)
+        mx, mr = O.err_stats(out.cpu().numpy(), ref)
+        assert mx <= 1e-4 and mr <= MEAN_REL, (n, i, mx, mr)
+    h.check_device()
+
+
+def test_split_tickets_rearm_across_launches_shapes_and_graph_replays(cuda):
+    """The last split CTA of each (sequence, kv head) merges the partials and
+    re-arms that pair's ticket; launches with other split counts, alternating
+    batch shapes and CUDA-graph replays must each give the first launch's
+    bits."""
+    import torch
+    Hq, Hkv = 32, 8
+    ca = cases.decode_case(70, Hq, Hkv, [9000, 300, 20000, 4100], num_blocks=140)
+    cb = cases.decode_case(71, Hq, Hkv, [700, 33000], num_blocks=140)
+    h = handle(Hq, Hkv, 140, max_seqs=4, max_context=40960)
+
+    def launch(c, out, stream=None):
+        h.decode(0, ins[id(c)][0], ins[id(c)][1], ins[id(c)][2], ins[id(c)][3], ins[id(c)][4],
+                 int(c.lens.max()), out, stream=stream)
+
+    ins = {id(c): (dev(c.q), dev(c.cache.k), dev(c.cache.v), dev(c.block_tables), dev(c.lens))
+           for c in (ca, cb)}
+    outs = {id(c): torch.empty((len(c.lens), Hq, 128), device="cuda") for c in (ca, cb)}
+    first = {}
+    for rep in range(3):
+        for c in (ca, cb):
+            launch(c, outs[id(c)])
+            torch.cuda.synchronize()
+            bits = outs[id(c)].cpu().numpy().view(np.uint32).copy()
+            if rep == 0:
+                first[id(c)] = bits
+                check_truth(outs[id(c)].cpu().numpy(), c)
+            assert np.array_equal(bits, first[id(c)]), (rep, len(c.lens))
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            launch(ca, outs[id(ca)], stream=s)
+            launch(cb, outs[id(cb)], stream=s)
+    for _ in range(3):
+        for c in (ca, cb):
+            outs[id(c)].fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        for c in (ca, cb):
+            assert np.array_equal(outs[id(c)].cpu().numpy().view(np.uint32), first[id(c)])
+    h.check_device()

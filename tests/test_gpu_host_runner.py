@@ -36,10 +36,6 @@ def load(d):
     return arrs
 
 
-def bf16_round(x):
-    return O.bf16_to_f32(O.f32_to_bf16(x))
-
-
 def test_host_runner_prefill_then_decode(cuda, tmp_path):
     assert os.path.exists(BIN), "runner_check not built (run __graft_entry__.build())"
     r = subprocess.run([BIN, str(tmp_path), "3"], capture_output=True, text=True, timeout=300)
@@ -62,7 +58,8 @@ def test_host_runner_prefill_then_decode(cuda, tmp_path):
                               a["q_norm_w"], a["k_norm_w"], pos, slot, kc, vc)
     assert np.array_equal(a["prefill_k_cache"], kc)  # rows written, everything else kept
     assert np.array_equal(a["prefill_v_cache"], vc)
-    ref = O.paged_prefill(p, O.MODE_TRUTH, layer, bf16_round(oq), cu, qs, cl, bt, kc, vc)
+    # exact math on the f32 normed/rotated q (the runner hands the prefill f16 q)
+    ref = O.paged_prefill(p, O.MODE_TRUTH, layer, oq, cu, qs, cl, bt, kc, vc)
     mx, mr = O.err_stats(a["prefill_out"], ref)
     assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
 

@@ -1,5 +1,5 @@
 """GPU parity of nvattn_kv_store_qk_norm_rope against the oracle: the normed,
-rotated q (f32 and bf16) and the bf16 K/V cache rows must match bit for bit
+rotated q (f32, bf16 and f16) and the bf16 K/V cache rows must match bit for bit
 (StorePrefillKV / AppendDecodeKV semantics, model_runner.cpp:248-415)."""
 import numpy as np
 import pytest
@@ -12,13 +12,14 @@ from gpu_util import dev, handle, host_bits
 pytestmark = pytest.mark.gpu
 
 
-def run_store(h, layer, q, k, v, qw, kw, pos, slots, n_slots, Hkv, n_layer=1, q_bf16=False,
+def run_store(h, layer, q, k, v, qw, kw, pos, slots, n_slots, Hkv, n_layer=1, q_dtype="f32",
               cache_fill=0):
     import torch
     kc = torch.full((n_layer, n_slots, Hkv, 128), cache_fill, dtype=torch.int16, device="cuda")
     vc = torch.full_like(kc, cache_fill)
     dq = dev(q)
-    qo = torch.empty(q.shape, dtype=torch.bfloat16 if q_bf16 else torch.float32, device="cuda")
+    dt = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[q_dtype]
+    qo = torch.empty(q.shape, dtype=dt, device="cuda")
     h.kv_store(layer, dq, dev(k), dev(v), dev(qw), dev(kw), dev(pos), dev(slots), qo, kc, vc)
     torch.cuda.synchronize()
     return qo, kc, vc
@@ -40,8 +41,8 @@ def test_golden_fixture_bit_exact(cuda):
 # token boundaries and the (cos, sin) reload path is exercised.
 @pytest.mark.parametrize("Hq,Hkv,T", [(16, 8, 3000), (32, 8, 777), (8, 1, 513), (64, 8, 129),
                                       (8, 1, 20000)])
-@pytest.mark.parametrize("q_bf16", [False, True])
-def test_random_tokens_bit_exact(cuda, Hq, Hkv, T, q_bf16):
+@pytest.mark.parametrize("q_dtype", ["f32", "bf16", "f16"])
+def test_random_tokens_bit_exact(cuda, Hq, Hkv, T, q_dtype):
     rng = np.random.default_rng(Hq * 1000 + T)
     n_layer, layer, num_blocks = 3, 1, (T + 255) // 256 + 2
     n_slots = num_blocks * 256
@@ -53,15 +54,18 @@ def test_random_tokens_bit_exact(cuda, Hq, Hkv, T, q_bf16):
     pos = rng.integers(0, 40960, T).astype(np.int32)
     slots = rng.permutation(n_slots)[:T].astype(np.int32)
     h = handle(Hq, Hkv, num_blocks, n_layer=n_layer)
-    qo, kc, vc = run_store(h, layer, q, k, v, qw, kw, pos, slots, n_slots, Hkv, n_layer, q_bf16)
+    qo, kc, vc = run_store(h, layer, q, k, v, qw, kw, pos, slots, n_slots, Hkv, n_layer, q_dtype)
     h.check_device()
     p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=n_slots)
     okc = np.zeros((n_layer, n_slots, Hkv, 128), np.uint16)
     ovc = np.zeros_like(okc)
     oq = O.qk_norm_rope_store(p, layer, q, k, v, qw, kw, pos, slots, okc, ovc)
-    if q_bf16:
+    if q_dtype == "bf16":
         import torch
         assert np.array_equal(host_bits(qo.view(torch.int16)), O.f32_to_bf16(oq))
+    elif q_dtype == "f16":
+        # round to nearest even (numpy's f32 -> f16 cast; the inputs are finite)
+        assert np.array_equal(qo.cpu().numpy().view(np.uint16), oq.astype(np.float16).view(np.uint16))
     else:
         assert np.array_equal(qo.cpu().numpy().view(np.uint32), oq.view(np.uint32))
     got_k, got_v = host_bits(kc), host_bits(vc)

@@ -1,10 +1,12 @@
 """GPU parity of nvattn_paged_prefill (tcgen05 kernel) against the oracle.
 
-The kernel multiplies bf16 Q and bf16 K on the tensor cores, rounds the
-softmax probabilities P to f16 and converts V to f16 (as the reference's
-ggml_cast does) for the P.V product, and accumulates in fp32.  Tolerances
-(BF16 inputs, FP32 accumulate):
-  * against fp64 math on the same bf16 inputs: max-abs-err <= 2e-2 and
+The kernel takes f16 Q, converts the cache's bf16 K and V tiles to f16 (as
+the reference's ggml_cast does), multiplies f16 Q and K on the tensor cores,
+rounds the softmax probabilities P to f16 for the P.V product, and
+accumulates in fp32.  The cases' queries are bf16 values, which f16 holds
+exactly (but for magnitudes below 2^-17).  Tolerances (BF16 cache, FP32
+accumulate):
+  * against fp64 math on the same inputs: max-abs-err <= 2e-2 and
     mean-rel-err <= 1e-3 (sum|a-b| / sum|b|);
   * against the reference's dtype chain (oracle GGML mode): max-abs-err <= 2e-2
     and mean-rel-err no more than 1e-3 above the chain's own distance from
@@ -17,16 +19,12 @@ import cases
 import make_golden
 import nvattn
 import oracle as O
-from gpu_util import dev, handle
+from gpu_util import dev, handle, prefill_q
 
 pytestmark = pytest.mark.gpu
 
 MAX_ABS = 2e-2
 MEAN_REL = 1e-3
-
-
-def to_bf16_dev(q):
-    return dev(O.f32_to_bf16(q))
 
 
 def run_prefill(c: cases.PrefillCase, h=None, k=None, v=None, block_tables=None):
@@ -38,7 +36,7 @@ def run_prefill(c: cases.PrefillCase, h=None, k=None, v=None, block_tables=None)
     out = torch.full((T, c.Hq, 128), float("nan"), device="cuda")
     max_q = int((c.seq_lens - c.q_starts).max())
     bt = c.block_tables if block_tables is None else block_tables
-    h.prefill(c.layer, to_bf16_dev(c.q), dev(c.cu_q), dev(c.q_starts), dev(c.seq_lens), dev(bt),
+    h.prefill(c.layer, prefill_q(c.q), dev(c.cu_q), dev(c.q_starts), dev(c.seq_lens), dev(bt),
               max_q, dev(c.cache.k if k is None else k), dev(c.cache.v if v is None else v), out)
     torch.cuda.synchronize()
     return h, out.cpu().numpy()

@@ -15,7 +15,7 @@ import pytest
 import cases
 import nvattn
 import oracle as O
-from gpu_util import dev, handle
+from gpu_util import dev, handle, prefill_q
 
 pytestmark = pytest.mark.gpu
 
@@ -35,7 +35,7 @@ class Inputs:
     def __init__(self, c, max_q=None):
         import torch
         self.c = c
-        self.q = dev(O.f32_to_bf16(c.q))
+        self.q = prefill_q(c.q)
         self.cu = dev(c.cu_q)
         self.qs = dev(c.q_starts)
         self.cl = dev(c.seq_lens)

@@ -106,3 +106,36 @@ def test_rank_failure_is_detected_by_the_survivor():
     res = _run("fail")
     assert res[1][0] == "exited"
     assert res[0][0] == "error", res  # the collective ends with an error, no hang
+
+
+def test_bench_reassembles_sharded_cache_rows_and_queries():
+    """bench.py's sharded parity check rebuilds every head from the ranks'
+    pieces; on a sharded copy of a case that must give the original cache
+    rows and queries back, and the oracle over them the unsharded output."""
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import bench
+    import cases
+    import nvattn
+    import oracle as O
+    Hq, Hkv, world = 32, 8, 4
+    c = cases.decode_case(91, Hq, Hkv, [300, 900])
+    need = (c.lens + 255) // 256
+    ids = np.concatenate([c.block_tables[s, :need[s]] for s in range(2)])
+    rows = (ids[:, None] * 256 + np.arange(256)[None]).reshape(-1)
+    kv_ranks, q_ranks = [], []
+    for r in range(world):
+        kv0, kv1, q0, q1 = nvattn.kv_head_shard(Hq, Hkv, world, r)
+        kv_ranks.append(np.concatenate([c.cache.k[0, rows, kv0:kv1], c.cache.v[0, rows, kv0:kv1]]))
+        q_ranks.append(c.q[:, q0:q1])
+    k_full, v_full, q_full, btc = bench.reassemble_shards(np.stack(kv_ranks), np.stack(q_ranks),
+                                                          need)
+    assert np.array_equal(k_full[0], c.cache.k[0, rows])
+    assert np.array_equal(v_full[0], c.cache.v[0, rows])
+    assert np.array_equal(q_full, c.q)
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=k_full.shape[1], n_threads=2)
+    got = O.paged_decode(p, O.MODE_TRUTH, 0, q_full, k_full, v_full, btc, c.lens)
+    pf = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=c.cache.n_slots, n_threads=2)
+    want = O.paged_decode(pf, O.MODE_TRUTH, 0, c.q, c.cache.k, c.cache.v, c.block_tables, c.lens)
+    assert np.array_equal(got, want)
