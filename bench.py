@@ -790,8 +790,8 @@ def allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq, lens
     ids = np.concatenate([bt_np[s, :need[i]] for i, s in enumerate(sel)])
     rows = (torch.from_numpy(ids.astype(np.int64)).to(kc.device)[:, None] * BS
             + torch.arange(BS, device=kc.device)[None]).reshape(-1)
-    mine = torch.cat([kc.index_select(0, rows).view(torch.int16),
-                      vc.index_select(0, rows).view(torch.int16)], 0).contiguous()
+    # bf16 on the wire (NCCL gathers no int16), bit patterns on the host
+    mine = torch.cat([kc.index_select(0, rows), vc.index_select(0, rows)], 0).contiguous()
     theirs = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype, device=mine.device)
     dist.all_gather_into_tensor(theirs, mine)
     qs = q[torch.from_numpy(sel).to(q.device)].contiguous()
@@ -804,7 +804,7 @@ def allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq, lens
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
         k_full, v_full, q_full, btc = reassemble_shards(
-            theirs.cpu().numpy().view(np.uint16), q_all.cpu().numpy(), need)
+            theirs.view(torch.int16).cpu().numpy().view(np.uint16), q_all.cpu().numpy(), need)
         p = O.params(n_q_heads=world * hq, n_kv_heads=k_full.shape[2],
                      n_slots=k_full.shape[1], n_threads=0)
         ref = O.paged_decode(p, O.MODE_TRUTH, 0, q_full, k_full, v_full, btc,
