@@ -605,6 +605,123 @@ def bench_decode_long(args, world, rank, device):
                          "algorithmic_bytes": alg, "frac_of_8tbs": gbs / 8000.0}}
 
 
+def bench_model_step(args, world, rank, device):
+    """The full-model decode step (one GPU): Qwen3-0.6B architecture, 28
+    layers, hidden 1024, 16 q / 8 kv heads, FFN 3072, vocabulary 151936,
+    random N(0, 0.02) bf16 weights, 64 sequences with contexts uniform in
+    [256, 8192] (seeded), greedy sampling.  ModelRunner::Run's decode step
+    (nano-vllm.cpp_b200/python/model_runner.py): libnvattn serves the fused
+    store, paged decode and sampling; embedding, norms, projections, FFN and
+    lm_head run as torch / cuBLAS ops ("not-ggml" -- the reference's ggml is
+    not vendored).  The step (all layers + sampling) is captured once in a
+    CUDA graph; each timed step writes the host planner's positions / slots /
+    block tables and the input tokens into the step's device buffers, replays
+    the graph and reads the 64 tokens back, which feed the next step.  The
+    attention share is a separate graph holding only the 28 layers' store +
+    decode, timed alone."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "nano-vllm.cpp_b200", "python"))
+    import model_runner as MR
+    shape = MR.Qwen3Shape()
+    B, steps, warm = 64, max(10, min(args.steps, 50)), 3
+    rng = np.random.default_rng(SEED + 8)
+    lens = rng.integers(256, 8193, B).astype(np.int64)
+    max_blocks = int((lens.max() + steps + warm + 2 + BS - 1) // BS)
+    num_blocks = int(((lens + steps + warm + 2 + BS - 1) // BS).sum()) + 8
+    w = MR.Qwen3Weights(shape, device, seed=8)
+    run = MR.DecodeRunner(shape, w, num_blocks, B, max_blocks, device)
+    bufs = run.allocate(B)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(8000)
+    for t in (run.k_cache, run.v_cache):
+        for layer in range(shape.n_layer):
+            t[layer].copy_(torch.randn(t[layer].shape, generator=gen, device=device)
+                           .to(torch.bfloat16).view(torch.int16))
+    tables = MR.BlockTables(lens, num_blocks, max_blocks, seed=SEED + 9)
+    tokens = rng.integers(0, shape.vocab, B)
+    stream = torch.cuda.current_stream(device)
+    run.set_inputs(tokens, tables)
+    run.forward()  # eager warm-up (kernel attributes, workspaces)
+    torch.cuda.synchronize(device)
+    run.h.check_device("model_step eager")
+    side = torch.cuda.Stream(device=device)
+    side.wait_stream(stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            run.forward(stream=side)
+    stream.wait_stream(side)
+    host_next = torch.empty(B, dtype=torch.int32).pin_memory()
+
+    def one_step():
+        run.set_inputs(tokens, tables)
+        g.replay()
+        host_next.copy_(bufs["next"], non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        tables.append_token()
+        return host_next.numpy().copy()
+
+    for _ in range(warm):
+        tokens = one_step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall = time.perf_counter()
+    e0.record(stream)
+    dev_ms = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        run.set_inputs(tokens, tables)
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+        host_next.copy_(bufs["next"], non_blocking=True)
+        stream.synchronize()
+        dev_ms.append(a.elapsed_time(b))
+        tables.append_token()
+        tokens = host_next.numpy().copy()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    wall = time.perf_counter() - t_wall
+    e2e_ms = e0.elapsed_time(e1) / steps
+    run.h.check_device("model_step")
+    # attention alone: the 28 layers' fused store + decode on the same inputs
+    q = torch.randn((B, shape.n_q_heads, shape.head_dim), generator=gen, device=device)
+    kv = torch.randn((B, shape.n_kv_heads, shape.head_dim), generator=gen, device=device)
+    qs = [q.clone() for _ in range(shape.n_layer)]
+    run.set_inputs(tokens, tables)
+    ga = torch.cuda.CUDAGraph()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(ga, stream=side):
+            for layer in range(shape.n_layer):
+                run.library_attention(layer, qs[layer], kv, kv, stream=side)
+    stream.wait_stream(side)
+    ga.replay()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(5):
+        ga.replay()
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    attn_ms = a.elapsed_time(b) / 5
+    run.h.check_device("model_step attention")
+    step_ms = statistics.median(dev_ms)
+    kv_bytes = int(tables.lens.sum()) * shape.n_kv_heads * shape.head_dim * 2 * 2 * shape.n_layer
+    del g, ga
+    run.close()
+    return {"workload": "decode_step_qwen3_0p6b_arch_28layers_64seq_ctx256-8192",
+            "ops_outside_attention": "not-ggml: torch / cuBLAS (bf16 weights, f32 residual)",
+            "n_layer": shape.n_layer, "n_seqs": B, "steps": steps,
+            "sum_context_start": int(lens.sum()),
+            "step_ms": step_ms, "tokens_per_s": B / (step_ms / 1e3),
+            "e2e": {"ms_per_step": e2e_ms, "tokens_per_s": B / (e2e_ms / 1e3),
+                    "note": "host planner + H2D inputs + graph replay + D2H tokens per step"},
+            "wall_tokens_per_s": B * steps / wall,
+            "attention_ms": attn_ms, "attention_share": attn_ms / step_ms,
+            "attention_kv_gb_per_step": kv_bytes / 1e9,
+            "attention_gbs": kv_bytes / (attn_ms / 1e3) / 1e9}
+
+
 def bench_sample(args, world, rank, device):
     """Token sampling over the headline batch: 256 rows of Qwen3's 151936
     logits (f32, N(0, 4^2)), temperature 0.8 and repetition penalty 1.2 (the
@@ -1006,10 +1123,15 @@ def main():
                          "4-sequence small batch)")
     ap.add_argument("--no-chunked", dest="chunked", action="store_false",
                     help="skip the chunked-prefill workload")
+    ap.add_argument("--no-model-step", action="store_true",
+                    help="skip the full-model (28-layer) decode step workload")
     ap.add_argument("--no-sample", action="store_true",
                     help="skip the token-sampling workload")
     ap.add_argument("--only-sample", action="store_true",
                     help="run only the token-sampling workload (one JSON line)")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="profiling on one GPU: time rank 0's kv-head shard of an N-way split "
+                         "(the per-GPU work of an N-GPU run)")
     ap.add_argument("--only-prefill", action="store_true",
                     help="skip the decode workload (for profiling the prefill kernel)")
     args = ap.parse_args()
@@ -1052,7 +1174,9 @@ def main():
             dist.destroy_process_group()
         return 0
 
-    hkv, hq = HKV // world, HQ // world
+    ways = world if world > 1 else max(1, args.shard_of)
+    assert HKV % ways == 0, "kv heads must divide across the shards"
+    hkv, hq = HKV // ways, HQ // ways
     B = args.seqs
     lens, bt_np, num_blocks = workload(n_seqs=B)
     max_ctx = int(lens.max())
@@ -1087,9 +1211,10 @@ def main():
     kc16, vc16, w16 = kc.view(torch.int16), vc.view(torch.int16), w.view(torch.int16)
 
     def step():
-        q.copy_(q0)  # the fused kernel writes q in place; keep every step identical
+        # the fused kernel reads the step's q (q0) and writes the normed,
+        # rotated q that decode reads (q)
         ev_z.record(stream)
-        h.kv_store(0, q, k_new, v_new, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
+        h.kv_store(0, q0, k_new, v_new, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
         ev_a.record(stream)
         h.decode(0, q, kc16, vc16, bt, ctx, max_ctx, out, stream=stream)
         ev_b.record(stream)
@@ -1215,7 +1340,7 @@ def main():
     # CPU baseline (rank 0, one GPU): the oracle's ggml-chain decode on the
     # host cores over the workload's first sequences, with this run's K/V.
     cpu_base = None
-    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and ways == 1 and rank == 0 and not args.no_cpu_baseline:
         def host_case(n):
             need = (lens[:n] + BS - 1) // BS
             ids = np.concatenate([bt_np[s, :need[s]] for s in range(n)])
@@ -1241,6 +1366,8 @@ def main():
     prefill_results = run_prefills(args, world, rank, device)
     decode_long = None if args.no_decode_long else bench_decode_long(args, world, rank, device)
     decode_small = None if args.no_decode_long else bench_decode_small(args, world, rank, device)
+    model_step = (bench_model_step(args, world, rank, device)
+                  if world == 1 and not args.no_model_step else None)
     sample = None if args.no_sample else bench_sample(args, world, rank, device)
     prefill_chunked = bench_prefill_chunked(args, world, rank, device) if args.chunked else None
 
@@ -1261,7 +1388,8 @@ def main():
                        "n_seqs": B, "q_heads": HQ, "kv_heads": HKV,
                        "head_dim": D, "block_size": BS, "sum_context": int(lens.sum()),
                        "kv_gb_per_gpu": round(kv_bytes / 1e9, 3),
-                       "parallelism": f"kv-head shard x{world}",
+                       "parallelism": (f"kv-head shard x{world}" if ways == world else
+                                       f"rank 0's kv-head shard of x{ways} on one GPU"),
                        "l2": "inputs larger than L2 (KV cache >> 126 MB), no flush",
                        "allgather": allgather is not None},
             "roofline": {"bound": "hbm", "kernel": "paged_decode (split-KV, merged in-kernel by the last split)",
@@ -1276,6 +1404,7 @@ def main():
             "clocks": clk,
             "decode_long": decode_long,
             "decode_small": decode_small,
+            "model_step": model_step,
             "sample": sample,
             "prefill_chunked": prefill_chunked,
             "kv_store": kv_store_roofline(B, hq, hkv, store_ms, q_out_bytes=4),
