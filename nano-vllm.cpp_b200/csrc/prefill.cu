@@ -1,5 +1,5 @@
 // prefill.cu -- causal paged prefill / prefix-hit / chunked-prefill attention
-// on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+// on the 5th-generation tensor cores (tcgen05 + TMEM, CTA pairs), sm_100a.
 //
 // Replaces the reference's prefill attention: FillCausalMask
 // (src/engine/model_runner.cpp:188-217), the prefill pad/permute
@@ -18,42 +18,53 @@
 // Q, 8 significant bits, put the output ~1.4e-3 mean-rel from exact math on
 // f32 queries; f16 Q, 11 bits, ~2e-4.)
 //
-// A work item is two 128-row query tiles that read the same keys: the two GQA
-// heads of a pair (same rows, same kv head), or, when a kv head serves one q
-// head, two consecutive row tiles.  Keys come in 128-key tiles.  The kernel
-// is persistent (one CTA per SM): the producer takes items in launch order
-// (query tiles of one sequence and kv head together, longest first) from a
-// counter in the handle's workspace and hands each to the other roles
-// through a 2-slot work ring in shared memory, so the next item's Q, first K
-// tile and first S MMAs overlap the current item's last softmax and epilogue,
-// and items without rows cost one counter step instead of a CTA launch.
-//   warp 0       work items from the counter; TMA producer: per item both Q
-//                tiles, then K(j), V(j), K(j+1) ... through a ring of
-//                5 x 32 KiB slots (two 64-column boxes per tile, 128-byte
-//                swizzle) that runs on across items.
-//   warp 1       TMEM allocation; one lane issues the MMAs, interleaving the
-//                two tiles so the tensor core works on one tile while the
-//                other tile's softmax runs:
+// CTA pairs (clusters of two, tcgen05 cta_group::2).  A work item is four
+// 128-row query tiles that read the same keys, two per CTA: four GQA heads
+// of the same rows, or -- when a kv head serves fewer than four q heads --
+// consecutive row tiles.  Keys come in 128-key tiles, and each CTA stages
+// half of every tile: K for keys [64r, 64r+64) of the tile (all 128 dims)
+// and V for dims [64r, 64r+64) (all 128 keys), r = the CTA's rank in the
+// pair.  The pair MMAs (M = 256) read A rows from each CTA's own shared
+// memory or TMEM and B columns from both CTAs' halves, and each CTA's TMEM
+// receives its own 128 rows:
+//   S_t  = Q_t K^T  (M=256 rows of the pair, N=128 keys, K=128 dims)
+//   O_t += P_t V    (A = P from each CTA's TMEM, N=128 dims, K=128 keys)
+// so each SM stages, converts and feeds the tensor core half of each K/V
+// tile, and one thread issues the MMAs of both SMs.  The kernel is
+// persistent (one CTA per SM): the leader (rank 0) takes items in the order a
+// (query tile, kv head, sequence) grid would launch them -- the query tiles
+// of one sequence and kv head together, longest first, which keeps their K/V
+// shared in L2 -- from a counter in the handle's workspace (the last CTA to
+// finish zeroes it) and hands each item to both CTAs' roles through a 2-slot
+// work ring in shared memory; the next item's Q, first K tile and first S
+// MMAs overlap the current item's last softmax and epilogue.
+//   warp 0       leader: work items from the counter into both CTAs' work
+//                rings; both CTAs: TMA producer of the CTA's own Q tiles and
+//                K/V halves through a ring of 16 KiB slots (128-byte swizzle)
+//                that runs on across items.
+//   warp 1       TMEM allocation for the pair; in the leader one lane issues
+//                the pair MMAs, interleaving the two tiles so the tensor cores
+//                work on one tile while the other tile's softmax runs:
 //                  PV0(j), S0(j+1), PV1(j), S1(j+1), ...
-//                S_t = Q_t K^T (M=128, N=128, K=128; f16 A and B K-major, smem)
-//                O_t += P_t V  (A = P from TMEM, B = V MN-major from smem)
-//   warps 12-15  K/V converters (one per SM sub-partition, so the
-//                conversion work does not fall on the sub-partitions of only
-//                some softmax warps): bf16 -> f16 in place, K(j) then V(j);
-//                V rows past the context zeroed (a cache slot past a
-//                sequence's end may hold NaN bits; masked K columns never
-//                reach P).
+//   warps 12-15  K/V converters (one per SM sub-partition): bf16 -> f16 in
+//                place, K(j) then V(j), V rows past the context zeroed (a
+//                cache slot past a sequence's end may hold NaN bits; masked K
+//                columns never reach P).
 //   warps 2-3    idle.
 //   warps 4-7    softmax of tile 0; warps 8-11 softmax of tile 1: thread =
 //                query row = TMEM lane.  Causal mask, online softmax in the
 //                log2 domain, P written as f16 into the TMEM columns of its
 //                own S (S was read to registers), lazy O rescaling (only when
 //                a row max grows by more than 2^8), epilogue O / l.
+// Barriers the leader's MMA lane waits on (K/V converted, P written, work
+// slot free) live in the leader and count both CTAs' arrivals; MMA
+// completions arrive on the barrier at the same offset in both CTAs.
 // MMAs issued by one thread execute in order, so S(j+1) may overwrite the
 // columns of P(j) right after PV(j) is issued, and the completion of S(j+1)
 // implies PV(j) is done (its O may then be rescaled).
-// TMEM columns: tile t uses [256t, 256t+128) for S/P and [256t+128, 256t+256)
-// for O.
+// TMEM columns (each CTA): tile t uses [256t, 256t+128) for S/P and
+// [256t+128, 256t+256) for O.
+#include <algorithm>
 #include <atomic>
 
 #include "common.cuh"
@@ -65,18 +76,19 @@ namespace {
 constexpr int kD = 128;
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // keys per tile
-constexpr int kSlots = 5;
+constexpr int kSlots = 8;
 constexpr int kThreads = 16 * 32;
-constexpr int kConvThreads = 128;         // warps 12-15
-constexpr int kConvAhead = 4;             // converter lead, in key tiles (barrier sets)
-constexpr int kHalfBytes = 128 * 64 * 2;  // one 128-row x 64-column 16-bit box: 16 KiB
+constexpr int kConvThreads = 128;          // warps 12-15
+constexpr int kConvAhead = 4;              // converter lead, in key tiles (barrier sets)
+constexpr int kSlotBytes = 16 * 1024;      // one CTA's half of a K or V tile
+constexpr int kQBoxBytes = 128 * 64 * 2;   // one 128-row x 64-column f16 box
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct PrefillParams {
-  int Hq, Hkv, G, layer, block_size, max_blocks, n_mtiles, pair_heads;
-  int gx, n_items;  // items per (sequence, kv head); items in all
+  int Hq, Hkv, G, layer, block_size, max_blocks, n_mtiles, mode;
+  int gx, n_items;  // pair items per (sequence, kv head); items in all
   int n_tokens;     // rows of q and out
   long long n_slots, num_blocks;
   float scale_log2;
@@ -89,25 +101,31 @@ struct PrefillParams {
   int* sched;  // [0] next work item, [1] CTAs finished; the last CTA zeroes both
 };
 
-// One work item (written by the producer, read by every role).  valid == 0
-// ends the CTA's loop.
+// Item modes: how a pair item's four query tiles are chosen.
+constexpr int kModeHeads = 0;  // four heads of one row tile (G >= 4)
+constexpr int kModePair = 1;   // two heads x two row tiles (G == 2)
+constexpr int kModeRows = 2;   // one head x four row tiles (G == 1)
+
+// One CTA's view of a work item (written by the leader's producer into both
+// CTAs' rings, read by every role).  valid == 0 ends the CTA's loop.
 struct Work {
   int valid, seq, kvh, q0, q_start, ctx, n_kv, p_last0;
   int head[2], row0[2], rows[2];
 };
+constexpr int kWorkWords = sizeof(Work) / 4;
 
 struct __align__(1024) PrefillSmem {
-  uint16_t q[2][2][kBM * 64];        // [tile][d half][row][64]
-  uint16_t kv[kSlots][2][kBN * 64];  // [slot][d half][key][64]
-  uint64_t q_full;
+  uint16_t q[2][2][kBM * 64];     // [tile][d half][row][64]
+  uint16_t kv[kSlots][kBN * 64];  // K half: [d half][64 keys][64]; V half: [128 keys][64]
+  uint64_t q_full;                // leader: both CTAs' Q bytes
   uint64_t full[kSlots], empty[kSlots];
   uint64_t s_full[2], p_full[2];
   // per key tile gj, indexed gj % kConvAhead: converted K / V ready for the
-  // MMAs, and P.V of the tile done (its V slot no longer read)
+  // MMAs (leader), and P.V of the tile done (its V slot no longer read)
   uint64_t k_ready[4], v_ready[4], v_consumed[4];
   uint64_t o_final;
   uint64_t q_empty;                      // the item's last S MMAs have read Q
-  uint64_t work_full[2], work_empty[2];  // the work ring
+  uint64_t work_full[2], work_empty[2];  // the work ring (work_empty: leader)
   Work work[2];
   uint32_t tmem_base;
   int abort_flag;  // raised by the first wait that times out
@@ -117,117 +135,161 @@ struct __align__(1024) PrefillSmem {
 // 227 KiB a CTA may use.
 static_assert(sizeof(PrefillSmem) + 1024 <= 227 * 1024, "prefill shared memory");
 
-// Arrivals that release a work-ring slot: the MMA lane, the 4 converter warps
-// and the 8 softmax warps.
-constexpr int kWorkReaders = 1 + 4 + 8;
+// Arrivals that release a work-ring slot: per CTA the 4 converter warps and
+// the 8 softmax warps, plus the leader's MMA lane and the follower's
+// producer.
+constexpr int kWorkReaders = 2 * (1 + 4 + 8);
+// Arrivals on the leader's per-tile barriers: one per warp of both CTAs.
+constexpr int kPairWarps4 = 2 * 4;
 
 __device__ __forceinline__ int ring_slot(int idx) { return idx % kSlots; }
 __device__ __forceinline__ uint32_t ring_parity(int idx) { return (uint32_t)(idx / kSlots) & 1u; }
 
 // ---------------------------------------------------------------- work items
-// Item `item` in launch order: x fastest, then kv head, then sequence, as a
-// gx x Hkv x n_seqs grid.  Returns false for an item without query rows or
-// with invalid metadata (the latter recorded in the status word).  The items
-// without rows of a (sequence, kv head) are its first x values (longest
-// tiles first); for one of them `skip_to` is the group's first item with rows
-// (or the next group), so the caller can move the counter past the rest.
-__device__ __forceinline__ bool decode_item(const PrefillParams& prm, int item, Work& w,
+// Pair item `item` in launch order: x fastest, then kv head, then sequence,
+// as a gx x Hkv x n_seqs grid.  Fills both CTAs' views.  Returns false for an
+// item without query rows or with invalid metadata (the latter recorded in
+// the status word).  The items without rows of a (sequence, kv head) are its
+// first x values (longest tiles first); for one of them `skip_to` is the
+// group's first item with rows (or the next group), so the caller can move
+// the counter past the rest.
+__device__ __forceinline__ bool decode_item(const PrefillParams& prm, int item, Work (&w)[2],
                                             int& skip_to) {
   const int x = item % prm.gx;
   const int yz = item / prm.gx;
-  w.kvh = yz % prm.Hkv;
-  w.seq = yz / prm.Hkv;
-  if (prm.pair_heads) {
-    const int n_pairs = prm.G / 2;
-    const int mt = prm.n_mtiles - 1 - x / n_pairs;  // longest tiles first
-    const int gp = x % n_pairs;
-    w.head[0] = w.kvh * prm.G + 2 * gp;
-    w.head[1] = w.head[0] + 1;
-    w.row0[0] = w.row0[1] = mt * kBM;
-  } else {
-    const int n_units = (prm.n_mtiles + 1) / 2;
-    const int u = n_units - 1 - x;
-    w.head[0] = w.head[1] = w.kvh * prm.G;
-    w.row0[0] = 2 * u * kBM;
-    w.row0[1] = w.row0[0] + kBM;
+  const int kvh = yz % prm.Hkv;
+  const int seq = yz / prm.Hkv;
+  for (int r = 0; r < 2; ++r) {
+    w[r].kvh = kvh;
+    w[r].seq = seq;
+    if (prm.mode == kModeHeads) {
+      const int per_tile = prm.G / 4;  // pair items per row tile
+      const int mt = prm.n_mtiles - 1 - x / per_tile;
+      const int h0 = kvh * prm.G + 4 * (x % per_tile) + 2 * r;
+      w[r].head[0] = h0;
+      w[r].head[1] = h0 + 1;
+      w[r].row0[0] = w[r].row0[1] = mt * kBM;
+    } else if (prm.mode == kModePair) {
+      const int m = (prm.n_mtiles + 1) / 2 - 1 - x;
+      w[r].head[0] = kvh * 2;
+      w[r].head[1] = kvh * 2 + 1;
+      w[r].row0[0] = w[r].row0[1] = (2 * m + r) * kBM;
+    } else {
+      const int m = (prm.n_mtiles + 3) / 4 - 1 - x;
+      w[r].head[0] = w[r].head[1] = kvh;
+      w[r].row0[0] = (4 * m + 2 * r) * kBM;
+      w[r].row0[1] = w[r].row0[0] + kBM;
+    }
   }
-  w.q0 = prm.cu_q[w.seq];
-  const int q1 = prm.cu_q[w.seq + 1];
-  if (w.q0 < 0 || q1 < w.q0 || q1 > prm.n_tokens) {
+  const int q0 = prm.cu_q[seq];
+  const int q1 = prm.cu_q[seq + 1];
+  if (q0 < 0 || q1 < q0 || q1 > prm.n_tokens) {
     // rows outside q / out: the sequence is skipped (all its items)
     record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 25, q1);
     skip_to = item - x + prm.gx;
     return false;
   }
-  const int n_q = q1 - w.q0;
-  if (n_q > prm.n_mtiles * kBM && x == 0 && w.kvh == 0)
+  const int n_q = q1 - q0;
+  if (n_q > prm.n_mtiles * kBM && x == 0 && kvh == 0)
     record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 21, n_q);
   skip_to = item + 1;
-  if (w.row0[0] >= n_q) {
+  if (w[0].row0[0] >= n_q) {  // the item's first (smallest-row) tile has no rows
     int x_first = prm.gx;
-    if (n_q > 0)
-      x_first = prm.pair_heads
-                    ? (prm.n_mtiles - 1 - (n_q - 1) / kBM) * (prm.G / 2)
-                    : (prm.n_mtiles + 1) / 2 - 1 - (n_q - 1) / (2 * kBM);
+    if (n_q > 0) {
+      const int last = (n_q - 1) / kBM;  // last row tile with rows
+      x_first = prm.mode == kModeHeads  ? (prm.n_mtiles - 1 - last) * (prm.G / 4)
+                : prm.mode == kModePair ? (prm.n_mtiles + 1) / 2 - 1 - last / 2
+                                        : (prm.n_mtiles + 3) / 4 - 1 - last / 4;
+    }
     skip_to = item - x + max(x_first, x + 1);
     return false;
   }
-  w.q_start = prm.q_starts[w.seq];
-  w.rows[0] = min(kBM, n_q - w.row0[0]);
-  w.rows[1] = max(0, min(kBM, n_q - w.row0[1]));
-  w.p_last0 = w.q_start + w.row0[0] + w.rows[0] - 1;
-  const int p_last =
-      w.rows[1] > 0 ? max(w.p_last0, w.q_start + w.row0[1] + w.rows[1] - 1) : w.p_last0;
-  if (w.q_start < 0 || (long long)p_last >= (long long)prm.max_blocks * prm.block_size) {
+  const int q_start = prm.q_starts[seq];
+  int p_last = 0;
+  for (int r = 0; r < 2; ++r)
+    for (int t = 0; t < 2; ++t) {
+      w[r].rows[t] = max(0, min(kBM, n_q - w[r].row0[t]));
+      if (w[r].rows[t] > 0) p_last = max(p_last, q_start + w[r].row0[t] + w[r].rows[t] - 1);
+    }
+  if (q_start < 0 || (long long)p_last >= (long long)prm.max_blocks * prm.block_size) {
     record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 22, p_last);
     return false;
   }
-  w.ctx = prm.context_lens[w.seq];
-  if (w.ctx <= p_last) {
-    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 23, w.ctx);
-    w.ctx = p_last + 1;
+  int ctx = prm.context_lens[seq];
+  if (ctx <= p_last) {
+    record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 23, ctx);
+    ctx = p_last + 1;
   }
-  w.n_kv = p_last / kBN + 1;
-  w.valid = 1;
+  // Rows past a tile's end (or a tile without rows) mimic the item's first
+  // tile's last row, which always exists.
+  const int p_last0 = q_start + w[0].row0[0] + w[0].rows[0] - 1;
+  for (int r = 0; r < 2; ++r) {
+    w[r].q0 = q0;
+    w[r].q_start = q_start;
+    w[r].ctx = ctx;
+    w[r].n_kv = p_last / kBN + 1;
+    w[r].p_last0 = p_last0;
+    w[r].valid = 1;
+  }
   return true;
 }
 
 // Every role runs the same sequence of items, so each keeps the CTA-wide
 // count of key tiles before the current item (`tb`): key tile j of the item
-// is tile gj = tb + j, its K and V are ring loads 2*gj and 2*gj + 1, and the
-// per-tile barriers are in phase gj.
+// is tile gj = tb + j, its K and V halves are ring loads 2*gj and 2*gj + 1,
+// and the per-tile barriers are in phase gj.
 
 // ---------------------------------------------------------------- producer
 __device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap* tm_q,
                                               const CUtensorMap* tm_k, const CUtensorMap* tm_v,
-                                              const PrefillParams& prm) {
+                                              const PrefillParams& prm, uint32_t rank) {
   volatile int* abort_flag = &sm.abort_flag;
   tma_prefetch_desc(tm_q);
   tma_prefetch_desc(tm_k);
   tma_prefetch_desc(tm_v);
+  const uint32_t q_full_leader = smem_peer(&sm.q_full, 0);
   int g = 0;  // ring loads issued so far
   for (int k = 0;; ++k) {
     const int ws = k & 1;
-    if (k >= 2 && !mbar_wait(&sm.work_empty[ws], ((k >> 1) - 1) & 1, prm.status, abort_flag, 45))
-      break;
-    Work& w = sm.work[ws];
-    w.valid = 0;
-    // An earlier launch that timed out leaves its status: take no work then.
-    while (!*abort_flag && !timeout_recorded(prm.status)) {
-      const int item = atomicAdd(prm.sched, 1);
-      int skip_to;
-      if (item >= prm.n_items || decode_item(prm, item, w, skip_to)) break;
-      // Items in (item, skip_to) are empty: nobody needs to take them.
-      if (skip_to > item + 1) atomicMax(prm.sched, skip_to);
+    Work w;
+    if (rank == 0) {
+      // Take the next item for the pair and publish both CTAs' views (after
+      // every reader of the slot, in both CTAs, has released it; a wait that
+      // ran out has raised the abort flag, which ends the work below).
+      if (k >= 2)
+        mbar_wait_cluster(&sm.work_empty[ws], ((k >> 1) - 1) & 1, prm.status, abort_flag, 45);
+      Work pw[2];
+      pw[0].valid = pw[1].valid = 0;
+      // An earlier launch that timed out leaves its status: take no work then.
+      while (!*abort_flag && !timeout_recorded(prm.status)) {
+        const int item = atomicAdd(prm.sched, 1);
+        int skip_to;
+        if (item >= prm.n_items) break;
+        if (decode_item(prm, item, pw, skip_to)) break;
+        pw[0].valid = pw[1].valid = 0;
+        // Items in (item, skip_to) are empty: nobody needs to take them.
+        if (skip_to > item + 1) atomicMax(prm.sched, skip_to);
+      }
+      sm.work[ws] = pw[0];
+      const uint32_t peer = smem_peer(&sm.work[ws], 1);
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(&pw[1]);
+#pragma unroll
+      for (int i = 0; i < kWorkWords; ++i) st_cluster_u32(peer + 4 * i, src[i]);
+      mbar_arrive(&sm.work_full[ws]);
+      mbar_arrive_cluster(smem_peer(&sm.work_full[ws], 1));
+      w = pw[0];
+    } else {
+      if (!mbar_wait_cluster(&sm.work_full[ws], (k >> 1) & 1, prm.status, abort_flag, 45)) break;
+      w = sm.work[ws];
+      mbar_arrive_cluster(smem_peer(&sm.work_empty[ws], 0));
     }
-    mbar_arrive(&sm.work_full[ws]);
     if (!w.valid) break;
     // Q of the previous item is free once its last S MMAs have completed.
     if (k >= 1) mbar_wait(&sm.q_empty, (k - 1) & 1, prm.status, abort_flag, 46);
-    mbar_arrive_expect_tx(&sm.q_full, 4 * kHalfBytes);
+    if (rank == 0) mbar_arrive_expect_tx(&sm.q_full, 2 * 4 * kQBoxBytes);
     for (int t = 0; t < 2; ++t) {
-      tma_load_3d(sm.q[t][0], tm_q, &sm.q_full, 0, w.head[t], w.q0 + w.row0[t]);
-      tma_load_3d(sm.q[t][1], tm_q, &sm.q_full, 64, w.head[t], w.q0 + w.row0[t]);
+      tma_load_3d_pair(sm.q[t][0], tm_q, q_full_leader, 0, w.head[t], w.q0 + w.row0[t]);
+      tma_load_3d_pair(sm.q[t][1], tm_q, q_full_leader, 64, w.head[t], w.q0 + w.row0[t]);
     }
     const int n_loads = 2 * w.n_kv;
     long long bid = 0;
@@ -246,10 +308,16 @@ __device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap
       }
       const int row = (int)((long long)prm.layer * prm.n_slots + bid * prm.block_size +
                             key0 % prm.block_size);
-      const CUtensorMap* map = (i & 1) ? tm_v : tm_k;
-      mbar_arrive_expect_tx(&sm.full[slot], 2 * kHalfBytes);
-      tma_load_3d(sm.kv[slot][0], map, &sm.full[slot], 0, w.kvh, row);
-      tma_load_3d(sm.kv[slot][1], map, &sm.full[slot], 64, w.kvh, row);
+      mbar_arrive_expect_tx(&sm.full[slot], kSlotBytes);
+      if ((i & 1) == 0) {
+        // K: keys [64r, 64r+64) of the tile, both 64-dim halves
+        uint16_t* dst = sm.kv[slot];
+        tma_load_3d(dst, tm_k, &sm.full[slot], 0, w.kvh, row + 64 * (int)rank);
+        tma_load_3d(dst + 64 * 64, tm_k, &sm.full[slot], 64, w.kvh, row + 64 * (int)rank);
+      } else {
+        // V: dims [64r, 64r+64) of all 128 keys
+        tma_load_3d(sm.kv[slot], tm_v, &sm.full[slot], 64 * (int)rank, w.kvh, row);
+      }
     }
     g += n_loads;
   }
@@ -260,29 +328,31 @@ __device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap
 }
 
 // Takes the next item from the work ring (every lane of a warp calls it; lane
-// 0 releases the slot).  Returns false when the CTA's work is over.
+// 0 releases the slot at the leader).  Returns false when the CTA's work is
+// over.
 __device__ __forceinline__ bool next_work(PrefillSmem& sm, const PrefillParams& prm, int k,
                                           int lane, Work& w, int site) {
   const int ws = k & 1;
-  if (!mbar_wait(&sm.work_full[ws], (k >> 1) & 1, prm.status, &sm.abort_flag, site)) return false;
+  if (!mbar_wait_cluster(&sm.work_full[ws], (k >> 1) & 1, prm.status, &sm.abort_flag, site))
+    return false;
   w = sm.work[ws];
   __syncwarp();
-  if (lane == 0) mbar_arrive(&sm.work_empty[ws]);
+  if (lane == 0) mbar_arrive_cluster(smem_peer(&sm.work_empty[ws], 0));
   return w.valid != 0;
 }
 
 // ---------------------------------------------------------------- K/V converters
-// Converts one 128-key tile (two 64-column halves, 2048 16-byte chunks) from
-// bf16 to f16 in place; with zero_from >= 0, keys at or past zero_from are
-// zeroed instead.  Consecutive threads touch consecutive chunks (no bank
-// conflicts).
-__device__ __forceinline__ void convert_tile(uint16_t (&tile)[2][kBN * 64], int c, int zero_from) {
+// Converts one CTA's half tile (16 KiB, 1024 16-byte chunks) from bf16 to f16
+// in place; with zero_from >= 0, V keys at or past zero_from are zeroed
+// instead (the V half is [128 keys][64 dims], one key per 128-byte row).
+// Consecutive threads touch consecutive chunks (no bank conflicts).
+__device__ __forceinline__ void convert_half(uint16_t* tile, int c, int zero_from) {
+  uint8_t* base = reinterpret_cast<uint8_t*>(tile);
 #pragma unroll 4
-  for (int f = c; f < 2 * 128 * 8; f += kConvThreads) {
-    const int half = f >> 10, key = (f & 1023) >> 3;
-    uint4* p = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(tile[half]) + (f & 1023) * 16);
+  for (int f = c; f < kSlotBytes / 16; f += kConvThreads) {
+    uint4* p = reinterpret_cast<uint4*>(base + f * 16);
     uint4 v = *p;
-    if (zero_from < 0 || key < zero_from) {
+    if (zero_from < 0 || (f >> 3) < zero_from) {
       v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
       v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
       v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
@@ -306,106 +376,102 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
   volatile int* abort_flag = &sm.abort_flag;
   const int lane = c & 31;
   int tb = 0;
-  for (int k = 0;; ++k) {
-    // Only the key count and the context length are needed here.
-    const int ws = k & 1;
-    if (!mbar_wait(&sm.work_full[ws], (k >> 1) & 1, prm.status, abort_flag, 49)) break;
-    const int valid = sm.work[ws].valid, n_kv = sm.work[ws].n_kv, ctx = sm.work[ws].ctx;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.work_empty[ws]);
-    if (!valid) break;
-    for (int j = 0; j < n_kv; ++j) {
+  Work w;
+  for (int k = 0; next_work(sm, prm, k, lane, w, 49); ++k) {
+    for (int j = 0; j < w.n_kv; ++j) {
       const int gj = tb + j;
       const int b = gj % kConvAhead;
       const uint32_t ph = (uint32_t)(gj / kConvAhead) & 1u;
       if (gj >= kConvAhead) mbar_wait(&sm.v_consumed[b], ph ^ 1u, prm.status, abort_flag, 43);
       const int kidx = 2 * gj, vidx = 2 * gj + 1;
       mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 50);
-      convert_tile(sm.kv[ring_slot(kidx)], c, -1);
-      if (lane == 0) mbar_arrive(&sm.k_ready[b]);
+      convert_half(sm.kv[ring_slot(kidx)], c, -1);
+      if (lane == 0) mbar_arrive_cluster(smem_peer(&sm.k_ready[b], 0));
       mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 44);
       const int key0 = j * kBN;
-      convert_tile(sm.kv[ring_slot(vidx)], c, ctx - key0 < kBN ? max(ctx - key0, 0) : -1);
-      if (lane == 0) mbar_arrive(&sm.v_ready[b]);
+      convert_half(sm.kv[ring_slot(vidx)], c, w.ctx - key0 < kBN ? max(w.ctx - key0, 0) : -1);
+      if (lane == 0) mbar_arrive_cluster(smem_peer(&sm.v_ready[b], 0));
     }
-    tb += n_kv;
+    tb += w.n_kv;
   }
 }
 
 // ---------------------------------------------------------------- MMA issuer
+// Leader only.
 __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
                                          const PrefillParams& prm) {
   volatile int* abort_flag = &sm.abort_flag;
-  constexpr uint32_t idesc_s = umma_idesc_f16_f32(kBM, kBN, 0, 0);
-  constexpr uint32_t idesc_o = umma_idesc_f16_f32(kBM, kD, 0, 1);
+  constexpr uint32_t idesc_s = umma_idesc_f16_f32(2 * kBM, kBN, 0, 0);
+  constexpr uint32_t idesc_o = umma_idesc_f16_f32(2 * kBM, kD, 0, 1);
   auto issue_s = [&](int t, int gj) {
-    const int slot = ring_slot(2 * gj);
+    const uint32_t kbase = smem_u32(sm.kv[ring_slot(2 * gj)]);
 #pragma unroll
     for (int k = 0; k < kD / 16; ++k) {
       const uint32_t koff = (uint32_t)(k & 3) * 32;
       const uint64_t a = umma_desc_sw128(smem_u32(sm.q[t][k >> 2]) + koff, 16, 1024);
-      const uint64_t b = umma_desc_sw128(smem_u32(sm.kv[slot][k >> 2]) + koff, 16, 1024);
-      umma_bf16(tmem + t * 256, a, b, idesc_s, k > 0 ? 1u : 0u);
+      const uint64_t b =
+          umma_desc_sw128(kbase + (uint32_t)(k >> 2) * (64 * 128) + koff, 16, 1024);
+      umma_pair_ss(tmem + t * 256, a, b, idesc_s, k > 0 ? 1u : 0u);
     }
   };
   auto issue_pv = [&](int t, int gj, bool accumulate) {
-    const uint32_t vbase = smem_u32(sm.kv[ring_slot(2 * gj + 1)][0]);
+    const uint32_t vbase = smem_u32(sm.kv[ring_slot(2 * gj + 1)]);
 #pragma unroll
     for (int k = 0; k < kBN / 16; ++k) {
-      const uint64_t b = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kHalfBytes, 1024);
-      umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, b, idesc_o,
+      const uint64_t b = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kSlotBytes, 1024);
+      umma_pair_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, b, idesc_o,
                    (accumulate || k > 0) ? 1u : 0u);
     }
   };
   int tb = 0, k = 0;
   for (;; ++k) {
     const int ws = k & 1;
-    if (!mbar_wait(&sm.work_full[ws], (k >> 1) & 1, prm.status, abort_flag, 48)) break;
+    if (!mbar_wait_cluster(&sm.work_full[ws], (k >> 1) & 1, prm.status, abort_flag, 48)) break;
     const int valid = sm.work[ws].valid, n_kv = sm.work[ws].n_kv;
-    mbar_arrive(&sm.work_empty[ws]);
+    mbar_arrive_cluster(smem_peer(&sm.work_empty[ws], 0));
     if (!valid) break;
     mbar_wait(&sm.q_full, k & 1, prm.status, abort_flag, 31);
-    mbar_wait(&sm.k_ready[tb % kConvAhead], (uint32_t)(tb / kConvAhead) & 1u, prm.status,
-              abort_flag, 32);
+    mbar_wait_cluster(&sm.k_ready[tb % kConvAhead], (uint32_t)(tb / kConvAhead) & 1u, prm.status,
+                      abort_flag, 32);
     tc_fence_after();
     // S_t(0) overwrites the S/P columns of the previous item: its P.V MMAs
     // were issued before and execute first.  Its O columns are rewritten by
     // the first P.V below, which waits for P_t(0), i.e. for the softmax warps
     // to have read the previous O out in their epilogue.
     issue_s(0, tb);
-    umma_commit(&sm.s_full[0]);
+    umma_commit_pair(&sm.s_full[0]);
     issue_s(1, tb);
-    umma_commit(&sm.s_full[1]);
-    umma_commit(&sm.empty[ring_slot(2 * tb)]);
-    if (n_kv == 1) umma_commit(&sm.q_empty);
+    umma_commit_pair(&sm.s_full[1]);
+    umma_commit_pair(&sm.empty[ring_slot(2 * tb)]);
+    if (n_kv == 1) umma_commit_pair(&sm.q_empty);
     for (int j = 0; j < n_kv; ++j) {
       const int gj = tb + j;
       const int vidx = 2 * gj + 1, kidx = 2 * gj + 2;
-      mbar_wait(&sm.v_ready[gj % kConvAhead], (uint32_t)(gj / kConvAhead) & 1u, prm.status,
-                abort_flag, 33);
-      mbar_wait(&sm.p_full[0], gj & 1, prm.status, abort_flag, 34);
+      mbar_wait_cluster(&sm.v_ready[gj % kConvAhead], (uint32_t)(gj / kConvAhead) & 1u,
+                        prm.status, abort_flag, 33);
+      mbar_wait_cluster(&sm.p_full[0], gj & 1, prm.status, abort_flag, 34);
       tc_fence_after();
       issue_pv(0, gj, j > 0);
       if (j + 1 < n_kv) {
-        mbar_wait(&sm.k_ready[(gj + 1) % kConvAhead], (uint32_t)((gj + 1) / kConvAhead) & 1u,
-                  prm.status, abort_flag, 35);
+        mbar_wait_cluster(&sm.k_ready[(gj + 1) % kConvAhead],
+                          (uint32_t)((gj + 1) / kConvAhead) & 1u, prm.status, abort_flag, 35);
         tc_fence_after();
         issue_s(0, gj + 1);
-        umma_commit(&sm.s_full[0]);
+        umma_commit_pair(&sm.s_full[0]);
       }
-      mbar_wait(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
+      mbar_wait_cluster(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
       tc_fence_after();
       issue_pv(1, gj, j > 0);
-      umma_commit(&sm.v_consumed[gj % kConvAhead]);
-      umma_commit(&sm.empty[ring_slot(vidx)]);
+      umma_commit_pair(&sm.v_consumed[gj % kConvAhead]);
+      umma_commit_pair(&sm.empty[ring_slot(vidx)]);
       if (j + 1 < n_kv) {
         issue_s(1, gj + 1);
-        umma_commit(&sm.s_full[1]);
-        umma_commit(&sm.empty[ring_slot(kidx)]);
-        if (j + 2 == n_kv) umma_commit(&sm.q_empty);
+        umma_commit_pair(&sm.s_full[1]);
+        umma_commit_pair(&sm.empty[ring_slot(kidx)]);
+        if (j + 2 == n_kv) umma_commit_pair(&sm.q_empty);
       }
     }
-    umma_commit(&sm.o_final);
+    umma_commit_pair(&sm.o_final);
     tb += n_kv;
   }
   // Drain: every MMA has completed before TMEM is released.
@@ -424,6 +490,7 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
   const uint32_t o_col = s_col + 128;
   const float sc = prm.scale_log2;
   const uint64_t sc2 = pack2(sc, sc);
+  const uint32_t p_full_leader = smem_peer(&sm.p_full[t], 0);
   int tb = 0;
   Work w;
   for (int k = 0; next_work(sm, prm, k, lane, w, 47); ++k) {
@@ -515,7 +582,7 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full[t]);
+      if (lane == 0) mbar_arrive_cluster(p_full_leader);
     }
 
     // ---- epilogue: O_t / l.  The next item's first P.V (which rewrites O_t)
@@ -540,7 +607,7 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, PrefillParams prm) {
@@ -549,6 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
     mbar_init(&sm.q_empty, 1);
@@ -557,13 +625,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm.empty[i], 1);
     }
     for (int i = 0; i < kConvAhead; ++i) {
-      mbar_init(&sm.k_ready[i], kConvThreads / 32);
-      mbar_init(&sm.v_ready[i], kConvThreads / 32);
+      mbar_init(&sm.k_ready[i], kPairWarps4);
+      mbar_init(&sm.v_ready[i], kPairWarps4);
       mbar_init(&sm.v_consumed[i], 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.p_full[t], 4);
+      mbar_init(&sm.p_full[t], kPairWarps4);
       mbar_init(&sm.work_full[t], 1);
       mbar_init(&sm.work_empty[t], kWorkReaders);
     }
@@ -572,11 +640,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(&sm.tmem_base, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(&sm.tmem_base, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
-  __syncthreads();
+  // Both CTAs' barriers exist before either CTA arrives on the other's.
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
@@ -585,8 +654,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // take 184 each (128*96 + 128*40 + 256*184 = 64512 <= 65536 = 512*128).
   if (warp < 4) {
     regs_dec<96>();
-    if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm);
-    if (warp == 1 && lane == 0) mma_role(sm, tmem, prm);
+    if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm, rank);
+    if (warp == 1 && lane == 0 && rank == 0) mma_role(sm, tmem, prm);
   } else if (warp >= 12) {
     regs_dec<40>();
     converter_role(sm, prm, threadIdx.x - 384);
@@ -597,9 +666,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  // Neither CTA leaves (or frees TMEM) while the other may still arrive on
+  // its barriers or run pair MMAs on its memory.
+  cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc_pair(tmem, kTmemCols);
   }
   // The last CTA to finish zeroes the work counter for the next launch
   // (every CTA has taken its last item before it counts itself finished).
@@ -628,8 +700,9 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
                            (uint64_t)Hq * kD * 2, 64, 1, kBM, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
   if (st != NVATTN_OK) return st;
+  // K halves: boxes of 64 keys x 64 dims; V halves: 128 keys x 64 dims.
   CUtensorMap tk, tv;
-  st = get_cache_tensor_map(h, k_cache, 64, kBN, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
+  st = get_cache_tensor_map(h, k_cache, 64, kBN / 2, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
   if (st != NVATTN_OK) return st;
   st = get_cache_tensor_map(h, v_cache, 64, kBN, CU_TENSOR_MAP_SWIZZLE_128B, &tv);
   if (st != NVATTN_OK) return st;
@@ -642,7 +715,7 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   prm.block_size = h->cfg.block_size;
   prm.max_blocks = max_blocks;
   prm.n_mtiles = (max_q_len + kBM - 1) / kBM;
-  prm.pair_heads = prm.G >= 2 ? 1 : 0;
+  prm.mode = prm.G >= 4 ? kModeHeads : prm.G == 2 ? kModePair : kModeRows;
   prm.n_slots = h->n_slots;
   prm.num_blocks = h->cfg.num_blocks;
   prm.scale_log2 = h->cfg.scale * kLog2e;
@@ -654,17 +727,19 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   prm.status = h->status_dev;
   prm.sched = h->prefill_sched_dev;
 
-  const long long gx = prm.pair_heads ? (long long)prm.n_mtiles * (prm.G / 2)
-                                      : (long long)(prm.n_mtiles + 1) / 2;
+  const long long gx = prm.mode == kModeHeads  ? (long long)prm.n_mtiles * (prm.G / 4)
+                       : prm.mode == kModePair ? (long long)(prm.n_mtiles + 1) / 2
+                                               : (long long)(prm.n_mtiles + 3) / 4;
   const long long n_items = gx * Hkv * (long long)n_seqs;
   if (n_items <= 0) return NVATTN_OK;
-  // The counter overshoots n_items by at most one step per CTA.
+  // The counter overshoots n_items by at most one step per pair.
   if (n_items > 0x7fffffffLL - h->sm_count) return NVATTN_ERR_UNSUPPORTED;
   prm.gx = (int)gx;
   prm.n_items = (int)n_items;
   prm.n_tokens = n_tokens;
-  // Persistent: one CTA per SM (the shared-memory footprint allows no more).
-  const int grid = (int)std::min<long long>(n_items, h->sm_count);
+  // Persistent: one CTA per SM (the shared-memory footprint allows no more),
+  // in pairs.
+  const int pairs = (int)std::min<long long>(n_items, std::max(1, h->sm_count / 2));
   const size_t smem = sizeof(PrefillSmem) + 1024;
   // The attribute is per device; remember which devices have it.
   // (atomic: handles on different threads may launch at the same time)
@@ -677,7 +752,7 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
       return NVATTN_ERR_CUDA;
     if (dev < 64) attr_set_mask.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
-  paged_prefill_kernel<<<grid, kThreads, smem, stream>>>(tm_q, tk, tv, prm);
+  paged_prefill_kernel<<<2 * pairs, kThreads, smem, stream>>>(tm_q, tk, tv, prm);
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 
