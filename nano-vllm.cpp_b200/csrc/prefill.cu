@@ -57,7 +57,8 @@
 //                own S (S was read to registers), lazy O rescaling (only when
 //                a row max grows by more than 2^8), epilogue O / l.
 // Barriers the leader's MMA lane waits on (K/V converted, P written, work
-// slot free) live in the leader and count both CTAs' arrivals; MMA
+// slot free) live in the leader and count both CTAs' arrivals (the leader's
+// warps arrive locally, the follower's with a cluster-scope release); MMA
 // completions arrive on the barrier at the same offset in both CTAs.
 // MMAs issued by one thread execute in order, so S(j+1) may overwrite the
 // columns of P(j) right after PV(j) is issued, and the completion of S(j+1)
@@ -76,7 +77,7 @@ namespace {
 constexpr int kD = 128;
 constexpr int kBM = 128;  // query rows per tile
 constexpr int kBN = 128;  // keys per tile
-constexpr int kSlots = 8;
+constexpr int kSlots = 10;
 constexpr int kThreads = 16 * 32;
 constexpr int kConvThreads = 128;          // warps 12-15
 constexpr int kConvAhead = 4;              // converter lead, in key tiles (barrier sets)
@@ -341,6 +342,16 @@ __device__ __forceinline__ bool next_work(PrefillSmem& sm, const PrefillParams& 
   return w.valid != 0;
 }
 
+// Arrives on the pair leader's copy of barrier `bar`: a local arrive in the
+// leader (release at CTA scope), a remote one with cluster-scope release in
+// the follower.
+__device__ __forceinline__ void arrive_leader(uint64_t* bar, bool leader) {
+  if (leader)
+    mbar_arrive(bar);
+  else
+    mbar_arrive_cluster(smem_peer(bar, 0));
+}
+
 // ---------------------------------------------------------------- K/V converters
 // Converts one CTA's half tile (16 KiB, 1024 16-byte chunks) from bf16 to f16
 // in place; with zero_from >= 0, V keys at or past zero_from are zeroed
@@ -372,7 +383,8 @@ __device__ __forceinline__ void convert_half(uint16_t* tile, int c, int zero_fro
 // per key tile mod kConvAhead; tile gj waits for P.V of tile gj-kConvAhead
 // (which has waited k_ready / v_ready of that tile), so no barrier runs more
 // than one phase ahead of its waiter.
-__device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillParams& prm, int c) {
+__device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillParams& prm, int c,
+                                               bool leader) {
   volatile int* abort_flag = &sm.abort_flag;
   const int lane = c & 31;
   int tb = 0;
@@ -386,11 +398,11 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
       const int kidx = 2 * gj, vidx = 2 * gj + 1;
       mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 50);
       convert_half(sm.kv[ring_slot(kidx)], c, -1);
-      if (lane == 0) mbar_arrive_cluster(smem_peer(&sm.k_ready[b], 0));
+      if (lane == 0) arrive_leader(&sm.k_ready[b], leader);
       mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 44);
       const int key0 = j * kBN;
       convert_half(sm.kv[ring_slot(vidx)], c, w.ctx - key0 < kBN ? max(w.ctx - key0, 0) : -1);
-      if (lane == 0) mbar_arrive_cluster(smem_peer(&sm.v_ready[b], 0));
+      if (lane == 0) arrive_leader(&sm.v_ready[b], leader);
     }
     tb += w.n_kv;
   }
@@ -480,7 +492,8 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
 
 // ---------------------------------------------------------------- softmax
 __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
-                                             const PrefillParams& prm, int warp, int lane) {
+                                             const PrefillParams& prm, int warp, int lane,
+                                             bool leader) {
   volatile int* abort_flag = &sm.abort_flag;
   const int t = (warp - 4) >> 2;  // query tile
   const int quad = warp & 3;      // TMEM lanes [32*quad, 32*quad+32)
@@ -490,7 +503,6 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
   const uint32_t o_col = s_col + 128;
   const float sc = prm.scale_log2;
   const uint64_t sc2 = pack2(sc, sc);
-  const uint32_t p_full_leader = smem_peer(&sm.p_full[t], 0);
   int tb = 0;
   Work w;
   for (int k = 0; next_work(sm, prm, k, lane, w, 47); ++k) {
@@ -582,7 +594,7 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(p_full_leader);
+      if (lane == 0) arrive_leader(&sm.p_full[t], leader);
     }
 
     // ---- epilogue: O_t / l.  The next item's first P.V (which rewrites O_t)
@@ -658,10 +670,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 1 && lane == 0 && rank == 0) mma_role(sm, tmem, prm);
   } else if (warp >= 12) {
     regs_dec<40>();
-    converter_role(sm, prm, threadIdx.x - 384);
+    converter_role(sm, prm, threadIdx.x - 384, rank == 0);
   } else {
     regs_inc<184>();
-    softmax_role(sm, tmem, prm, warp, lane);
+    softmax_role(sm, tmem, prm, warp, lane, rank == 0);
   }
 
   tc_fence_before();
