@@ -250,6 +250,21 @@ NVATTN_API nvattn_status nvattn_kv_store_qk_norm_rope(
     const int32_t* slot_mapping_dev, void* q_out_dev, nvattn_dtype q_out_dtype,
     uint16_t* k_cache_dev, uint16_t* v_cache_dev, nvattn_stream_t stream);
 
+/* nvattn_kv_store_qk_norm_rope that also writes the step's own K rows
+ * (normed, rotated) and V rows as f16 -- the reference's F16 cast of its
+ * graph's f32 rows (ggml_cast in BuildAttention, qwen3.cpp:388-393; round to
+ * nearest even) -- for nvattn_paged_prefill_rows:
+ *   k_rows_f16_dev, v_rows_f16_dev [n_tokens][n_kv_heads][head_dim] f16
+ * (also for rows whose slot is < 0).  Everything else as
+ * nvattn_kv_store_qk_norm_rope. */
+NVATTN_API nvattn_status nvattn_kv_store_qk_norm_rope_rows(
+    nvattn_handle* h, int layer, int n_tokens, const float* q_dev,
+    const float* k_dev, const float* v_dev, const uint16_t* q_norm_w_dev,
+    const uint16_t* k_norm_w_dev, const int32_t* positions_dev,
+    const int32_t* slot_mapping_dev, void* q_out_dev, nvattn_dtype q_out_dtype,
+    uint16_t* k_cache_dev, uint16_t* v_cache_dev, uint16_t* k_rows_f16_dev,
+    uint16_t* v_rows_f16_dev, nvattn_stream_t stream);
+
 /* Paged GQA decode: for each sequence s, one query row per q head attends
  * keys [0, context_lens[s]) of layer `layer`, read through
  * block_tables[s][t / block_size].  The new token's K/V must already be in
@@ -289,6 +304,25 @@ NVATTN_API nvattn_status nvattn_paged_prefill(
     const int32_t* q_starts_dev, const int32_t* context_lens_dev,
     const int32_t* block_tables_dev, int max_blocks, int max_q_len,
     const uint16_t* k_cache_dev, const uint16_t* v_cache_dev, float* out_dev,
+    nvattn_stream_t stream);
+
+/* nvattn_paged_prefill where the keys and values at or past each sequence's
+ * cached prefix (positions q_starts[s] .. q_starts[s] + its row count - 1)
+ * are the step's own rows as nvattn_kv_store_qk_norm_rope_rows wrote them in
+ * f16 (row cu_q_lens[s] + position - q_starts[s]), while the prefix comes
+ * from the BF16 cache.  This is the reference's prefill attention
+ * (qwen3.cpp:461-533, model_runner.cpp:188-217), which attends the batch's
+ * own graph rows cast to F16, extended to a cached prefix; the plain
+ * nvattn_paged_prefill attends the step's rows as the BF16 cache holds them
+ * (what every later step reads), which moves a prompt's outputs by the
+ * cache's rounding (~2e-3 mean-rel on a prompt without prefix). */
+NVATTN_API nvattn_status nvattn_paged_prefill_rows(
+    nvattn_handle* h, int layer, int n_seqs, int n_tokens,
+    const uint16_t* q_dev, const int32_t* cu_q_lens_dev,
+    const int32_t* q_starts_dev, const int32_t* context_lens_dev,
+    const int32_t* block_tables_dev, int max_blocks, int max_q_len,
+    const uint16_t* k_cache_dev, const uint16_t* v_cache_dev,
+    const uint16_t* k_rows_f16_dev, const uint16_t* v_rows_f16_dev, float* out_dev,
     nvattn_stream_t stream);
 
 /* ---- decode without any allocation -------------------------------------- */

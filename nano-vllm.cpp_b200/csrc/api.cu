@@ -249,10 +249,12 @@ nvattn_status nvattn_get_error(nvattn_handle* h, int64_t* detail) {
     return NVATTN_ERR_CUDA;
   if (st.code != 0 && cudaMemset(h->status_dev, 0, sizeof(st)) != cudaSuccess)
     return NVATTN_ERR_CUDA;
-  // A decode launch cut short by a timeout may leave split tickets taken.
+  // A launch cut short by a timeout may leave split tickets taken (and, in
+  // the worst case, a work counter short of its reset).
   if (st.code == NVATTN_ERR_TIMEOUT &&
-      cudaMemset(h->decode_tickets, 0,
-                 (size_t)h->cfg.max_seqs * h->cfg.n_kv_heads * sizeof(int)) != cudaSuccess)
+      (cudaMemset(h->decode_tickets, 0,
+                  (size_t)h->cfg.max_seqs * h->cfg.n_kv_heads * sizeof(int)) != cudaSuccess ||
+       cudaMemset(h->prefill_sched_dev, 0, 2 * sizeof(int)) != cudaSuccess))
     return NVATTN_ERR_CUDA;
   if (detail) *detail = st.detail;
   return (nvattn_status)st.code;
@@ -398,14 +400,17 @@ nvattn_status nvattn_sample(nvattn_handle* h, int n_seqs, int n_vocab, const flo
                                tokens_dev, st);
 }
 
-nvattn_status nvattn_kv_store_qk_norm_rope(nvattn_handle* h, int layer, int n_tokens,
-                                           const float* q_dev, const float* k_dev,
-                                           const float* v_dev, const uint16_t* q_norm_w_dev,
-                                           const uint16_t* k_norm_w_dev,
-                                           const int32_t* positions_dev,
-                                           const int32_t* slot_mapping_dev, void* q_out_dev,
-                                           nvattn_dtype q_out_dtype, uint16_t* k_cache_dev,
-                                           uint16_t* v_cache_dev, nvattn_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+nvattn_status kv_store_common(nvattn_handle* h, int layer, int n_tokens, const float* q_dev,
+                              const float* k_dev, const float* v_dev,
+                              const uint16_t* q_norm_w_dev, const uint16_t* k_norm_w_dev,
+                              const int32_t* positions_dev, const int32_t* slot_mapping_dev,
+                              void* q_out_dev, nvattn_dtype q_out_dtype, uint16_t* k_cache_dev,
+                              uint16_t* v_cache_dev, uint16_t* k_rows_dev, uint16_t* v_rows_dev,
+                              nvattn_stream_t stream) {
   if (h == nullptr || layer < 0 || layer >= h->cfg.n_layer || n_tokens < 0)
     return NVATTN_ERR_INVALID_ARG;
   if (q_out_dtype != NVATTN_DTYPE_F32 && q_out_dtype != NVATTN_DTYPE_BF16 &&
@@ -417,12 +422,68 @@ nvattn_status nvattn_kv_store_qk_norm_rope(nvattn_handle* h, int layer, int n_to
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return NVATTN_ERR_INVALID_ARG;
   if (positions_dev == nullptr || slot_mapping_dev == nullptr) return NVATTN_ERR_INVALID_ARG;
+  if ((k_rows_dev != nullptr && !aligned16(k_rows_dev)) ||
+      (v_rows_dev != nullptr && !aligned16(v_rows_dev)))
+    return NVATTN_ERR_INVALID_ARG;
   DeviceGuard guard(h->cfg.device);
   if (!guard.ok()) return NVATTN_ERR_CUDA;
   return nvattn::launch_kv_store(h, layer, n_tokens, q_dev, k_dev, v_dev, q_norm_w_dev,
                                  k_norm_w_dev, positions_dev, slot_mapping_dev, q_out_dev,
-                                 q_out_dtype, k_cache_dev, v_cache_dev,
+                                 q_out_dtype, k_cache_dev, v_cache_dev, k_rows_dev, v_rows_dev,
                                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+nvattn_status prefill_common(nvattn_handle* h, int layer, int n_seqs, int n_tokens,
+                             const uint16_t* q_dev, const int32_t* cu_q_lens_dev,
+                             const int32_t* q_starts_dev, const int32_t* context_lens_dev,
+                             const int32_t* block_tables_dev, int max_blocks, int max_q_len,
+                             const uint16_t* k_cache_dev, const uint16_t* v_cache_dev,
+                             const uint16_t* k_rows_dev, const uint16_t* v_rows_dev,
+                             float* out_dev, nvattn_stream_t stream) {
+  if (h == nullptr || layer < 0 || layer >= h->cfg.n_layer || n_seqs < 0 ||
+      n_seqs > h->cfg.max_seqs || n_tokens < 0 || max_blocks <= 0 || max_q_len < 0)
+    return NVATTN_ERR_INVALID_ARG;
+  if (n_seqs == 0 || n_tokens == 0) return NVATTN_OK;
+  if (!q_dev || !cu_q_lens_dev || !q_starts_dev || !context_lens_dev || !block_tables_dev ||
+      !k_cache_dev || !v_cache_dev || !out_dev || !aligned16(q_dev) || !aligned16(out_dev) ||
+      !aligned16(k_cache_dev) || !aligned16(v_cache_dev))
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  return nvattn::launch_paged_prefill(h, layer, n_seqs, n_tokens, q_dev, cu_q_lens_dev,
+                                      q_starts_dev, context_lens_dev, block_tables_dev,
+                                      max_blocks, max_q_len, k_cache_dev, v_cache_dev,
+                                      k_rows_dev, v_rows_dev, out_dev,
+                                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+nvattn_status nvattn_kv_store_qk_norm_rope(nvattn_handle* h, int layer, int n_tokens,
+                                           const float* q_dev, const float* k_dev,
+                                           const float* v_dev, const uint16_t* q_norm_w_dev,
+                                           const uint16_t* k_norm_w_dev,
+                                           const int32_t* positions_dev,
+                                           const int32_t* slot_mapping_dev, void* q_out_dev,
+                                           nvattn_dtype q_out_dtype, uint16_t* k_cache_dev,
+                                           uint16_t* v_cache_dev, nvattn_stream_t stream) {
+  return kv_store_common(h, layer, n_tokens, q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev,
+                         positions_dev, slot_mapping_dev, q_out_dev, q_out_dtype, k_cache_dev,
+                         v_cache_dev, nullptr, nullptr, stream);
+}
+
+nvattn_status nvattn_kv_store_qk_norm_rope_rows(
+    nvattn_handle* h, int layer, int n_tokens, const float* q_dev, const float* k_dev,
+    const float* v_dev, const uint16_t* q_norm_w_dev, const uint16_t* k_norm_w_dev,
+    const int32_t* positions_dev, const int32_t* slot_mapping_dev, void* q_out_dev,
+    nvattn_dtype q_out_dtype, uint16_t* k_cache_dev, uint16_t* v_cache_dev,
+    uint16_t* k_rows_f16_dev, uint16_t* v_rows_f16_dev, nvattn_stream_t stream) {
+  if (k_rows_f16_dev == nullptr || v_rows_f16_dev == nullptr) return NVATTN_ERR_INVALID_ARG;
+  return kv_store_common(h, layer, n_tokens, q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev,
+                         positions_dev, slot_mapping_dev, q_out_dev, q_out_dtype, k_cache_dev,
+                         v_cache_dev, k_rows_f16_dev, v_rows_f16_dev, stream);
 }
 
 nvattn_status nvattn_paged_decode(nvattn_handle* h, int layer, int n_seqs, const float* q_dev,
@@ -454,20 +515,27 @@ nvattn_status nvattn_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
                                    const int32_t* block_tables_dev, int max_blocks, int max_q_len,
                                    const uint16_t* k_cache_dev, const uint16_t* v_cache_dev,
                                    float* out_dev, nvattn_stream_t stream) {
-  if (h == nullptr || layer < 0 || layer >= h->cfg.n_layer || n_seqs < 0 ||
-      n_seqs > h->cfg.max_seqs || n_tokens < 0 || max_blocks <= 0 || max_q_len < 0)
+  return prefill_common(h, layer, n_seqs, n_tokens, q_dev, cu_q_lens_dev, q_starts_dev,
+                        context_lens_dev, block_tables_dev, max_blocks, max_q_len, k_cache_dev,
+                        v_cache_dev, nullptr, nullptr, out_dev, stream);
+}
+
+nvattn_status nvattn_paged_prefill_rows(nvattn_handle* h, int layer, int n_seqs, int n_tokens,
+                                        const uint16_t* q_dev, const int32_t* cu_q_lens_dev,
+                                        const int32_t* q_starts_dev,
+                                        const int32_t* context_lens_dev,
+                                        const int32_t* block_tables_dev, int max_blocks,
+                                        int max_q_len, const uint16_t* k_cache_dev,
+                                        const uint16_t* v_cache_dev,
+                                        const uint16_t* k_rows_f16_dev,
+                                        const uint16_t* v_rows_f16_dev, float* out_dev,
+                                        nvattn_stream_t stream) {
+  if (k_rows_f16_dev == nullptr || v_rows_f16_dev == nullptr || !aligned16(k_rows_f16_dev) ||
+      !aligned16(v_rows_f16_dev))
     return NVATTN_ERR_INVALID_ARG;
-  if (n_seqs == 0 || n_tokens == 0) return NVATTN_OK;
-  if (!q_dev || !cu_q_lens_dev || !q_starts_dev || !context_lens_dev || !block_tables_dev ||
-      !k_cache_dev || !v_cache_dev || !out_dev || !aligned16(q_dev) || !aligned16(out_dev) ||
-      !aligned16(k_cache_dev) || !aligned16(v_cache_dev))
-    return NVATTN_ERR_INVALID_ARG;
-  DeviceGuard guard(h->cfg.device);
-  if (!guard.ok()) return NVATTN_ERR_CUDA;
-  return nvattn::launch_paged_prefill(h, layer, n_seqs, n_tokens, q_dev, cu_q_lens_dev,
-                                      q_starts_dev, context_lens_dev, block_tables_dev,
-                                      max_blocks, max_q_len, k_cache_dev, v_cache_dev, out_dev,
-                                      reinterpret_cast<cudaStream_t>(stream));
+  return prefill_common(h, layer, n_seqs, n_tokens, q_dev, cu_q_lens_dev, q_starts_dev,
+                        context_lens_dev, block_tables_dev, max_blocks, max_q_len, k_cache_dev,
+                        v_cache_dev, k_rows_f16_dev, v_rows_f16_dev, out_dev, stream);
 }
 
 }  // extern "C"

@@ -81,7 +81,8 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
                               const float* k, const float* v, const uint16_t* qw,
                               const uint16_t* kw, const int32_t* positions,
                               const int32_t* slots, void* q_out, nvattn_dtype q_out_dtype,
-                              uint16_t* k_cache, uint16_t* v_cache, cudaStream_t stream);
+                              uint16_t* k_cache, uint16_t* v_cache, uint16_t* k_rows,
+                              uint16_t* v_rows, cudaStream_t stream);
 
 nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const float* q,
                                   const uint16_t* k_cache, const uint16_t* v_cache,
@@ -94,8 +95,8 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
                                    const int32_t* q_starts, const int32_t* context_lens,
                                    const int32_t* block_tables, int max_blocks,
                                    int max_q_len, const uint16_t* k_cache,
-                                   const uint16_t* v_cache, float* out,
-                                   cudaStream_t stream);
+                                   const uint16_t* v_cache, const uint16_t* k_rows,
+                                   const uint16_t* v_rows, float* out, cudaStream_t stream);
 
 // Device-side planners (plan.cu): the host planners' outputs from
 // device-resident sequence lengths and block tables, errors to status_dev.

@@ -83,6 +83,8 @@ struct KvStoreParams {
   void* q_out;
   uint16_t* k_cache;
   uint16_t* v_cache;
+  uint16_t* k_rows;  // nullable: f16 copies of the stored K rows, [n_tokens][Hkv][128]
+  uint16_t* v_rows;  // nullable: f16 copies of the V rows
   DeviceStatus* status;
 };
 
@@ -263,12 +265,20 @@ __device__ __forceinline__ void store_row(const KvStoreParams& p, const float (&
     }
     return;
   }
+  const int head = kind == 1 ? rr - p.Hq : rr - p.Hq - p.Hkv;
+  uint16_t* rows = kind == 1 ? p.k_rows : p.v_rows;
+  if (rows != nullptr) {
+    // The step's own row as the reference's attention sees it: the graph's
+    // f32 value cast to F16 (round to nearest even).
+    uint16_t* o = rows + ((long long)t * p.Hkv + head) * kD + kPer * l8;
+    *reinterpret_cast<uint4*>(o) = pack8_f16(x);
+    *reinterpret_cast<uint4*>(o + kHalf) = pack8_f16(x + kPer);
+  }
   if (slot < 0) return;
   if ((long long)slot >= p.n_slots) {
     record_error(p.status, NVATTN_ERR_OUT_OF_RANGE, 2, slot);
     return;
   }
-  const int head = kind == 1 ? rr - p.Hq : rr - p.Hq - p.Hkv;
   uint16_t* dst = (kind == 1 ? p.k_cache : p.v_cache) +
                   (((long long)p.layer * p.n_slots + slot) * p.Hkv + head) * kD + kPer * l8;
   *reinterpret_cast<uint4*>(dst) = pack8_bf16(x, nan_rule);
@@ -654,7 +664,8 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
                               const float* k, const float* v, const uint16_t* qw,
                               const uint16_t* kw, const int32_t* positions,
                               const int32_t* slots, void* q_out, nvattn_dtype q_out_dtype,
-                              uint16_t* k_cache, uint16_t* v_cache, cudaStream_t stream) {
+                              uint16_t* k_cache, uint16_t* v_cache, uint16_t* k_rows,
+                              uint16_t* v_rows, cudaStream_t stream) {
   if (n_tokens == 0) return NVATTN_OK;
   KvStoreParams p;
   p.n_tokens = n_tokens;
@@ -671,6 +682,8 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
   p.q_out = q_out;
   p.k_cache = k_cache;
   p.v_cache = v_cache;
+  p.k_rows = k_rows;
+  p.v_rows = v_rows;
   p.status = h->status_dev;
   const long long rows = (long long)n_tokens * (p.Hq + 2 * p.Hkv);
   if (rows > 0x7fffffffLL - kMaxRowsPerGroup * kGroupsPerBlock) return NVATTN_ERR_INVALID_ARG;

@@ -50,6 +50,12 @@
 //                place, K(j) then V(j), V rows past the context zeroed (a
 //                cache slot past a sequence's end may hold NaN bits; masked K
 //                columns never reach P).
+// With the step's own K/V rows given in f16 (nvattn_paged_prefill_rows),
+// keys at or past a sequence's cached prefix are the reference's F16 casts of
+// the graph rows instead of the BF16 cache's: a key tile that starts there is
+// loaded from those rows (no conversion), and the one tile that straddles
+// the prefix end takes its later keys from the rows while converting the
+// rest.
 //   warps 2-3    idle.
 //   warps 4-7    softmax of tile 0; warps 8-11 softmax of tile 1: thread =
 //                query row = TMEM lane.  Causal mask, online softmax in the
@@ -67,6 +73,7 @@
 // [256t+128, 256t+256) for O.
 #include <algorithm>
 #include <atomic>
+#include <climits>
 
 #include "common.cuh"
 #include "internal.h"
@@ -97,6 +104,8 @@ struct PrefillParams {
   const int32_t* q_starts;
   const int32_t* context_lens;
   const int32_t* block_tables;
+  const uint16_t* k_rows;  // nullable: the step's rows in f16, [n_tokens][Hkv][128]
+  const uint16_t* v_rows;
   float* out;
   DeviceStatus* status;
   int* sched;  // [0] next work item, [1] CTAs finished; the last CTA zeroes both
@@ -110,7 +119,7 @@ constexpr int kModeRows = 2;   // one head x four row tiles (G == 1)
 // One CTA's view of a work item (written by the leader's producer into both
 // CTAs' rings, read by every role).  valid == 0 ends the CTA's loop.
 struct Work {
-  int valid, seq, kvh, q0, q_start, ctx, n_kv, p_last0;
+  int valid, seq, kvh, q0, q_start, ctx, n_kv, p_last0, n_q;
   int head[2], row0[2], rows[2];
 };
 constexpr int kWorkWords = sizeof(Work) / 4;
@@ -226,6 +235,7 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& prm, int item, 
   const int p_last0 = q_start + w[0].row0[0] + w[0].rows[0] - 1;
   for (int r = 0; r < 2; ++r) {
     w[r].q0 = q0;
+    w[r].n_q = n_q;
     w[r].q_start = q_start;
     w[r].ctx = ctx;
     w[r].n_kv = p_last / kBN + 1;
@@ -243,11 +253,17 @@ __device__ __forceinline__ bool decode_item(const PrefillParams& prm, int item, 
 // ---------------------------------------------------------------- producer
 __device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap* tm_q,
                                               const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                                              const CUtensorMap* tm_kr, const CUtensorMap* tm_vr,
                                               const PrefillParams& prm, uint32_t rank) {
   volatile int* abort_flag = &sm.abort_flag;
   tma_prefetch_desc(tm_q);
   tma_prefetch_desc(tm_k);
   tma_prefetch_desc(tm_v);
+  const bool staged = prm.k_rows != nullptr;
+  if (staged) {
+    tma_prefetch_desc(tm_kr);
+    tma_prefetch_desc(tm_vr);
+  }
   const uint32_t q_full_leader = smem_peer(&sm.q_full, 0);
   int g = 0;  // ring loads issued so far
   for (int k = 0;; ++k) {
@@ -307,17 +323,23 @@ __device__ __forceinline__ void producer_role(PrefillSmem& sm, const CUtensorMap
           bid = 0;
         }
       }
-      const int row = (int)((long long)prm.layer * prm.n_slots + bid * prm.block_size +
-                            key0 % prm.block_size);
+      // A tile at or past the cached prefix comes from the step's f16 rows
+      // (row q0 + key - q_start); every other tile from the cache.
+      const bool from_rows = staged && key0 >= w.q_start;
+      const int row = from_rows ? w.q0 + key0 - w.q_start
+                                : (int)((long long)prm.layer * prm.n_slots +
+                                        bid * prm.block_size + key0 % prm.block_size);
+      const CUtensorMap* map_k = from_rows ? tm_kr : tm_k;
+      const CUtensorMap* map_v = from_rows ? tm_vr : tm_v;
       mbar_arrive_expect_tx(&sm.full[slot], kSlotBytes);
       if ((i & 1) == 0) {
         // K: keys [64r, 64r+64) of the tile, both 64-dim halves
         uint16_t* dst = sm.kv[slot];
-        tma_load_3d(dst, tm_k, &sm.full[slot], 0, w.kvh, row + 64 * (int)rank);
-        tma_load_3d(dst + 64 * 64, tm_k, &sm.full[slot], 64, w.kvh, row + 64 * (int)rank);
+        tma_load_3d(dst, map_k, &sm.full[slot], 0, w.kvh, row + 64 * (int)rank);
+        tma_load_3d(dst + 64 * 64, map_k, &sm.full[slot], 64, w.kvh, row + 64 * (int)rank);
       } else {
         // V: dims [64r, 64r+64) of all 128 keys
-        tma_load_3d(sm.kv[slot], tm_v, &sm.full[slot], 64 * (int)rank, w.kvh, row);
+        tma_load_3d(sm.kv[slot], map_v, &sm.full[slot], 64 * (int)rank, w.kvh, row);
       }
     }
     g += n_loads;
@@ -353,26 +375,59 @@ __device__ __forceinline__ void arrive_leader(uint64_t* bar, bool leader) {
 }
 
 // ---------------------------------------------------------------- K/V converters
-// Converts one CTA's half tile (16 KiB, 1024 16-byte chunks) from bf16 to f16
-// in place; with zero_from >= 0, V keys at or past zero_from are zeroed
-// instead (the V half is [128 keys][64 dims], one key per 128-byte row).
+// One CTA's half of a key tile, 16 KiB = 1024 16-byte chunks, 128-byte rows
+// with 16-byte chunks swizzled by row % 8.  K half: [d half][64 keys][64
+// dims] (keys 64r + row of the tile); V half: [128 keys][64 dims] (dims 64r
+// + ...).  Each chunk of a key past the context is zeroed (V only), of a key
+// at or past the cached prefix taken from the step's f16 rows (a tile that
+// straddles the prefix end), and otherwise converted bf16 -> f16 in place.
 // Consecutive threads touch consecutive chunks (no bank conflicts).
-__device__ __forceinline__ void convert_half(uint16_t* tile, int c, int zero_from) {
-  uint8_t* base = reinterpret_cast<uint8_t*>(tile);
+struct HalfTile {
+  uint16_t* smem;
+  bool is_v;
+  int key_base;       // key of the half tile's first row
+  int zero_from;      // keys at or past this are zeroed (V), INT_MAX for none
+  int rows_from;      // keys in [rows_from, rows_end) come from the rows
+  int rows_end;       //   (the sequence's own rows: never past the buffer)
+  const uint16_t* rows;  // row of key rows_from, at this CTA's dims / head
+  int row_stride;        // elements between consecutive keys' rows
+};
+
+__device__ __forceinline__ void convert_half(const HalfTile& t, int c, uint32_t rank) {
+  uint8_t* base = reinterpret_cast<uint8_t*>(t.smem);
 #pragma unroll 4
   for (int f = c; f < kSlotBytes / 16; f += kConvThreads) {
     uint4* p = reinterpret_cast<uint4*>(base + f * 16);
-    uint4 v = *p;
-    if (zero_from < 0 || (f >> 3) < zero_from) {
+    const int row = t.is_v ? (f >> 3) : ((f >> 3) & 63);
+    const int key = t.key_base + row;
+    uint4 v;
+    if (key >= t.zero_from) {
+      v = make_uint4(0, 0, 0, 0);
+    } else if (key >= t.rows_from && key < t.rows_end) {
+      // logical 8-dim chunk of this physical chunk, and (K) its d half
+      const int chunk = (f & 7) ^ (row & 7);
+      const int dim = t.is_v ? chunk * 8 : (f >> 9) * 64 + chunk * 8;
+      v = *reinterpret_cast<const uint4*>(t.rows + (long long)(key - t.rows_from) * t.row_stride +
+                                          dim);
+    } else {
+      v = *p;
       v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
       v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
       v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
       v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
-    } else {
-      v = make_uint4(0, 0, 0, 0);
     }
     *p = v;
   }
+  fence_proxy_async_smem();
+  __syncwarp();
+}
+
+// Zeroes the V half's keys at or past zero_from (a tile loaded from the
+// step's f16 rows needs no conversion).
+__device__ __forceinline__ void zero_v_tail(uint16_t* smem, int c, int first_zero_row) {
+  uint8_t* base = reinterpret_cast<uint8_t*>(smem);
+  for (int f = c; f < kSlotBytes / 16; f += kConvThreads)
+    if ((f >> 3) >= first_zero_row) *reinterpret_cast<uint4*>(base + f * 16) = make_uint4(0, 0, 0, 0);
   fence_proxy_async_smem();
   __syncwarp();
 }
@@ -387,6 +442,8 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
                                                bool leader) {
   volatile int* abort_flag = &sm.abort_flag;
   const int lane = c & 31;
+  const bool staged = prm.k_rows != nullptr;
+  const uint32_t rank = leader ? 0u : 1u;
   int tb = 0;
   Work w;
   for (int k = 0; next_work(sm, prm, k, lane, w, 49); ++k) {
@@ -396,12 +453,28 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
       const uint32_t ph = (uint32_t)(gj / kConvAhead) & 1u;
       if (gj >= kConvAhead) mbar_wait(&sm.v_consumed[b], ph ^ 1u, prm.status, abort_flag, 43);
       const int kidx = 2 * gj, vidx = 2 * gj + 1;
+      const int key0 = j * kBN;
+      // from the rows entirely (TMA), partly (the prefix end inside), or not
+      const bool tile_rows = staged && key0 >= w.q_start;
+      const int rows_from = staged && w.q_start < key0 + kBN ? w.q_start : INT_MAX;
+      const int rows_end = w.q_start + w.n_q;
+      const long long row0 = (long long)w.q0 * prm.Hkv + w.kvh;  // key q_start's row
       mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 50);
-      convert_half(sm.kv[ring_slot(kidx)], c, -1);
+      if (!tile_rows) {
+        HalfTile t{sm.kv[ring_slot(kidx)], false, key0 + 64 * (int)rank, INT_MAX, rows_from,
+                   rows_end, staged ? prm.k_rows + row0 * kD : nullptr, prm.Hkv * kD};
+        convert_half(t, c, rank);
+      }
       if (lane == 0) arrive_leader(&sm.k_ready[b], leader);
       mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 44);
-      const int key0 = j * kBN;
-      convert_half(sm.kv[ring_slot(vidx)], c, w.ctx - key0 < kBN ? max(w.ctx - key0, 0) : -1);
+      const int zero_from = w.ctx - key0 < kBN ? w.ctx : INT_MAX;
+      if (!tile_rows) {
+        HalfTile t{sm.kv[ring_slot(vidx)], true, key0, zero_from, rows_from, rows_end,
+                   staged ? prm.v_rows + row0 * kD + 64 * (int)rank : nullptr, prm.Hkv * kD};
+        convert_half(t, c, rank);
+      } else if (zero_from != INT_MAX) {
+        zero_v_tail(sm.kv[ring_slot(vidx)], c, max(zero_from - key0, 0));
+      }
       if (lane == 0) arrive_leader(&sm.v_ready[b], leader);
     }
     tb += w.n_kv;
@@ -622,7 +695,9 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     paged_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_k,
-                         const __grid_constant__ CUtensorMap tm_v, PrefillParams prm) {
+                         const __grid_constant__ CUtensorMap tm_v,
+                         const __grid_constant__ CUtensorMap tm_kr,
+                         const __grid_constant__ CUtensorMap tm_vr, PrefillParams prm) {
   extern __shared__ uint8_t smem_raw[];
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -666,7 +741,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   // take 184 each (128*96 + 128*40 + 256*184 = 64512 <= 65536 = 512*128).
   if (warp < 4) {
     regs_dec<96>();
-    if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, prm, rank);
+    if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, &tm_kr, &tm_vr, prm, rank);
     if (warp == 1 && lane == 0 && rank == 0) mma_role(sm, tmem, prm);
   } else if (warp >= 12) {
     regs_dec<40>();
@@ -702,7 +777,8 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
                                    const uint16_t* q, const int32_t* cu_q,
                                    const int32_t* q_starts, const int32_t* context_lens,
                                    const int32_t* block_tables, int max_blocks, int max_q_len,
-                                   const uint16_t* k_cache, const uint16_t* v_cache, float* out,
+                                   const uint16_t* k_cache, const uint16_t* v_cache,
+                                   const uint16_t* k_rows, const uint16_t* v_rows, float* out,
                                    cudaStream_t stream) {
   if (max_q_len <= 0) return NVATTN_OK;
   const int Hq = h->cfg.n_q_heads, Hkv = h->cfg.n_kv_heads;
@@ -718,6 +794,18 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   if (st != NVATTN_OK) return st;
   st = get_cache_tensor_map(h, v_cache, 64, kBN, CU_TENSOR_MAP_SWIZZLE_128B, &tv);
   if (st != NVATTN_OK) return st;
+  // The step's f16 rows [n_tokens][Hkv][128], boxed like the cache.
+  CUtensorMap tkr = tk, tvr = tv;
+  if (k_rows != nullptr) {
+    st = encode_tensor_map_3d(&tkr, k_rows, kD, (uint64_t)Hkv, (uint64_t)n_tokens, kD * 2,
+                              (uint64_t)Hkv * kD * 2, 64, 1, kBN / 2, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    if (st != NVATTN_OK) return st;
+    st = encode_tensor_map_3d(&tvr, v_rows, kD, (uint64_t)Hkv, (uint64_t)n_tokens, kD * 2,
+                              (uint64_t)Hkv * kD * 2, 64, 1, kBN, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+    if (st != NVATTN_OK) return st;
+  }
 
   PrefillParams prm;
   prm.Hq = Hq;
@@ -735,6 +823,8 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
   prm.q_starts = q_starts;
   prm.context_lens = context_lens;
   prm.block_tables = block_tables;
+  prm.k_rows = k_rows;
+  prm.v_rows = v_rows;
   prm.out = out;
   prm.status = h->status_dev;
   prm.sched = h->prefill_sched_dev;
@@ -764,7 +854,7 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
       return NVATTN_ERR_CUDA;
     if (dev < 64) attr_set_mask.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
-  paged_prefill_kernel<<<2 * pairs, kThreads, smem, stream>>>(tm_q, tk, tv, prm);
+  paged_prefill_kernel<<<2 * pairs, kThreads, smem, stream>>>(tm_q, tk, tv, tkr, tvr, prm);
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 

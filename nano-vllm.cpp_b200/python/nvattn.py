@@ -31,7 +31,8 @@ EXPORTED = [
     "nvattn_version", "nvattn_get_error", "nvattn_plan_prefill", "nvattn_plan_decode",
     "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
     "nvattn_paged_decode_noalloc", "nvattn_plan_prefill_device", "nvattn_plan_decode_device",
-    "nvattn_sample", "nvattn_schedule_prefill_chunks",
+    "nvattn_sample", "nvattn_schedule_prefill_chunks", "nvattn_kv_store_qk_norm_rope_rows",
+    "nvattn_paged_prefill_rows",
 ]
 ERR_SCRATCH_LIMIT = 7
 
@@ -100,6 +101,11 @@ def lib():
                                                      ctypes.POINTER(_i32)]
         L.nvattn_kv_store_qk_norm_rope.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                                                    _vp, _vp, _i32, _vp, _vp, _vp]
+        L.nvattn_kv_store_qk_norm_rope_rows.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
+                                                        _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp,
+                                                        _vp]
+        L.nvattn_paged_prefill_rows.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
+                                                _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]
         L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
                                           _vp, _vp]
         L.nvattn_paged_prefill.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32,
@@ -222,13 +228,19 @@ class Handle:
         return st
 
     def kv_store(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, q_out, k_cache,
-                 v_cache, stream=None, check=True):
+                 v_cache, stream=None, check=True, k_rows=None, v_rows=None):
+        """nvattn_kv_store_qk_norm_rope; with k_rows / v_rows (f16 [T][Hkv][128])
+        nvattn_kv_store_qk_norm_rope_rows, which also writes the step's rows."""
         import torch
         dt = {torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}.get(q_out.dtype, DTYPE_F32)
-        st = lib().nvattn_kv_store_qk_norm_rope(
-            self._h, layer, positions.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm_w),
-            _ptr(k_norm_w), _ptr(positions), _ptr(slots), _ptr(q_out), dt, _ptr(k_cache),
-            _ptr(v_cache), _stream_ptr(stream))
+        args = (self._h, layer, positions.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm_w),
+                _ptr(k_norm_w), _ptr(positions), _ptr(slots), _ptr(q_out), dt, _ptr(k_cache),
+                _ptr(v_cache))
+        if k_rows is None:
+            st = lib().nvattn_kv_store_qk_norm_rope(*args, _stream_ptr(stream))
+        else:
+            st = lib().nvattn_kv_store_qk_norm_rope_rows(*args, _ptr(k_rows), _ptr(v_rows),
+                                                         _stream_ptr(stream))
         if check:
             _check(st, "nvattn_kv_store_qk_norm_rope")
         return st
@@ -244,11 +256,17 @@ class Handle:
         return st
 
     def prefill(self, layer, q, cu_q, q_starts, context_lens, block_tables, max_q_len, k_cache,
-                v_cache, out, stream=None, check=True):
-        st = lib().nvattn_paged_prefill(
-            self._h, layer, context_lens.shape[0], q.shape[0], _ptr(q), _ptr(cu_q),
-            _ptr(q_starts), _ptr(context_lens), _ptr(block_tables), block_tables.shape[1],
-            int(max_q_len), _ptr(k_cache), _ptr(v_cache), _ptr(out), _stream_ptr(stream))
+                v_cache, out, stream=None, check=True, k_rows=None, v_rows=None):
+        """nvattn_paged_prefill; with k_rows / v_rows (the step's f16 rows)
+        nvattn_paged_prefill_rows."""
+        args = (self._h, layer, context_lens.shape[0], q.shape[0], _ptr(q), _ptr(cu_q),
+                _ptr(q_starts), _ptr(context_lens), _ptr(block_tables), block_tables.shape[1],
+                int(max_q_len), _ptr(k_cache), _ptr(v_cache))
+        if k_rows is None:
+            st = lib().nvattn_paged_prefill(*args, _ptr(out), _stream_ptr(stream))
+        else:
+            st = lib().nvattn_paged_prefill_rows(*args, _ptr(k_rows), _ptr(v_rows), _ptr(out),
+                                                 _stream_ptr(stream))
         if check:
             _check(st, "nvattn_paged_prefill")
         return st

@@ -215,3 +215,74 @@ def test_prefill_step_against_the_reference_concat_algorithm(cuda):
     assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
     mx, mr = O.err_stats(got, ref)
     assert mx <= MAX_ABS and mr <= chain + storage + MEAN_REL, (mx, mr, chain, storage)
+
+
+def _store_then_prefill(Hq, Hkv, lens, starts, seed, rows, num_blocks=None):
+    """Fused store (f16 q, and with `rows` the step's f16 rows) then prefill
+    on the GPU; returns the output and the oracle's view of the step."""
+    import torch
+    lens = np.asarray(lens, np.int64)
+    starts = np.asarray(starts, np.int64)
+    c = cases.decode_case(seed, Hq, Hkv, lens, num_blocks=num_blocks)
+    cu, qs, cl, pos, slot = nvattn.plan_prefill(lens, starts, c.block_tables)
+    T = int(cu[-1])
+    rng = np.random.default_rng(seed + 1)
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    qw, kw = _norm_weights(rng)
+    h = handle(Hq, Hkv, c.cache.num_blocks, max_seqs=len(lens))
+    kc, vc = dev(c.cache.k), dev(c.cache.v)
+    qh = torch.empty((T, Hq, 128), dtype=torch.float16, device="cuda")
+    kr = torch.empty((T, Hkv, 128), dtype=torch.float16, device="cuda") if rows else None
+    vr = torch.empty_like(kr) if rows else None
+    h.kv_store(0, dev(q), dev(k), dev(v), dev(qw), dev(kw), dev(pos), dev(slot), qh, kc, vc,
+               k_rows=kr, v_rows=vr)
+    out = torch.full((T, Hq, 128), float("nan"), device="cuda")
+    h.prefill(0, qh, dev(cu), dev(qs), dev(cl), dev(c.block_tables), int((cl - qs).max()), kc,
+              vc, out, k_rows=kr, v_rows=vr)
+    h.check_device()
+    got = out.cpu().numpy()
+    h.close()
+    p = cases.oracle_params(Hq, Hkv, c.cache)
+    okc, ovc = c.cache.k.copy(), c.cache.v.copy()
+    q_out, k_out = O.qk_norm_rope_store(p, 0, q, k, v, qw, kw, pos, slot, okc, ovc,
+                                        want_k_out=True)
+    return got, p, (cu, qs, cl, c.block_tables, okc, ovc, q_out, k_out, v)
+
+
+def test_prefill_step_with_the_steps_own_rows_meets_the_plain_bar(cuda):
+    """With the step's own rows in f16 (nvattn_kv_store_qk_norm_rope_rows +
+    nvattn_paged_prefill_rows) the prefill attends what the reference's step
+    attends -- the graph rows cast to F16 -- so the plain bars hold against
+    the reference's FillCausalMask attention over the batch's rows: mean-rel
+    <= chain + 1e-3 (chain = its own distance from exact math) and <= 1e-3
+    against exact math on the f32 rows."""
+    got, p, (cu, qs, cl, bt, okc, ovc, q_out, k_out, v) = _store_then_prefill(
+        16, 8, [300, 77, 513], [0, 0, 0], 920, rows=True, num_blocks=8)
+    ref = O.concat_prefill_ggml(p, q_out, cu, k_out, v)
+    exact = O.paged_prefill(p, O.MODE_TRUTH, 0, q_out, cu, qs, cl, bt, okc, ovc,
+                            new_k=k_out, new_v=v)
+    _, chain = O.err_stats(ref, exact)
+    assert np.isfinite(got).all()
+    mx, mr = O.err_stats(got, exact)
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)
+    mx, mr = O.err_stats(got, ref)
+    assert mx <= MAX_ABS and mr <= chain + MEAN_REL, (mx, mr, chain)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(16, 8), (64, 8), (8, 8)])
+def test_prefill_rows_with_a_cached_prefix_and_unaligned_starts(cuda, Hq, Hkv):
+    """Prefix keys from the BF16 cache, the step's keys from its f16 rows:
+    whole-block and unaligned prefix ends (a key tile that straddles the
+    prefix end takes its later keys from the rows), a fully cached prompt
+    (one row), against exact math on exactly those keys and values."""
+    lens, starts = [600, 300, 1030, 1, 700], [512, 44, 1024, 0, 699]
+    got, p, (cu, qs, cl, bt, okc, ovc, q_out, k_out, v) = _store_then_prefill(
+        Hq, Hkv, lens, starts, 930 + Hq, rows=True)
+    f16 = lambda a: a.astype(np.float16).astype(np.float32)
+    exact = O.paged_prefill(p, O.MODE_TRUTH, 0, q_out, cu, qs, cl, bt, okc, ovc,
+                            new_k=f16(k_out), new_v=f16(v))
+    assert np.isfinite(got).all()
+    mx, mr = O.err_stats(got, exact)
+    assert mx <= MAX_ABS and mr <= MEAN_REL, (mx, mr)

@@ -227,3 +227,40 @@ def test_non_finite_rows(cuda, T):
     assert np.array_equal(np.isnan(gq), np.isnan(oq)) and np.isnan(gq[13, 6]).any()
     fin = ~np.isnan(gq)
     assert np.array_equal(gq[fin].view(np.uint32), oq[fin].view(np.uint32))
+
+
+@pytest.mark.parametrize("T", [300, 3000])  # register-row kernel, staged kernel
+def test_step_rows_in_f16(cuda, T):
+    """nvattn_kv_store_qk_norm_rope_rows also writes the step's own K (normed,
+    rotated) and V rows as f16: the reference's F16 cast of its graph rows,
+    bit for bit; everything else equals the plain store's."""
+    import torch
+    rng = np.random.default_rng(900 + T)
+    Hq, Hkv = 16, 8
+    q = rng.standard_normal((T, Hq, 128), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, 128), dtype=np.float32)
+    qw = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(128)).astype(np.float32))
+    kw = O.f32_to_bf16((1 + 0.02 * rng.standard_normal(128)).astype(np.float32))
+    nb = (T + 255) // 256 + 1
+    pos = rng.integers(0, 40960, T).astype(np.int32)
+    slots = rng.permutation(nb * 256)[:T].astype(np.int32)
+    slots[:3] = -1  # rows are written whatever the slot
+    h = handle(Hq, Hkv, nb)
+    kc = torch.zeros((1, nb * 256, Hkv, 128), dtype=torch.int16, device="cuda")
+    vc = torch.zeros_like(kc)
+    qo = torch.empty((T, Hq, 128), dtype=torch.float16, device="cuda")
+    kr = torch.empty((T, Hkv, 128), dtype=torch.float16, device="cuda")
+    vr = torch.empty_like(kr)
+    h.kv_store(0, dev(q), dev(k), dev(v), dev(qw), dev(kw), dev(pos), dev(slots), qo, kc, vc,
+               k_rows=kr, v_rows=vr)
+    h.check_device()
+    p = O.params(n_q_heads=Hq, n_kv_heads=Hkv, n_slots=nb * 256)
+    okc = np.zeros((1, nb * 256, Hkv, 128), np.uint16)
+    ovc = np.zeros_like(okc)
+    oq, ok = O.qk_norm_rope_store(p, 0, q, k, v, qw, kw, pos, slots, okc, ovc, want_k_out=True)
+    f16 = lambda a: a.astype(np.float16).view(np.uint16)
+    assert np.array_equal(kr.cpu().numpy().view(np.uint16), f16(ok))
+    assert np.array_equal(vr.cpu().numpy().view(np.uint16), f16(v))
+    assert np.array_equal(qo.cpu().numpy().view(np.uint16), f16(oq))
+    assert np.array_equal(host_bits(kc), okc) and np.array_equal(host_bits(vc), ovc)
