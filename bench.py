@@ -42,15 +42,16 @@ SEED = 0
 
 # DRAM traffic per decode launch of this workload (dram__bytes_read.sum +
 # dram__bytes_write.sum): an ncu capture of the first 32 sequences of this
-# workload moved 1.3767 GB for 1.3632 GB of
-# algorithmic bytes (x1.0099); scaled to the full launch's 10.987 GB.
-NCU_TRAFFIC_BYTES_N1 = 11.096e9
+# workload moved 1.3774 GB (1.3722 read, 0.0052 written) for 1.3632 GB of
+# algorithmic bytes (x1.0104); scaled to the full launch's 10.987 GB.
+NCU_TRAFFIC_BYTES_N1 = 11.101e9
 
 # sm__pipe_tensor_cycles_active of paged_prefill_kernel, fraction of elapsed
-# cycles, from full ncu captures: the chunk shape (2 x 2048 new tokens at
-# [30720, 32768), 32B heads) and the prefix-hit workload itself.
-NCU_PREFILL_TENSOR_ACTIVE = 0.543
-NCU_PREFIX_HIT_TENSOR_ACTIVE = 0.366
+# cycles, from full ncu captures of the CTA-pair kernel with f16 Q/K/V: the
+# chunk shape (2 x 2048 new tokens at [30720, 32768), 32B heads) and the
+# prefix-hit workload itself (None until captured).
+NCU_PREFILL_TENSOR_ACTIVE = 0.388
+NCU_PREFIX_HIT_TENSOR_ACTIVE = None
 
 
 def log(*a):
@@ -224,7 +225,7 @@ def bench_prefill(kind, args, world, rank, device):
     h.close()
     fields = {"workload": name, "q_heads": Hq, "kv_heads": Hkv, "n_seqs": len(lens),
               "new_tokens": T, "sum_context": int(cl.sum()), "flops_per_step": flops,
-              "steps": steps, "pv_precision": "f16 P x f16 V (V converted in smem)",
+              "steps": steps, "precision": "f16 Q x f16 K, f16 P x f16 V (K, V converted in smem), f32 accumulation",
               "kv_store": kv_store_roofline(T, hq, hkv, store_ms, q_out_bytes=2),
               "clocks": clk}
     if cpu is not None:
