@@ -319,6 +319,18 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
                : "memory");
 }
 
+// Arrives on an mbarrier of any CTA of the cluster with the default
+// semantics (release at CTA scope).  For signals whose payload reaches the
+// waiter through the tensor cores, not through generic loads: shared memory
+// made visible to the async proxy (fence.proxy.async) or TMEM completed by
+// tcgen05.wait and ordered by tcgen05.fence, which the waiting thread only
+// hands to tcgen05.mma.  This is the form the 2-SM MMA pipelines use for
+// their peer-to-leader arrivals; the cluster-scope release above costs a
+// cluster-wide memory fence per arrive.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }

@@ -64,8 +64,10 @@
 //                a row max grows by more than 2^8), epilogue O / l.
 // Barriers the leader's MMA lane waits on (K/V converted, P written, work
 // slot free) live in the leader and count both CTAs' arrivals (the leader's
-// warps arrive locally, the follower's with a cluster-scope release); MMA
-// completions arrive on the barrier at the same offset in both CTAs.
+// warps arrive locally, the follower's remotely: CTA-scope release for the
+// per-tile barriers, whose payload only the MMAs read, cluster scope for the
+// work ring, which carries data); MMA completions arrive on the barrier at
+// the same offset in both CTAs.
 // MMAs issued by one thread execute in order, so S(j+1) may overwrite the
 // columns of P(j) right after PV(j) is issued, and the completion of S(j+1)
 // implies PV(j) is done (its O may then be rescaled).
@@ -364,14 +366,19 @@ __device__ __forceinline__ bool next_work(PrefillSmem& sm, const PrefillParams& 
   return w.valid != 0;
 }
 
-// Arrives on the pair leader's copy of barrier `bar`: a local arrive in the
-// leader (release at CTA scope), a remote one with cluster-scope release in
-// the follower.
+// Arrives on the pair leader's copy of a per-tile barrier `bar`: a local
+// arrive in the leader, a remote one in the follower, both with the default
+// (CTA-scope) release.  What these barriers publish -- converted K/V halves
+// behind fence.proxy.async, P in TMEM behind tcgen05.wait::st and
+// tcgen05.fence -- is read only by the pair MMAs that the leader's MMA lane
+// issues after its wait; a cluster-scope release would add a cluster-wide
+// memory fence (about a thousand cycles) to every follower arrival on the
+// S -> softmax -> P.V chain.
 __device__ __forceinline__ void arrive_leader(uint64_t* bar, bool leader) {
   if (leader)
     mbar_arrive(bar);
   else
-    mbar_arrive_cluster(smem_peer(bar, 0));
+    mbar_arrive_remote(smem_peer(bar, 0));
 }
 
 // ---------------------------------------------------------------- K/V converters
@@ -516,8 +523,8 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
     mbar_arrive_cluster(smem_peer(&sm.work_empty[ws], 0));
     if (!valid) break;
     mbar_wait(&sm.q_full, k & 1, prm.status, abort_flag, 31);
-    mbar_wait_cluster(&sm.k_ready[tb % kConvAhead], (uint32_t)(tb / kConvAhead) & 1u, prm.status,
-                      abort_flag, 32);
+    mbar_wait(&sm.k_ready[tb % kConvAhead], (uint32_t)(tb / kConvAhead) & 1u, prm.status,
+              abort_flag, 32);
     tc_fence_after();
     // S_t(0) overwrites the S/P columns of the previous item: its P.V MMAs
     // were issued before and execute first.  Its O columns are rewritten by
@@ -532,19 +539,19 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
     for (int j = 0; j < n_kv; ++j) {
       const int gj = tb + j;
       const int vidx = 2 * gj + 1, kidx = 2 * gj + 2;
-      mbar_wait_cluster(&sm.v_ready[gj % kConvAhead], (uint32_t)(gj / kConvAhead) & 1u,
-                        prm.status, abort_flag, 33);
-      mbar_wait_cluster(&sm.p_full[0], gj & 1, prm.status, abort_flag, 34);
+      mbar_wait(&sm.v_ready[gj % kConvAhead], (uint32_t)(gj / kConvAhead) & 1u, prm.status,
+                abort_flag, 33);
+      mbar_wait(&sm.p_full[0], gj & 1, prm.status, abort_flag, 34);
       tc_fence_after();
       issue_pv(0, gj, j > 0);
       if (j + 1 < n_kv) {
-        mbar_wait_cluster(&sm.k_ready[(gj + 1) % kConvAhead],
-                          (uint32_t)((gj + 1) / kConvAhead) & 1u, prm.status, abort_flag, 35);
+        mbar_wait(&sm.k_ready[(gj + 1) % kConvAhead], (uint32_t)((gj + 1) / kConvAhead) & 1u,
+                  prm.status, abort_flag, 35);
         tc_fence_after();
         issue_s(0, gj + 1);
         umma_commit_pair(&sm.s_full[0]);
       }
-      mbar_wait_cluster(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
+      mbar_wait(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
       tc_fence_after();
       issue_pv(1, gj, j > 0);
       umma_commit_pair(&sm.v_consumed[gj % kConvAhead]);
