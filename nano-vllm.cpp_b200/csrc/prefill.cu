@@ -400,7 +400,46 @@ struct HalfTile {
   int row_stride;        // elements between consecutive keys' rows
 };
 
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
+  v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
+  v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
+  v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
+  v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
+  return v;
+}
+
 __device__ __forceinline__ void convert_half(const HalfTile& t, int c, uint32_t rank) {
+  const int n_keys = t.is_v ? kBN : kBN / 2;
+  if (t.key_base + n_keys <= t.zero_from &&
+      (t.rows_from >= t.key_base + n_keys || t.rows_end <= t.key_base)) {
+    // Every chunk converts in place: shared-memory loads of four chunks are
+    // issued before any is converted and stored.
+    const uint32_t base = smem_u32(t.smem) + (uint32_t)c * 16;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint4 v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = lds128(base + (uint32_t)(4 * h + i) * kConvThreads * 16);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        sts128(base + (uint32_t)(4 * h + i) * kConvThreads * 16, bf16x8_to_f16x8(v[i]));
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    return;
+  }
   uint8_t* base = reinterpret_cast<uint8_t*>(t.smem);
 #pragma unroll 4
   for (int f = c; f < kSlotBytes / 16; f += kConvThreads) {
@@ -417,11 +456,7 @@ __device__ __forceinline__ void convert_half(const HalfTile& t, int c, uint32_t 
       v = *reinterpret_cast<const uint4*>(t.rows + (long long)(key - t.rows_from) * t.row_stride +
                                           dim);
     } else {
-      v = *p;
-      v.x = cvt_f16x2(bf16lo_to_f32(v.x), bf16hi_to_f32(v.x));
-      v.y = cvt_f16x2(bf16lo_to_f32(v.y), bf16hi_to_f32(v.y));
-      v.z = cvt_f16x2(bf16lo_to_f32(v.z), bf16hi_to_f32(v.z));
-      v.w = cvt_f16x2(bf16lo_to_f32(v.w), bf16hi_to_f32(v.w));
+      v = bf16x8_to_f16x8(*p);
     }
     *p = v;
   }
@@ -744,14 +779,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sm.tmem_base;
 
   // 512 threads x 128 registers at launch: warpgroup 0 (TMA, MMA) gives back
-  // down to 96, warpgroup 3 (converters) to 40, the two softmax warpgroups
-  // take 184 each (128*96 + 128*40 + 256*184 = 64512 <= 65536 = 512*128).
+  // down to 96, warpgroup 3 (converters) to 48 (at 40 their loop spilled),
+  // the two softmax warpgroups take 184 each
+  // (128*96 + 128*48 + 256*184 = 65536 = 512*128).
   if (warp < 4) {
     regs_dec<96>();
     if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, &tm_kr, &tm_vr, prm, rank);
     if (warp == 1 && lane == 0 && rank == 0) mma_role(sm, tmem, prm);
   } else if (warp >= 12) {
-    regs_dec<40>();
+    regs_dec<48>();
     converter_role(sm, prm, threadIdx.x - 384, rank == 0);
   } else {
     regs_inc<184>();
