@@ -530,25 +530,37 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
   volatile int* abort_flag = &sm.abort_flag;
   constexpr uint32_t idesc_s = umma_idesc_f16_f32(2 * kBM, kBN, 0, 0);
   constexpr uint32_t idesc_o = umma_idesc_f16_f32(2 * kBM, kD, 0, 1);
+  // Shared-memory descriptors are built once; an MMA adds its operand's
+  // offset to the start-address field (16-byte units; no field overflows: a
+  // shared address is below 2^18 bytes).  A single thread issues at most one
+  // tcgen05.mma per ~53 cycles against 64 cycles of tensor work per MMA, so
+  // per-MMA descriptor arithmetic would leave the tensor pipe idle.
+  const uint64_t q_desc[2][2] = {
+      {umma_desc_sw128(smem_u32(sm.q[0][0]), 16, 1024),
+       umma_desc_sw128(smem_u32(sm.q[0][1]), 16, 1024)},
+      {umma_desc_sw128(smem_u32(sm.q[1][0]), 16, 1024),
+       umma_desc_sw128(smem_u32(sm.q[1][1]), 16, 1024)}};
+  const uint64_t k_desc0 = umma_desc_sw128(smem_u32(sm.kv[0]), 16, 1024);
+  const uint64_t v_desc0 = umma_desc_sw128(smem_u32(sm.kv[0]), kSlotBytes, 1024);
+  constexpr uint64_t kSlotUnits = kSlotBytes / 16;
   auto issue_s = [&](int t, int gj) {
-    const uint32_t kbase = smem_u32(sm.kv[ring_slot(2 * gj)]);
+    const uint64_t kd = k_desc0 + (uint64_t)ring_slot(2 * gj) * kSlotUnits;
+    const uint64_t qd0 = q_desc[t][0], qd1 = q_desc[t][1];
 #pragma unroll
     for (int k = 0; k < kD / 16; ++k) {
-      const uint32_t koff = (uint32_t)(k & 3) * 32;
-      const uint64_t a = umma_desc_sw128(smem_u32(sm.q[t][k >> 2]) + koff, 16, 1024);
-      const uint64_t b =
-          umma_desc_sw128(kbase + (uint32_t)(k >> 2) * (64 * 128) + koff, 16, 1024);
+      // +32 bytes per 16 dims inside a 64-dim half; K's second half starts
+      // 64 x 128 bytes further
+      const uint64_t a = (k < 4 ? qd0 : qd1) + (uint64_t)((k & 3) * 2);
+      const uint64_t b = kd + (uint64_t)((k >> 2) * (64 * 128 / 16) + (k & 3) * 2);
       umma_pair_ss(tmem + t * 256, a, b, idesc_s, k > 0 ? 1u : 0u);
     }
   };
   auto issue_pv = [&](int t, int gj, bool accumulate) {
-    const uint32_t vbase = smem_u32(sm.kv[ring_slot(2 * gj + 1)]);
+    const uint64_t vd = v_desc0 + (uint64_t)ring_slot(2 * gj + 1) * kSlotUnits;
 #pragma unroll
-    for (int k = 0; k < kBN / 16; ++k) {
-      const uint64_t b = umma_desc_sw128(vbase + (uint32_t)k * 16 * 128, kSlotBytes, 1024);
-      umma_pair_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, b, idesc_o,
-                   (accumulate || k > 0) ? 1u : 0u);
-    }
+    for (int k = 0; k < kBN / 16; ++k)
+      umma_pair_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, vd + (uint64_t)(k * 16 * 128 / 16),
+                   idesc_o, (accumulate || k > 0) ? 1u : 0u);
   };
   int tb = 0, k = 0;
   for (;; ++k) {
