@@ -133,8 +133,8 @@ struct __align__(1024) PrefillSmem {
   uint64_t full[kSlots], empty[kSlots];
   uint64_t s_full[2], p_full[2];
   // per key tile gj, indexed gj % kConvAhead: converted K / V ready for the
-  // MMAs (leader), and P.V of the tile done (its V slot no longer read)
-  uint64_t k_ready[4], v_ready[4], v_consumed[4];
+  // MMAs (leader; v_ready(gj) also covers K(gj+1))
+  uint64_t k_ready[4], v_ready[4];
   uint64_t o_final;
   uint64_t q_empty;                      // the item's last S MMAs have read Q
   uint64_t work_full[2], work_empty[2];  // the work ring (work_empty: leader)
@@ -474,12 +474,17 @@ __device__ __forceinline__ void zero_v_tail(uint16_t* smem, int c, int first_zer
   __syncwarp();
 }
 
-// The converters run ahead of the MMAs as far as the TMA ring lets them
-// (K(gj) and V(gj) as soon as they land), so the conversion stays off the
-// S -> softmax -> P.V chain.  Their barriers come in sets of kConvAhead, one
-// per key tile mod kConvAhead; tile gj waits for P.V of tile gj-kConvAhead
-// (which has waited k_ready / v_ready of that tile), so no barrier runs more
-// than one phase ahead of its waiter.
+// The converters run ahead of the MMAs as far as the TMA ring and their lead
+// limit let them, so the conversion stays off the S -> softmax -> P.V chain,
+// and keep K one key tile ahead of V: an item's first K, then per key tile
+// the next tile's K and this tile's V.  v_ready(gj) therefore also publishes
+// K(gj+1), and the MMA lane waits once per key tile (on k_ready only for an
+// item's first tile; the converters arrive on it for every tile, so its
+// phases stay in step).  Their barriers come in sets of kConvAhead, one per
+// key tile mod kConvAhead; converting K(g) first waits for P.V of tile
+// g - kConvAhead (the completion of that tile's V ring slot), which has
+// waited for its v_ready and k_ready phases, so no barrier runs more than one
+// phase ahead of its waiter.
 __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillParams& prm, int c,
                                                bool leader) {
   volatile int* abort_flag = &sm.abort_flag;
@@ -488,36 +493,47 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
   const uint32_t rank = leader ? 0u : 1u;
   int tb = 0;
   Work w;
-  for (int k = 0; next_work(sm, prm, k, lane, w, 49); ++k) {
-    for (int j = 0; j < w.n_kv; ++j) {
-      const int gj = tb + j;
-      const int b = gj % kConvAhead;
-      const uint32_t ph = (uint32_t)(gj / kConvAhead) & 1u;
-      if (gj >= kConvAhead) mbar_wait(&sm.v_consumed[b], ph ^ 1u, prm.status, abort_flag, 43);
-      const int kidx = 2 * gj, vidx = 2 * gj + 1;
-      const int key0 = j * kBN;
-      // from the rows entirely (TMA), partly (the prefix end inside), or not
-      const bool tile_rows = staged && key0 >= w.q_start;
-      const int rows_from = staged && w.q_start < key0 + kBN ? w.q_start : INT_MAX;
-      const int rows_end = w.q_start + w.n_q;
+  // key tile j of the current item (global tile g = tb + j)
+  auto convert_k = [&](int j) {
+    const int g = tb + j;
+    if (g >= kConvAhead) {
+      const int lead_idx = 2 * (g - kConvAhead) + 1;  // V of tile g - kConvAhead
+      mbar_wait(&sm.empty[ring_slot(lead_idx)], ring_parity(lead_idx), prm.status, abort_flag,
+                43);
+    }
+    const int key0 = j * kBN, kidx = 2 * g;
+    mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 50);
+    // from the rows entirely (TMA), partly (the prefix end inside), or not
+    if (!(staged && key0 >= w.q_start)) {
       const long long row0 = (long long)w.q0 * prm.Hkv + w.kvh;  // key q_start's row
-      mbar_wait(&sm.full[ring_slot(kidx)], ring_parity(kidx), prm.status, abort_flag, 50);
-      if (!tile_rows) {
-        HalfTile t{sm.kv[ring_slot(kidx)], false, key0 + 64 * (int)rank, INT_MAX, rows_from,
-                   rows_end, staged ? prm.k_rows + row0 * kD : nullptr, prm.Hkv * kD};
-        convert_half(t, c, rank);
-      }
-      if (lane == 0) arrive_leader(&sm.k_ready[b], leader);
-      mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 44);
-      const int zero_from = w.ctx - key0 < kBN ? w.ctx : INT_MAX;
-      if (!tile_rows) {
-        HalfTile t{sm.kv[ring_slot(vidx)], true, key0, zero_from, rows_from, rows_end,
-                   staged ? prm.v_rows + row0 * kD + 64 * (int)rank : nullptr, prm.Hkv * kD};
-        convert_half(t, c, rank);
-      } else if (zero_from != INT_MAX) {
-        zero_v_tail(sm.kv[ring_slot(vidx)], c, max(zero_from - key0, 0));
-      }
-      if (lane == 0) arrive_leader(&sm.v_ready[b], leader);
+      HalfTile t{sm.kv[ring_slot(kidx)], false, key0 + 64 * (int)rank, INT_MAX,
+                 staged && w.q_start < key0 + kBN ? w.q_start : INT_MAX, w.q_start + w.n_q,
+                 staged ? prm.k_rows + row0 * kD : nullptr, prm.Hkv * kD};
+      convert_half(t, c, rank);
+    }
+    if (lane == 0) arrive_leader(&sm.k_ready[g % kConvAhead], leader);
+  };
+  auto convert_v = [&](int j) {
+    const int g = tb + j;
+    const int key0 = j * kBN, vidx = 2 * g + 1;
+    mbar_wait(&sm.full[ring_slot(vidx)], ring_parity(vidx), prm.status, abort_flag, 44);
+    const int zero_from = w.ctx - key0 < kBN ? w.ctx : INT_MAX;
+    if (!(staged && key0 >= w.q_start)) {
+      const long long row0 = (long long)w.q0 * prm.Hkv + w.kvh;
+      HalfTile t{sm.kv[ring_slot(vidx)], true, key0, zero_from,
+                 staged && w.q_start < key0 + kBN ? w.q_start : INT_MAX, w.q_start + w.n_q,
+                 staged ? prm.v_rows + row0 * kD + 64 * (int)rank : nullptr, prm.Hkv * kD};
+      convert_half(t, c, rank);
+    } else if (zero_from != INT_MAX) {
+      zero_v_tail(sm.kv[ring_slot(vidx)], c, max(zero_from - key0, 0));
+    }
+    if (lane == 0) arrive_leader(&sm.v_ready[g % kConvAhead], leader);
+  };
+  for (int k = 0; next_work(sm, prm, k, lane, w, 49); ++k) {
+    convert_k(0);
+    for (int j = 0; j < w.n_kv; ++j) {
+      if (j + 1 < w.n_kv) convert_k(j + 1);
+      convert_v(j);
     }
     tb += w.n_kv;
   }
@@ -586,22 +602,19 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
     for (int j = 0; j < n_kv; ++j) {
       const int gj = tb + j;
       const int vidx = 2 * gj + 1, kidx = 2 * gj + 2;
+      // V(gj) converted, and K(gj+1) with it
       mbar_wait(&sm.v_ready[gj % kConvAhead], (uint32_t)(gj / kConvAhead) & 1u, prm.status,
                 abort_flag, 33);
       mbar_wait(&sm.p_full[0], gj & 1, prm.status, abort_flag, 34);
       tc_fence_after();
       issue_pv(0, gj, j > 0);
       if (j + 1 < n_kv) {
-        mbar_wait(&sm.k_ready[(gj + 1) % kConvAhead], (uint32_t)((gj + 1) / kConvAhead) & 1u,
-                  prm.status, abort_flag, 35);
-        tc_fence_after();
         issue_s(0, gj + 1);
         umma_commit_pair(&sm.s_full[0]);
       }
       mbar_wait(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
       tc_fence_after();
       issue_pv(1, gj, j > 0);
-      umma_commit_pair(&sm.v_consumed[gj % kConvAhead]);
       umma_commit_pair(&sm.empty[ring_slot(vidx)]);
       if (j + 1 < n_kv) {
         issue_s(1, gj + 1);
@@ -768,7 +781,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kConvAhead; ++i) {
       mbar_init(&sm.k_ready[i], kPairWarps4);
       mbar_init(&sm.v_ready[i], kPairWarps4);
-      mbar_init(&sm.v_consumed[i], 1);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
