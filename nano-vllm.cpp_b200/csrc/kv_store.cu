@@ -704,10 +704,25 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
       default: return launch_staged<kQOutF32>(p, plan, h->sm_count, stream);
     }
   }
-  // Enough groups for about four resident blocks per SM; beyond that each
-  // group takes more rows so the per-token loads are shared.
-  const long long per_wave = (long long)h->sm_count * 4 * kGroupsPerBlock;
-  p.rows_per_group = (int)std::max(1LL, std::min<long long>(kMaxRowsPerGroup, rows / per_wave));
+  // One wave: as many groups as the resident blocks hold (the kernel's
+  // registers allow two 256-thread blocks per SM; the occupancy is queried
+  // once per device), each group taking as many consecutive rows as that
+  // needs -- a second, partial wave would double the latency of a decode
+  // step's store.
+  static std::atomic<int> rows_blocks_per_sm[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
+  int per_sm = dev < 64 ? rows_blocks_per_sm[dev].load(std::memory_order_relaxed) : 0;
+  if (per_sm <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kv_store_rows_kernel<kQOutF32>,
+                                                      kThreads, 0) != cudaSuccess)
+      return NVATTN_ERR_CUDA;
+    per_sm = std::max(1, per_sm);
+    if (dev < 64) rows_blocks_per_sm[dev].store(per_sm, std::memory_order_relaxed);
+  }
+  const long long per_wave = (long long)h->sm_count * per_sm * kGroupsPerBlock;
+  p.rows_per_group =
+      (int)std::max(1LL, std::min<long long>(kMaxRowsPerGroup, (rows + per_wave - 1) / per_wave));
   const long long groups = (rows + p.rows_per_group - 1) / p.rows_per_group;
   const long long blocks = (groups + kGroupsPerBlock - 1) / kGroupsPerBlock;
   switch (q_kind) {
