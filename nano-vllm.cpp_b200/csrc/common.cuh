@@ -255,6 +255,20 @@ __device__ __forceinline__ uint32_t cvt_f16x2(float lo, float hi) {
   return r;
 }
 
+// True in one lane of a converged warp (elect.sync over all 32 lanes).  A
+// warp that runs an MMA-issuing loop converged keeps its descriptor and loop
+// values warp-uniform and elects the issuing lane only at each tcgen05
+// instruction.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by a single thread.
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {

@@ -540,9 +540,11 @@ __device__ __forceinline__ void converter_role(PrefillSmem& sm, const PrefillPar
 }
 
 // ---------------------------------------------------------------- MMA issuer
-// Leader only.
-__device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
-                                         const PrefillParams& prm) {
+// Leader only, the whole warp: the loop, its waits and the descriptor
+// arithmetic run converged (warp-uniform values), and one elected lane
+// issues each tcgen05.mma and commit.
+__device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem, const PrefillParams& prm,
+                                         int lane) {
   volatile int* abort_flag = &sm.abort_flag;
   constexpr uint32_t idesc_s = umma_idesc_f16_f32(2 * kBM, kBN, 0, 0);
   constexpr uint32_t idesc_o = umma_idesc_f16_f32(2 * kBM, kD, 0, 1);
@@ -568,22 +570,27 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
       // 64 x 128 bytes further
       const uint64_t a = (k < 4 ? qd0 : qd1) + (uint64_t)((k & 3) * 2);
       const uint64_t b = kd + (uint64_t)((k >> 2) * (64 * 128 / 16) + (k & 3) * 2);
-      umma_pair_ss(tmem + t * 256, a, b, idesc_s, k > 0 ? 1u : 0u);
+      if (elect_one()) umma_pair_ss(tmem + t * 256, a, b, idesc_s, k > 0 ? 1u : 0u);
     }
   };
   auto issue_pv = [&](int t, int gj, bool accumulate) {
     const uint64_t vd = v_desc0 + (uint64_t)ring_slot(2 * gj + 1) * kSlotUnits;
 #pragma unroll
     for (int k = 0; k < kBN / 16; ++k)
-      umma_pair_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8, vd + (uint64_t)(k * 16 * 128 / 16),
-                   idesc_o, (accumulate || k > 0) ? 1u : 0u);
+      if (elect_one())
+        umma_pair_ts(tmem + t * 256 + 128, tmem + t * 256 + k * 8,
+                     vd + (uint64_t)(k * 16 * 128 / 16), idesc_o, (accumulate || k > 0) ? 1u : 0u);
+  };
+  auto commit = [&](uint64_t* bar) {
+    if (elect_one()) umma_commit_pair(bar);
   };
   int tb = 0, k = 0;
   for (;; ++k) {
     const int ws = k & 1;
     if (!mbar_wait_cluster(&sm.work_full[ws], (k >> 1) & 1, prm.status, abort_flag, 48)) break;
     const int valid = sm.work[ws].valid, n_kv = sm.work[ws].n_kv;
-    mbar_arrive_cluster(smem_peer(&sm.work_empty[ws], 0));
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(smem_peer(&sm.work_empty[ws], 0));
     if (!valid) break;
     mbar_wait(&sm.q_full, k & 1, prm.status, abort_flag, 31);
     mbar_wait(&sm.k_ready[tb % kConvAhead], (uint32_t)(tb / kConvAhead) & 1u, prm.status,
@@ -594,11 +601,11 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
     // the first P.V below, which waits for P_t(0), i.e. for the softmax warps
     // to have read the previous O out in their epilogue.
     issue_s(0, tb);
-    umma_commit_pair(&sm.s_full[0]);
+    commit(&sm.s_full[0]);
     issue_s(1, tb);
-    umma_commit_pair(&sm.s_full[1]);
-    umma_commit_pair(&sm.empty[ring_slot(2 * tb)]);
-    if (n_kv == 1) umma_commit_pair(&sm.q_empty);
+    commit(&sm.s_full[1]);
+    commit(&sm.empty[ring_slot(2 * tb)]);
+    if (n_kv == 1) commit(&sm.q_empty);
     for (int j = 0; j < n_kv; ++j) {
       const int gj = tb + j;
       const int vidx = 2 * gj + 1, kidx = 2 * gj + 2;
@@ -610,20 +617,20 @@ __device__ __forceinline__ void mma_role(PrefillSmem& sm, uint32_t tmem,
       issue_pv(0, gj, j > 0);
       if (j + 1 < n_kv) {
         issue_s(0, gj + 1);
-        umma_commit_pair(&sm.s_full[0]);
+        commit(&sm.s_full[0]);
       }
       mbar_wait(&sm.p_full[1], gj & 1, prm.status, abort_flag, 36);
       tc_fence_after();
       issue_pv(1, gj, j > 0);
-      umma_commit_pair(&sm.empty[ring_slot(vidx)]);
+      commit(&sm.empty[ring_slot(vidx)]);
       if (j + 1 < n_kv) {
         issue_s(1, gj + 1);
-        umma_commit_pair(&sm.s_full[1]);
-        umma_commit_pair(&sm.empty[ring_slot(kidx)]);
-        if (j + 2 == n_kv) umma_commit_pair(&sm.q_empty);
+        commit(&sm.s_full[1]);
+        commit(&sm.empty[ring_slot(kidx)]);
+        if (j + 2 == n_kv) commit(&sm.q_empty);
       }
     }
-    umma_commit_pair(&sm.o_final);
+    commit(&sm.o_final);
     tb += n_kv;
   }
   // Drain: every MMA has completed before TMEM is released.
@@ -809,7 +816,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp < 4) {
     regs_dec<96>();
     if (warp == 0 && lane == 0) producer_role(sm, &tm_q, &tm_k, &tm_v, &tm_kr, &tm_vr, prm, rank);
-    if (warp == 1 && lane == 0 && rank == 0) mma_role(sm, tmem, prm);
+    if (warp == 1 && rank == 0) mma_role(sm, tmem, prm, lane);
   } else if (warp >= 12) {
     regs_dec<48>();
     converter_role(sm, prm, threadIdx.x - 384, rank == 0);
