@@ -1044,6 +1044,21 @@ def cpu_sample(lens, bt, k_host_fn, n_target_s=12.0):
     return n / dt, n, dt, cores
 
 
+def headline_config(world, ways, n_seqs, lens, allgather):
+    """The headline workload's `config` object, shared by both arms so that
+    they describe the same job (the reference arm: the same N, its own
+    sample of it timed on the host)."""
+    kv_bytes = int(lens.sum()) * (HKV // ways) * D * 2 * 2
+    return {"workload": WORKLOAD if n_seqs == N_SEQS else f"{WORKLOAD}[first {n_seqs}]",
+            "n_seqs": n_seqs, "q_heads": HQ, "kv_heads": HKV,
+            "head_dim": D, "block_size": BS, "sum_context": int(lens.sum()),
+            "kv_gb_per_gpu": round(kv_bytes / 1e9, 3),
+            "parallelism": (f"kv-head shard x{world}" if ways == world else
+                            f"rank 0's kv-head shard of x{ways} on one GPU"),
+            "l2": "inputs larger than L2 (KV cache >> 126 MB), no flush",
+            "allgather": allgather}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -1093,9 +1108,9 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f16/f32 (ggml chain)",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "n_seqs": N_SEQS,
-                                            "q_heads": HQ, "kv_heads": HKV, "head_dim": D,
-                                            "block_size": BS},
+            "data": "synthetic",
+            "config": headline_config(args.gpus, args.gpus, N_SEQS, lens,
+                                      args.gpus > 1 and not args.no_allgather),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -1385,14 +1400,7 @@ def main():
             "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 KV, fp32 accumulate",
             "data": "synthetic (seeded N(0,1) Q/K/V, log-uniform context lengths)",
-            "config": {"workload": WORKLOAD if B == N_SEQS else f"{WORKLOAD}[first {B}]",
-                       "n_seqs": B, "q_heads": HQ, "kv_heads": HKV,
-                       "head_dim": D, "block_size": BS, "sum_context": int(lens.sum()),
-                       "kv_gb_per_gpu": round(kv_bytes / 1e9, 3),
-                       "parallelism": (f"kv-head shard x{world}" if ways == world else
-                                       f"rank 0's kv-head shard of x{ways} on one GPU"),
-                       "l2": "inputs larger than L2 (KV cache >> 126 MB), no flush",
-                       "allgather": allgather is not None},
+            "config": headline_config(world, ways, B, lens, allgather is not None),
             "roofline": {"bound": "hbm", "kernel": "paged_decode (split-KV, merged in-kernel by the last split)",
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_kind,
