@@ -42,14 +42,18 @@
 //                rings; both CTAs: TMA producer of the CTA's own Q tiles and
 //                K/V halves through a ring of 16 KiB slots (128-byte swizzle)
 //                that runs on across items.
-//   warp 1       TMEM allocation for the pair; in the leader one lane issues
-//                the pair MMAs, interleaving the two tiles so the tensor cores
-//                work on one tile while the other tile's softmax runs:
+//   warp 1       TMEM allocation for the pair; in the leader the warp runs
+//                the MMA loop converged and one elected lane issues the pair
+//                MMAs, interleaving the two tiles so the tensor cores work on
+//                one tile while the other tile's softmax runs:
 //                  PV0(j), S0(j+1), PV1(j), S1(j+1), ...
+//                (strictly in this order from one thread: MMAs execute in
+//                issue order, and two issuing threads would interleave the
+//                tiles' P.V -> S bursts and lengthen each tile's chain).
 //   warps 12-15  K/V converters (one per SM sub-partition): bf16 -> f16 in
-//                place, K(j) then V(j), V rows past the context zeroed (a
-//                cache slot past a sequence's end may hold NaN bits; masked K
-//                columns never reach P).
+//                place, K one key tile ahead of V, V rows past the context
+//                zeroed (a cache slot past a sequence's end may hold NaN
+//                bits; masked K columns never reach P).
 // With the step's own K/V rows given in f16 (nvattn_paged_prefill_rows),
 // keys at or past a sequence's cached prefix are the reference's F16 casts of
 // the graph rows instead of the BF16 cache's: a key tile that starts there is
