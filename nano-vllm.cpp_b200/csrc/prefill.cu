@@ -705,27 +705,40 @@ __device__ __forceinline__ void softmax_role(PrefillSmem& sm, uint32_t tmem,
         m_used = m_new;
       }
       // p = 2^(s*sc - m) in f32 pairs (ex2.approx on the XU port), stored as
-      // f16.  An FMA-pipe polynomial for a share of the pairs was measured
-      // slower: the softmax is issue-bound, and the polynomial costs about six
-      // issue slots per element against one.
+      // f16.  The exponentials set this loop's length (~1,800 cycles per
+      // tile with them, ~700 without); an FMA-pipe polynomial for a share of
+      // the pairs and ex2.approx.f16x2 were both measured slower.
       const uint64_t nm2 = pack2(-m_used, -m_used);
-      uint64_t sum2 = pack2(0.0f, 0.0f);
+      // Pairs of the next 32-key chunk are exponentiated interleaved with
+      // the conversion, sum and store of the current chunk, and the row sum
+      // runs in four accumulators, so the sums do not serialise behind each
+      // pair's ex2 results.
+      uint64_t sum4[4] = {pack2(0.0f, 0.0f), pack2(0.0f, 0.0f), pack2(0.0f, 0.0f),
+                          pack2(0.0f, 0.0f)};
+      auto expo = [&](int i) {  // pair i: 2^(s*sc - m) in place
+        const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
+                                  sc2, nm2);
+        float x0, x1;
+        unpack2(x2, x0, x1);
+        sr[2 * i] = __float_as_uint(fast_exp2(x0));
+        sr[2 * i + 1] = __float_as_uint(fast_exp2(x1));
+      };
+#pragma unroll
+      for (int i = 0; i < 16; ++i) expo(i);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {  // 32 keys -> 16 packed columns
         uint32_t ph[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const uint64_t x2 = ffma2(pack2(__uint_as_float(sr[c * 32 + 2 * i]),
-                                          __uint_as_float(sr[c * 32 + 2 * i + 1])),
-                                    sc2, nm2);
-          float x0, x1;
-          unpack2(x2, x0, x1);
-          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          sum2 = fadd2(sum2, pack2(p0, p1));
+          if (c < 3) expo((c + 1) * 16 + i);  // the next chunk's pair, interleaved
+          const float p0 = __uint_as_float(sr[c * 32 + 2 * i]);
+          const float p1 = __uint_as_float(sr[c * 32 + 2 * i + 1]);
+          sum4[i & 3] = fadd2(sum4[i & 3], pack2(p0, p1));
           ph[i] = cvt_f16x2(p0, p1);
         }
         tmem_st16(s_col + c * 16, ph);
       }
+      const uint64_t sum2 = fadd2(fadd2(sum4[0], sum4[1]), fadd2(sum4[2], sum4[3]));
       float s0, s1;
       unpack2(sum2, s0, s1);
       l = l * alpha + (s0 + s1);
