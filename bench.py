@@ -50,7 +50,7 @@ NCU_TRAFFIC_BYTES_N1 = 11.101e9
 # cycles, from full ncu captures of the CTA-pair kernel with f16 Q/K/V: the
 # chunk shape (2 x 2048 new tokens at [30720, 32768), 32B heads) and the
 # prefix-hit workload itself (None until captured).
-NCU_PREFILL_TENSOR_ACTIVE = 0.547
+NCU_PREFILL_TENSOR_ACTIVE = 0.556
 NCU_PREFIX_HIT_TENSOR_ACTIVE = None
 
 
