@@ -54,7 +54,7 @@ extern "C" {
 #endif
 
 #define NVATTN_VERSION_MAJOR 0
-#define NVATTN_VERSION_MINOR 2
+#define NVATTN_VERSION_MINOR 3
 
 typedef enum nvattn_status {
   NVATTN_OK = 0,
@@ -280,6 +280,31 @@ NVATTN_API nvattn_status nvattn_paged_decode(
     const int32_t* block_tables_dev, int max_blocks,
     const int32_t* context_lens_dev, int max_context_len, float* out_dev,
     nvattn_stream_t stream);
+
+/* One decode step in one launch: nvattn_kv_store_qk_norm_rope of the step's
+ * new token (one per sequence) followed by nvattn_paged_decode -- the
+ * reference's q/k RMSNorm + NEOX RoPE of the decode graph (qwen3.cpp:619-641),
+ * AppendDecodeKV (model_runner.cpp:380-415) and the decode attention -- with
+ * the same results bit for bit (the stored K/V rows and the output rows):
+ *   q_dev        [n_seqs][n_q_heads][head_dim] f32, the raw q projection
+ *                (read only; the normed, rotated q stays on chip)
+ *   k_dev, v_dev [n_seqs][n_kv_heads][head_dim] f32, the new token's rows
+ *   q_norm_w_dev, k_norm_w_dev, positions_dev: as nvattn_kv_store_qk_norm_rope
+ *   slot_mapping_dev[s]: the cache slot of position context_lens[s] - 1
+ *                (what nvattn_plan_decode produces; -1 stores nothing); any
+ *                other slot is still written but reported as
+ *                NVATTN_ERR_INVALID_ARG, since the attention reads position
+ *                context_lens[s] - 1 through the block table
+ *   the rest as nvattn_paged_decode.
+ * The CTA whose key range holds the new token stores its K/V row and reads
+ * the tile that holds it only afterwards; no other CTA reads that position. */
+NVATTN_API nvattn_status nvattn_paged_decode_step(
+    nvattn_handle* h, int layer, int n_seqs, const float* q_dev,
+    const float* k_dev, const float* v_dev, const uint16_t* q_norm_w_dev,
+    const uint16_t* k_norm_w_dev, const int32_t* positions_dev,
+    const int32_t* slot_mapping_dev, uint16_t* k_cache_dev, uint16_t* v_cache_dev,
+    const int32_t* block_tables_dev, int max_blocks, const int32_t* context_lens_dev,
+    int max_context_len, float* out_dev, nvattn_stream_t stream);
 
 /* Causal paged prefill, prefix aware (also serves chunked prefill): sequence
  * s owns query rows [cu_q_lens[s], cu_q_lens[s+1]) at positions

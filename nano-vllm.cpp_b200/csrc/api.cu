@@ -509,6 +509,37 @@ nvattn_status nvattn_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
                                      reinterpret_cast<cudaStream_t>(stream));
 }
 
+nvattn_status nvattn_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, const float* q_dev,
+                                       const float* k_dev, const float* v_dev,
+                                       const uint16_t* q_norm_w_dev,
+                                       const uint16_t* k_norm_w_dev,
+                                       const int32_t* positions_dev,
+                                       const int32_t* slot_mapping_dev, uint16_t* k_cache_dev,
+                                       uint16_t* v_cache_dev, const int32_t* block_tables_dev,
+                                       int max_blocks, const int32_t* context_lens_dev,
+                                       int max_context_len, float* out_dev,
+                                       nvattn_stream_t stream) {
+  if (h == nullptr || layer < 0 || layer >= h->cfg.n_layer || n_seqs < 0 ||
+      n_seqs > h->cfg.max_seqs || n_seqs > nvattn::kMaxDecodeSeqs || max_blocks <= 0 ||
+      max_context_len < 0 || max_context_len > h->cfg.max_context ||
+      (long long)max_context_len > (long long)max_blocks * h->cfg.block_size)
+    return NVATTN_ERR_INVALID_ARG;
+  if (n_seqs == 0) return NVATTN_OK;
+  const void* ptrs[] = {q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev, k_cache_dev,
+                        v_cache_dev, out_dev};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return NVATTN_ERR_INVALID_ARG;
+  if (positions_dev == nullptr || slot_mapping_dev == nullptr || block_tables_dev == nullptr ||
+      context_lens_dev == nullptr)
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  return nvattn::launch_paged_decode_step(
+      h, layer, n_seqs, q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev, positions_dev,
+      slot_mapping_dev, k_cache_dev, v_cache_dev, block_tables_dev, max_blocks,
+      context_lens_dev, max_context_len, out_dev, reinterpret_cast<cudaStream_t>(stream));
+}
+
 nvattn_status nvattn_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int n_tokens,
                                    const uint16_t* q_dev, const int32_t* cu_q_lens_dev,
                                    const int32_t* q_starts_dev, const int32_t* context_lens_dev,

@@ -31,12 +31,23 @@
 // partial; the last split CTA of a (sequence, kv head) to finish -- found by
 // an atomic ticket per (sequence, kv head), which that CTA re-arms to zero --
 // merges the partials and writes the rows, so a decode is one launch.
+//
+// The fused step (nvattn_paged_decode_step) also does the step's q/k
+// RMSNorm + NEOX RoPE and the store of the new K/V row, so a decode step is
+// one launch instead of the store kernel plus this one: warps 2-5 of every
+// CTA norm and rotate the CTA's G query rows (eight lanes per row, the KV
+// store's bit-exact row arithmetic from row_math.cuh) into shared memory,
+// and the CTA whose split holds position ctx-1 -- the only one that reads
+// it -- also writes the new K and V rows to the cache, fences them to the
+// async proxy and releases its producer, which loads the tile holding that
+// position only afterwards.
 #include <atomic>
 #include <functional>
 #include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
+#include "row_math.cuh"
 
 namespace nvattn {
 namespace {
@@ -64,6 +75,18 @@ struct DecodeParams {
   float* ws_ml;
   int* tickets;  // [n_seqs][Hkv] split tickets, zero between launches
   DeviceStatus* status;
+  // fused step only: q above is the raw projection [n_seqs][Hq][128]
+  const float* k_new;  // raw k, v rows [n_seqs][Hkv][128]
+  const float* v_new;
+  const uint16_t* qw;  // RMSNorm weights, bf16 [128]
+  const uint16_t* kw;
+  const int32_t* positions;
+  const int32_t* slots;
+  const float* rope;  // [max_position][cos x 64 | sin x 64]
+  int max_position;
+  float eps;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
 };
 
 template <int G>
@@ -73,8 +96,10 @@ struct __align__(1024) DecodeSmem {
   uint16_t pt[2][kN * 64];             // P^T operand: [token half][row][64]
   float red[2][4][kN];                 // per-warp tile maxima (double-buffered)
   float red_sum[4][kN];
+  float qf[G][128];                    // fused step: the normed, rotated q rows
   uint64_t full[kSlots], empty[kSlots];
   uint64_t q_ready, s_full[2], p_full, o_done;
+  uint64_t kv_stored;                  // fused step: the new K/V row is in the cache
   uint32_t tmem_base;
   int abort_flag;  // raised by the first wait that times out
   int last_split;  // this CTA merges the (sequence, kv head)'s partials
@@ -93,7 +118,97 @@ __device__ __forceinline__ uint16_t bf16_rn(float x) {
   return (uint16_t)(cvt_bf16x2(x, 0.0f) & 0xffffu);
 }
 
+// Fused step, warps 2-5 (128 threads = 16 groups of eight lanes): group g <
+// G norms and rotates q row kvh*G + g into sm.qf[g]; in the CTA that stores
+// (store_here) group G does the K row and group G+1 the V row and writes
+// them to slot_mapping[seq] as the KV store does (positions outside the RoPE
+// table and slots outside the cache reported, slot -1 skipped), and a slot
+// that is not the block table's slot of position ctx-1 is reported (the
+// attention would not read the new row there).  Every warp calls the
+// warp-collective norm; the warps end on a barrier over the four.  (Issuing
+// these loads before the CTA's barrier and TMEM set-up was measured slower.)
 template <int G>
+__device__ __forceinline__ void fused_rows(DecodeSmem<G>& sm, const DecodeParams& prm, int seq,
+                                           int kvh, int ctx, bool store_here, int lane) {
+  using namespace rowmath;
+  const int tq = (int)threadIdx.x - 64;  // 0..127
+  const int grp = tq >> 3, l8 = tq & 7;
+  const int kind = grp < G ? 0 : (store_here && grp == G) ? 1 : (store_here && grp == G + 1) ? 2 : -1;
+  const float* src = kind == 0   ? prm.q + ((long long)seq * prm.Hq + kvh * G + grp) * kD
+                     : kind == 1 ? prm.k_new + ((long long)seq * prm.Hkv + kvh) * kD
+                     : kind == 2 ? prm.v_new + ((long long)seq * prm.Hkv + kvh) * kD
+                                 : nullptr;
+  float x[2 * kPer];
+  if (src != nullptr) {
+    load_row(src, l8, x);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 2 * kPer; ++e) x[e] = 0.0f;
+  }
+  const int pos = prm.positions[seq];
+  const bool pos_ok = pos >= 0 && pos < prm.max_position;
+  bool finite;
+  const float scale = rms_scale(x, kind == 0 || kind == 1, prm.eps, finite);
+  bool nan_rule = !finite;
+  if ((kind == 0 || kind == 1) && pos_ok) {
+    LaneWeights lw;
+    load_weights(kind == 0 ? prm.qw : prm.kw, l8, lw);
+    float w[2 * kPer], c[kPer], sn[kPer];
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) {
+      w[2 * e] = bf16lo_to_f32(lw.w[e]);
+      w[2 * e + 1] = bf16hi_to_f32(lw.w[e]);
+    }
+    const float4* cs = reinterpret_cast<const float4*>(prm.rope + (long long)pos * kD + kPer * l8);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float4 a = __ldg(cs + j), b = __ldg(cs + kHalf / 4 + j);
+      c[4 * j] = a.x; c[4 * j + 1] = a.y; c[4 * j + 2] = a.z; c[4 * j + 3] = a.w;
+      sn[4 * j] = b.x; sn[4 * j + 1] = b.y; sn[4 * j + 2] = b.z; sn[4 * j + 3] = b.w;
+    }
+    norm_rope(x, scale, w, c, sn);
+    nan_rule = nan_rule || !lw.tame;
+  }
+  if (kind >= 0 && !pos_ok && l8 == 0) record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 26, pos);
+  if (kind == 0) {
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) {
+      sm.qf[grp][kPer * l8 + e] = pos_ok ? x[e] : 0.0f;
+      sm.qf[grp][kHalf + kPer * l8 + e] = pos_ok ? x[kPer + e] : 0.0f;
+    }
+  } else if (kind > 0 && pos_ok) {
+    const int slot = prm.slots[seq];
+    if (slot >= 0) {
+      if ((long long)slot >= prm.n_slots) {
+        if (l8 == 0) record_error(prm.status, NVATTN_ERR_OUT_OF_RANGE, 27, slot);
+      } else {
+        if (kind == 1 && l8 == 0 && ctx > 0) {
+          const int p = ctx - 1;
+          const long long want =
+              (long long)prm.block_tables[(long long)seq * prm.max_blocks + p / prm.block_size] *
+                  prm.block_size + p % prm.block_size;
+          if (want != slot) record_error(prm.status, NVATTN_ERR_INVALID_ARG, 28, slot);
+        }
+        uint16_t* dst = (kind == 1 ? prm.k_cache : prm.v_cache) +
+                        (((long long)prm.layer * prm.n_slots + slot) * prm.Hkv + kvh) * kD +
+                        kPer * l8;
+        *reinterpret_cast<uint4*>(dst) = pack8_bf16(x, nan_rule);
+        *reinterpret_cast<uint4*>(dst + kHalf) = pack8_bf16(x + kPer, nan_rule);
+      }
+    }
+  }
+  if (store_here) {
+    // The row's generic-proxy stores reach L2 and are ordered before the
+    // producer's TMA (async proxy) load of the same tile.
+    __threadfence();
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.kv_stored);
+  }
+  named_barrier_sync(1, 128);  // sm.qf complete
+}
+
+template <int G, bool kFused>
 __global__ void __launch_bounds__(kThreads, 2)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, DecodeParams prm) {
@@ -126,6 +241,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int t_end = min(ctx, t_begin + prm.split_tokens);
   const int n_tiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
   volatile int* abort_flag = &sm.abort_flag;
+  // fused step: this split holds position ctx-1 (split 0 for an empty
+  // context) and stores the new K/V row
+  const bool store_here = kFused && split == (ctx > 0 ? (ctx - 1) / prm.split_tokens : 0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSlots; ++i) {
@@ -137,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(&sm.s_full[1], 1);
     mbar_init(&sm.p_full, 4);
     mbar_init(&sm.o_done, 1);
+    mbar_init(&sm.kv_stored, 4);
     sm.abort_flag = 0;
     fence_barrier_init();
   }
@@ -161,6 +280,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int slot = ring_slot(idx);
         if (idx >= kSlots)
           mbar_wait(&sm.empty[slot], ring_parity(idx) ^ 1u, prm.status, abort_flag, 11);
+        // the last tile holds position ctx-1: load it after the new row is stored
+        if (store_here && idx == 2 * (n_tiles - 1))
+          mbar_wait(&sm.kv_stored, 0, prm.status, abort_flag, 24);
         const int tok = t_begin + (idx >> 1) * kTile;
         if ((idx & 1) == 0) {
           bid = prm.block_tables[(long long)seq * prm.max_blocks + tok / prm.block_size];
@@ -227,6 +349,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
 
+    if constexpr (kFused) fused_rows<G>(sm, prm, seq, kvh, ctx, store_here, lane);
+
     // Q^T operand: row g = bf16(q_g * scale*log2e), row G+g = the bf16
     // remainder, rows >= 2G zero; thread r fills column (dim) r.  P^T rows
     // >= 2G are zeroed once and never written again.
@@ -237,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int c = r & 63;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float x = qp[g * kD] * prm.scale_log2;
+        const float x = (kFused ? sm.qf[g][r] : qp[g * kD]) * prm.scale_log2;
         const uint16_t hi = bf16_rn(x);
         const uint16_t lo = bf16_rn(x - __uint_as_float((uint32_t)hi << 16));
         *reinterpret_cast<uint16_t*>(qt + sw128_offset(g, c)) = hi;
@@ -430,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-template <int G>
+template <int G, bool kFused = false>
 nvattn_status launch_g(const CUtensorMap* tk, const CUtensorMap* tv, const DecodeParams& prm,
                        int n_seqs, int max_context_len, cudaStream_t stream) {
   const size_t smem = sizeof(DecodeSmem<G>) + 1024;
@@ -440,8 +564,8 @@ nvattn_status launch_g(const CUtensorMap* tk, const CUtensorMap* tv, const Decod
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
   if (dev >= 64 || !(attr_set_mask.load(std::memory_order_relaxed) & (1ull << dev))) {
-    if (cudaFuncSetAttribute(paged_decode_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(paged_decode_kernel<G, kFused>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return NVATTN_ERR_CUDA;
     if (dev < 64) attr_set_mask.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
@@ -449,7 +573,7 @@ nvattn_status launch_g(const CUtensorMap* tk, const CUtensorMap* tv, const Decod
                                ? (max_context_len + prm.split_tokens - 1) / prm.split_tokens
                                : 1;
   dim3 grid(n_splits_max, prm.Hkv, n_seqs);
-  paged_decode_kernel<G><<<grid, kThreads, smem, stream>>>(*tk, *tv, prm);
+  paged_decode_kernel<G, kFused><<<grid, kThreads, smem, stream>>>(*tk, *tv, prm);
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }
 
@@ -483,11 +607,23 @@ int decode_split_tokens(const nvattn_handle* h, int n_seqs, int max_context_len)
                           n_seqs, max_context_len);
 }
 
-nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const float* q,
-                                  const uint16_t* k_cache, const uint16_t* v_cache,
-                                  const int32_t* block_tables, int max_blocks,
-                                  const int32_t* context_lens, int max_context_len,
-                                  float* out, cudaStream_t stream) {
+// Handle-path launch of the plain decode (fused == nullptr) or of the fused
+// step (fused: the raw k/v rows, norm weights, positions and slots).
+struct FusedStepInputs {
+  const float* k_new;
+  const float* v_new;
+  const uint16_t* qw;
+  const uint16_t* kw;
+  const int32_t* positions;
+  const int32_t* slots;
+};
+
+static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seqs, const float* q,
+                                          const uint16_t* k_cache, const uint16_t* v_cache,
+                                          const int32_t* block_tables, int max_blocks,
+                                          const int32_t* context_lens, int max_context_len,
+                                          float* out, const FusedStepInputs* fused,
+                                          cudaStream_t stream) {
   if (n_seqs == 0) return NVATTN_OK;
   CUtensorMap tk, tv;
   nvattn_status st = get_cache_tensor_map(h, k_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
@@ -495,7 +631,7 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
   st = get_cache_tensor_map(h, v_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tv);
   if (st != NVATTN_OK) return st;
 
-  DecodeParams prm;
+  DecodeParams prm = {};
   prm.Hq = h->cfg.n_q_heads;
   prm.Hkv = h->cfg.n_kv_heads;
   prm.layer = layer;
@@ -515,6 +651,26 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
   prm.ws_ml = h->ws_ml;
   prm.tickets = h->decode_tickets;
   prm.status = h->status_dev;
+  if (fused != nullptr) {
+    prm.k_new = fused->k_new;
+    prm.v_new = fused->v_new;
+    prm.qw = fused->qw;
+    prm.kw = fused->kw;
+    prm.positions = fused->positions;
+    prm.slots = fused->slots;
+    prm.rope = h->rope_table_dev;
+    prm.max_position = h->cfg.max_position;
+    prm.eps = h->cfg.rms_eps;
+    prm.k_cache = const_cast<uint16_t*>(k_cache);
+    prm.v_cache = const_cast<uint16_t*>(v_cache);
+    switch (prm.Hq / prm.Hkv) {
+      case 1: return launch_g<1, true>(&tk, &tv, prm, n_seqs, max_context_len, stream);
+      case 2: return launch_g<2, true>(&tk, &tv, prm, n_seqs, max_context_len, stream);
+      case 4: return launch_g<4, true>(&tk, &tv, prm, n_seqs, max_context_len, stream);
+      case 8: return launch_g<8, true>(&tk, &tv, prm, n_seqs, max_context_len, stream);
+      default: return NVATTN_ERR_UNSUPPORTED;
+    }
+  }
   switch (prm.Hq / prm.Hkv) {
     case 1: return launch_g<1>(&tk, &tv, prm, n_seqs, max_context_len, stream);
     case 2: return launch_g<2>(&tk, &tv, prm, n_seqs, max_context_len, stream);
@@ -522,6 +678,28 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
     case 8: return launch_g<8>(&tk, &tv, prm, n_seqs, max_context_len, stream);
     default: return NVATTN_ERR_UNSUPPORTED;
   }
+}
+
+nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const float* q,
+                                  const uint16_t* k_cache, const uint16_t* v_cache,
+                                  const int32_t* block_tables, int max_blocks,
+                                  const int32_t* context_lens, int max_context_len,
+                                  float* out, cudaStream_t stream) {
+  return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
+                              context_lens, max_context_len, out, nullptr, stream);
+}
+
+nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, const float* q,
+                                       const float* k_new, const float* v_new,
+                                       const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                                       const int32_t* positions, const int32_t* slots,
+                                       uint16_t* k_cache, uint16_t* v_cache,
+                                       const int32_t* block_tables, int max_blocks,
+                                       const int32_t* context_lens, int max_context_len,
+                                       float* out, cudaStream_t stream) {
+  const FusedStepInputs f{k_new, v_new, q_norm_w, k_norm_w, positions, slots};
+  return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
+                              context_lens, max_context_len, out, &f, stream);
 }
 
 // ---------------------------------------------------------------------------

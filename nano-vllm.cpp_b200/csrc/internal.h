@@ -89,6 +89,16 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
                                   const int32_t* block_tables, int max_blocks,
                                   const int32_t* context_lens, int max_context_len,
                                   float* out, cudaStream_t stream);
+// The fused decode step: q/k RMSNorm + RoPE of the raw rows, the store of the
+// new K/V row and the decode in one launch (nvattn_paged_decode_step).
+nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, const float* q,
+                                       const float* k_new, const float* v_new,
+                                       const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                                       const int32_t* positions, const int32_t* slots,
+                                       uint16_t* k_cache, uint16_t* v_cache,
+                                       const int32_t* block_tables, int max_blocks,
+                                       const int32_t* context_lens, int max_context_len,
+                                       float* out, cudaStream_t stream);
 
 nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int n_tokens,
                                    const uint16_t* q, const int32_t* cu_q,

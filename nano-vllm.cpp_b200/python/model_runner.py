@@ -7,9 +7,9 @@ architecture, with the hot path served by libnvattn through its C ABI:
   reference                                          here
   -------------------------------------------------  -----------------------------
   PrepareInputs positions / slots (:138-186)         nvattn.plan_decode (host)
-  q/k RMSNorm + NEOX RoPE (qwen3.cpp:619-641),       nvattn_kv_store_qk_norm_rope
-    AppendDecodeKV (model_runner.cpp:380-415)
-  LoadHistoryKV + concat + FillVarlenMask +           nvattn_paged_decode
+  q/k RMSNorm + NEOX RoPE (qwen3.cpp:619-641),       nvattn_paged_decode_step
+    AppendDecodeKV (model_runner.cpp:380-415),          (one launch)
+    LoadHistoryKV + concat + FillVarlenMask +
     BuildAttention (:300-376; qwen3.cpp:648-662)
   Sample, greedy (model_runner.cpp:417-489)          nvattn_sample
 
@@ -161,16 +161,16 @@ class DecodeRunner:
         return self.bufs
 
     def library_attention(self, layer, q, k, v, stream=None):
-        """Fused q/k norm + RoPE + KV store, then paged decode (libnvattn),
-        on the caller's current stream."""
+        """q/k norm + RoPE, the store of the new K/V rows and the paged decode
+        in one launch (nvattn_paged_decode_step), on the caller's current
+        stream; q, k, v are the raw projections (not modified)."""
         import torch
         stream = stream or torch.cuda.current_stream(self.device)
         b, L = self.bufs, self.w.layers[layer]
-        self.h.kv_store(layer, q, k, v, L["q_norm"].view(torch_int16()),
-                        L["k_norm"].view(torch_int16()), b["pos"], b["slots"], q, self.k_cache,
-                        self.v_cache, stream=stream)
-        self.h.decode(layer, q, self.k_cache, self.v_cache, b["bt"], b["ctx"], self.max_context,
-                      b["attn"], stream=stream)
+        self.h.decode_step(layer, q, k, v, L["q_norm"].view(torch_int16()),
+                           L["k_norm"].view(torch_int16()), b["pos"], b["slots"], self.k_cache,
+                           self.v_cache, b["bt"], b["ctx"], self.max_context, b["attn"],
+                           stream=stream)
         return b["attn"]
 
     def set_inputs(self, tokens, tables: BlockTables):

@@ -32,7 +32,7 @@ EXPORTED = [
     "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
     "nvattn_paged_decode_noalloc", "nvattn_plan_prefill_device", "nvattn_plan_decode_device",
     "nvattn_sample", "nvattn_schedule_prefill_chunks", "nvattn_kv_store_qk_norm_rope_rows",
-    "nvattn_paged_prefill_rows",
+    "nvattn_paged_prefill_rows", "nvattn_paged_decode_step",
 ]
 ERR_SCRATCH_LIMIT = 7
 
@@ -106,6 +106,9 @@ def lib():
                                                         _vp]
         L.nvattn_paged_prefill_rows.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp,
                                                 _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]
+        L.nvattn_paged_decode_step.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                               _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp]
+        L.nvattn_paged_decode_step.restype = _i32
         L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
                                           _vp, _vp]
         L.nvattn_paged_prefill.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32,
@@ -253,6 +256,19 @@ class Handle:
             _ptr(out), _stream_ptr(stream))
         if check:
             _check(st, "nvattn_paged_decode")
+        return st
+
+    def decode_step(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, k_cache, v_cache,
+                    block_tables, context_lens, max_context_len, out, stream=None, check=True):
+        """nvattn_paged_decode_step: the fused store of the new token and the
+        decode in one launch (q, k, v the raw f32 projections)."""
+        st = lib().nvattn_paged_decode_step(
+            self._h, layer, context_lens.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm_w),
+            _ptr(k_norm_w), _ptr(positions), _ptr(slots), _ptr(k_cache), _ptr(v_cache),
+            _ptr(block_tables), block_tables.shape[1], _ptr(context_lens), int(max_context_len),
+            _ptr(out), _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_paged_decode_step")
         return st
 
     def prefill(self, layer, q, cu_q, q_starts, context_lens, block_tables, max_q_len, k_cache,
