@@ -616,6 +616,8 @@ struct FusedStepInputs {
   const uint16_t* kw;
   const int32_t* positions;
   const int32_t* slots;
+  uint16_t* k_cache;  // the caches the new rows are written to
+  uint16_t* v_cache;
 };
 
 static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seqs, const float* q,
@@ -661,8 +663,8 @@ static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seq
     prm.rope = h->rope_table_dev;
     prm.max_position = h->cfg.max_position;
     prm.eps = h->cfg.rms_eps;
-    prm.k_cache = const_cast<uint16_t*>(k_cache);
-    prm.v_cache = const_cast<uint16_t*>(v_cache);
+    prm.k_cache = fused->k_cache;
+    prm.v_cache = fused->v_cache;
     switch (prm.Hq / prm.Hkv) {
       case 1: return launch_g<1, true>(&tk, &tv, prm, n_seqs, max_context_len, stream);
       case 2: return launch_g<2, true>(&tk, &tv, prm, n_seqs, max_context_len, stream);
@@ -697,7 +699,7 @@ nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, 
                                        const int32_t* block_tables, int max_blocks,
                                        const int32_t* context_lens, int max_context_len,
                                        float* out, cudaStream_t stream) {
-  const FusedStepInputs f{k_new, v_new, q_norm_w, k_norm_w, positions, slots};
+  const FusedStepInputs f{k_new, v_new, q_norm_w, k_norm_w, positions, slots, k_cache, v_cache};
   return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
                               context_lens, max_context_len, out, &f, stream);
 }
