@@ -4,9 +4,12 @@ Workload (one step = one decode layer-step): 256 sequences, Qwen3-8B
 attention shape (32 q heads, 8 kv heads, head_dim 128, 256-token blocks,
 BF16 KV), context lengths log-uniform in [1k, 32k] (seeded), block tables
 from a seeded permutation of a pool 10% larger than needed, Q/K/V N(0,1).
-A step stores the new token's K/V through the fused q/k RMSNorm + RoPE +
-slot_mapping kernel and then runs paged split-KV decode over all cached
-tokens.  With --gpus N the 8 kv heads are sharded N ways (rank r owns kv
+A step is one nvattn_paged_decode_step call: the new token's q/k RMSNorm +
+RoPE, the slot_mapping store of its K/V rows, then paged split-KV decode over
+all cached tokens -- one fused launch, or the store and decode launches when
+the decode grid is large (the full workload on one GPU); the explicit two
+calls (nvattn_kv_store_qk_norm_rope, nvattn_paged_decode) are timed beside
+it.  With --gpus N the 8 kv heads are sharded N ways (rank r owns kv
 heads [r*8/N, (r+1)*8/N) and their q heads) -- strong scaling, no collective
 on the data path (--allgather adds the optional all-gather of head outputs).
 
@@ -40,11 +43,15 @@ WORKLOAD = "decode_qwen3_8b_attn_256seq_ctx1k-32k"
 N_SEQS, HQ, HKV, D, BS = 256, 32, 8, 128, 256
 SEED = 0
 
-# DRAM traffic per decode launch of this workload (dram__bytes_read.sum +
-# dram__bytes_write.sum): an ncu capture of the first 32 sequences of this
-# workload moved 1.3774 GB (1.3722 read, 0.0052 written) for 1.3632 GB of
-# algorithmic bytes (x1.0104); scaled to the full launch's 10.987 GB.
-NCU_TRAFFIC_BYTES_N1 = 11.101e9
+# DRAM traffic per step of this workload on one GPU (dram__bytes_read.sum +
+# dram__bytes_write.sum), where the step runs as the store launch and the
+# decode launch.  The decode kernel: an ncu capture of the first 32 sequences
+# moved 1.3774 GB (1.3722 read, 0.0052 written) for 1.3632 GB of algorithmic
+# bytes (x1.0104), scaled to the full launch's 10.987 GB = 11.101 GB; the
+# store launch adds its 11.7 MB (each byte read or written once).  (The fused
+# one-launch kernel on the same 32-sequence capture: 1.3771 GB, x1.0099 of
+# its algorithmic bytes.)
+NCU_TRAFFIC_BYTES_N1 = 11.113e9
 
 # sm__pipe_tensor_cycles_active of paged_prefill_kernel, fraction of elapsed
 # cycles, from full ncu captures of the CTA-pair kernel with f16 Q/K/V: the
@@ -355,8 +362,9 @@ def bench_decode_small(args, world, rank, device):
     """Small decode batch: 4 sequences of 37, 256, 513 and 1000 tokens (the new
     token included), Qwen3-0.6B attention heads (16 q / 8 kv), 64 physical
     blocks of a permuted pool, kv-head sharded.  Far too small to approach the
-    HBM roofline (7.4 MB of K/V); reports the step's device time (fused store +
-    decode) and the decode's GB/s.  On one GPU it also times, on the host
+    HBM roofline (7.4 MB of K/V); reports the step's device time (store +
+    decode, eager and as a CUDA graph; the fused decode step likewise), the
+    decode launch's own device time and its GB/s.  On one GPU it also times, on the host
     cores, the oracle's paged decode in the reference's dtype chain and the
     reference's own decode algorithm (gather every history, append the new
     rows, masked attention over the concatenation) on the same inputs."""
@@ -393,41 +401,43 @@ def bench_decode_small(args, world, rank, device):
     q, out = torch.empty_like(q0), torch.empty((B, hq, D), device=device)
     kc16, vc16 = kc.view(torch.int16), vc.view(torch.int16)
     stream = torch.cuda.current_stream(device)
-    evs = []
 
     def step():
-        z, a, b = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        z.record(stream)
         q.copy_(q0)
         h.kv_store(0, q, kn, vn, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
-        a.record(stream)
         h.decode(0, q, kc16, vc16, bt, ctx, int(lens.max()), out, stream=stream)
+
+    def queue_ahead():
+        # a ~10 ms spin kernel holds the stream while the host issues the
+        # timed calls, so the events around them see back-to-back device work
+        torch.cuda._sleep(20_000_000)
+
+    def loop_ms(body, n, queued):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if queued:
+            queue_ahead()
+        a.record(stream)
+        for _ in range(n):
+            body()
         b.record(stream)
-        evs.append((z, a, b))
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / n
 
     for _ in range(5):
         step()
     torch.cuda.synchronize(device)
     h.check_device("decode_small warmup")
-    evs.clear()
     steps = 50
-    for _ in range(steps):
-        step()
-    torch.cuda.synchronize(device)
+    # the step paced by the host (each call waits for Python to issue it),
+    # then its device time (the same calls queued ahead of the device)
+    host_ms = loop_ms(step, steps, queued=False)
+    step_ms = loop_ms(step, steps, queued=True)
     h.check_device("decode_small")
-    t = torch.tensor([sum(z.elapsed_time(b) for z, _, b in evs) / steps,
-                      sum(a.elapsed_time(b) for _, a, b in evs) / steps],
-                     dtype=torch.float64, device=device)
-    if world > 1:
-        import torch.distributed as dist
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    step_ms, dec_ms = t.tolist()
-    # The eager steps above include the gaps while Python issues each call;
-    # the same step captured once in a CUDA graph and replayed shows the
-    # device time alone (what a C++ caller or a graph-capturing engine sees).
-    # A decode engine that keeps its sequence lengths on the device can also
-    # capture the step's planning: the second graph derives positions, slots
-    # and context lengths with the device planner before the store and decode.
+    # The same step captured once in a CUDA graph and replayed (what a C++
+    # caller or a graph-capturing engine issues).  A decode engine that keeps
+    # its sequence lengths on the device can also capture the step's
+    # planning: the second graph derives positions, slots and context lengths
+    # with the device planner before the store and decode.
     d_lens = torch.from_numpy(lens).to(device)
     ctx_p, pos_p, slots_p = (torch.empty(B, dtype=torch.int32, device=device) for _ in range(3))
 
@@ -451,6 +461,7 @@ def bench_decode_small(args, world, rank, device):
                 g.replay()
             torch.cuda.synchronize(device)
             ga, gb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            queue_ahead()
             ga.record(stream)
             for _ in range(steps):
                 g.replay()
@@ -478,6 +489,7 @@ def bench_decode_small(args, world, rank, device):
     torch.cuda.synchronize(device)
     h.check_device("decode_small planned warmup")
     fz, fb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    queue_ahead()
     fz.record(stream)
     for _ in range(steps):
         fused_body(stream)
@@ -485,23 +497,39 @@ def bench_decode_small(args, world, rank, device):
     torch.cuda.synchronize(device)
     h.check_device("decode_small fused")
     fused_us = fz.elapsed_time(fb) / steps * 1e3
+
+    # the decode launch alone: 20 launches captured in one graph, replayed
+    # queued ahead (per-launch device time, no events between launches)
+    def decode_body20(cs):
+        for _ in range(20):
+            h.decode(0, q, kc16, vc16, bt, ctx, int(lens.max()), out, stream=cs)
+
     graph_us, planned_us = graph_us_of(plain_body), graph_us_of(planned_body)
     fgraph_us, fplanned_us = graph_us_of(fused_body), graph_us_of(fused_planned_body)
-    vals = (graph_us, planned_us, fgraph_us, fplanned_us, fused_us)
+    dec20_us = graph_us_of(decode_body20)
+    vals = (graph_us, planned_us, fgraph_us, fplanned_us, fused_us, dec20_us,
+            host_ms * 1e3, step_ms * 1e3)
     gt = torch.tensor([v if isinstance(v, float) else -1.0 for v in vals],
                       dtype=torch.float64, device=device)
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(gt, op=dist.ReduceOp.MAX)
-    graph_us, planned_us, fgraph_us, fplanned_us, fused_us = (
+    graph_us, planned_us, fgraph_us, fplanned_us, fused_us, dec20_us, host_us, step_us = (
         gt[i].item() if isinstance(v, float) else v for i, v in enumerate(vals))
+    if not isinstance(dec20_us, float):
+        raise RuntimeError(f"decode_small: {dec20_us}")
+    dec_ms = dec20_us / 20 / 1e3
     hbm_peak, _, kind = peaks()
     alg = int(lens.sum()) * hkv * D * 2 * 2 + B * hq * D * 4 * 2 + int(need.sum()) * 4 + B * 4
     gbs = alg / (dec_ms / 1e3) / 1e9
     res = {"workload": "decode_qwen3_0p6b_attn_4seq_len37-1000", "q_heads": Hq, "kv_heads": Hkv,
-           "lens": lens.tolist(), "steps": steps, "step_us": step_ms * 1e3,
+           "lens": lens.tolist(), "steps": steps, "step_us": step_us,
+           "host_paced_step_us": host_us,
            "graph_step_us": graph_us, "graph_step_device_planned_us": planned_us,
            "decode_us": dec_ms * 1e3,
+           "timing": "device time with the host queued ahead (a spin kernel first), events "
+                     "around whole loops; decode_us: 20 decode launches per graph replay; "
+                     "host_paced_step_us: the eager step as Python issues it",
            "fused_step_us": fused_us, "fused_graph_step_us": fgraph_us,
            "fused_graph_step_device_planned_us": fplanned_us,
            "roofline": {"bound": "hbm", "kernel": "paged_decode (split-KV, merged in-kernel by the last split)",
@@ -883,15 +911,15 @@ def run_prefills(args, world, rank, device):
 
 
 def allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq, lens, bt_np, kc,
-                   vc, q):
-    """Second timed loop at N > 1: every step is the store + decode step
-    followed by NCCL's all-gather of the [B][Hq/N][128] head outputs into
+                   vc, normed_q):
+    """Second timed loop at N > 1: every step is the decode step followed by
+    NCCL's all-gather of the [B][Hq/N][128] head outputs into
     [N][B][Hq/N][128] (the head-concatenated attention output o_proj needs).
     Then rank 0 checks the gathered output of the two shortest sequences
     against the oracle (exact math over all heads): every rank hands over
-    those sequences' cache rows and normed q for its heads, and rank 0
-    reassembles them.  Every rank runs the same collectives in the same
-    order."""
+    those sequences' cache rows and normed q for its heads (normed_q() runs
+    the step's KV store, which writes them), and rank 0 reassembles them.
+    Every rank runs the same collectives in the same order."""
     import torch
     import torch.distributed as dist
     gathered = torch.empty((world * B, hq, D), device=device_of(out))
@@ -934,6 +962,7 @@ def allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq, lens
     mine = torch.cat([kc.index_select(0, rows), vc.index_select(0, rows)], 0).contiguous()
     theirs = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype, device=mine.device)
     dist.all_gather_into_tensor(theirs, mine)
+    q = normed_q()
     qs = q[torch.from_numpy(sel).to(q.device)].contiguous()
     q_all = torch.empty((world,) + tuple(qs.shape), dtype=qs.dtype, device=qs.device)
     dist.all_gather_into_tensor(q_all, qs)
@@ -1248,14 +1277,33 @@ def main():
     stream = torch.cuda.current_stream(device)
     kc16, vc16, w16 = kc.view(torch.int16), vc.view(torch.int16), w.view(torch.int16)
 
+    # nvattn_paged_decode_step: the new token's q/k RMSNorm + RoPE and K/V
+    # row store, then the split-KV decode, reading the step's raw q (q0) --
+    # one fused launch, or the store and decode launches for grids past 32
+    # CTAs per SM (this workload's full grid and its 2- and 4-way shards; the
+    # 8-way shard fuses)
+    step_launches = h.decode_step_launches(B, max_ctx)
+
     def step():
-        # the fused store kernel reads the step's q (q0) and writes the
-        # normed, rotated q that decode reads (q)
         ev_z.record(stream)
-        h.kv_store(0, q0, k_new, v_new, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
-        ev_a.record(stream)
-        h.decode(0, q, kc16, vc16, bt, ctx, max_ctx, out, stream=stream)
+        h.decode_step(0, q0, k_new, v_new, w16, w16, pos, slots, kc16, vc16, bt, ctx, max_ctx,
+                      out, stream=stream)
         ev_b.record(stream)
+
+    def two_call_step(z, a, b):
+        # the same step as two launches: the KV store writes the normed,
+        # rotated q (q) that the decode then reads
+        z.record(stream)
+        h.kv_store(0, q0, k_new, v_new, w16, w16, pos, slots, q, kc16, vc16, stream=stream)
+        a.record(stream)
+        h.decode(0, q, kc16, vc16, bt, ctx, max_ctx, out, stream=stream)
+        b.record(stream)
+
+    def normed_q():
+        # the normed, rotated q of this step (what the decode attends with),
+        # for the sharded parity check; the store rewrites the same K/V bits
+        two_call_step(*(torch.cuda.Event() for _ in range(3)))
+        return q
 
     def barrier():
         if world > 1:
@@ -1263,7 +1311,6 @@ def main():
         torch.cuda.synchronize(device)
 
     ev_z = torch.cuda.Event(enable_timing=True)
-    ev_a = torch.cuda.Event(enable_timing=True)
     ev_b = torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local_rank)
     clocks.start()
@@ -1281,34 +1328,32 @@ def main():
     t0.record(stream)
     for _ in range(args.steps):
         ev_z = torch.cuda.Event(enable_timing=True)
-        ev_a = torch.cuda.Event(enable_timing=True)
         ev_b = torch.cuda.Event(enable_timing=True)
         step()
-        pairs.append((ev_z, ev_a, ev_b))
+        pairs.append((ev_z, ev_b))
     t1.record(stream)
     barrier()
     clk = clocks.stop(mark)
     elapsed = t0.elapsed_time(t1) / 1e3
-    dec_ms = sum(a.elapsed_time(b) for _, a, b in pairs) / len(pairs)
-    store_ms = sum(z.elapsed_time(a) for z, a, _ in pairs) / len(pairs)
+    dec_ms = sum(z.elapsed_time(b) for z, b in pairs) / len(pairs)
     h.check_device("timed region")
 
-    # ---- the same step as one launch (nvattn_paged_decode_step) ----
-    # untimed for `value`: with ~11,000 decode CTAs per GPU each CTA's own
-    # q norm + RoPE costs more than the store launch it saves, so the two
-    # calls above stay the headline; the fused step is reported beside it
-    fz = []
-    for i in range(23):
-        z, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        z.record(stream)
-        h.decode_step(0, q0, k_new, v_new, w16, w16, pos, slots, kc16, vc16, bt, ctx, max_ctx,
-                      out, stream=stream)
-        b.record(stream)
-        if i >= 3:
-            fz.append((z, b))
+    # ---- the same step as two launches (KV store, then decode) ----
+    # reported beside the headline, timed the same way (events around the
+    # whole loop, per-launch events inside it)
+    tri = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(23)]
+    for z, a, b in tri[:3]:
+        two_call_step(z, a, b)
+    tc0, tc1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    tc0.record(stream)
+    for z, a, b in tri[3:]:
+        two_call_step(z, a, b)
+    tc1.record(stream)
     torch.cuda.synchronize(device)
-    fused_ms = sum(z.elapsed_time(b) for z, b in fz) / len(fz)
-    h.check_device("fused step")
+    two_ms = tc0.elapsed_time(tc1) / len(tri[3:])
+    store_ms = sum(z.elapsed_time(a) for z, a, _ in tri[3:]) / len(tri[3:])
+    two_dec_ms = sum(a.elapsed_time(b) for _, a, b in tri[3:]) / len(tri[3:])
+    h.check_device("two-call step")
 
     # ---- e2e: the same step through the C ABI with pinned host buffers ----
     # Every step uploads its inputs (q, new k/v, block tables, context
@@ -1349,9 +1394,8 @@ def main():
         stream.wait_event(bb["up"])
         if i >= 2:
             stream.wait_event(bb["down"])  # step i-2's output has been read back
-        h.kv_store(0, bb["q"], bb["k"], bb["v"], w16, w16, bb["pos"], bb["slot"], bb["q"], kc16,
-                   vc16, stream=stream)
-        h.decode(0, bb["q"], kc16, vc16, bb["bt"], bb["ctx"], max_ctx, bb["out"], stream=stream)
+        h.decode_step(0, bb["q"], bb["k"], bb["v"], w16, w16, bb["pos"], bb["slot"], kc16, vc16,
+                      bb["bt"], bb["ctx"], max_ctx, bb["out"], stream=stream)
         bb["done"].record(stream)
         with torch.cuda.stream(down_stream):
             down_stream.wait_event(bb["done"])
@@ -1381,17 +1425,17 @@ def main():
     # the read-back holds the last step's attention output
     assert torch.isfinite(bufs[(args.steps - 1) & 1]["hout"]).all()
 
-    times = torch.tensor([elapsed, e2e_elapsed, dec_ms, store_ms, fused_ms],
+    times = torch.tensor([elapsed, e2e_elapsed, dec_ms, two_ms, store_ms, two_dec_ms],
                          dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    elapsed, e2e_elapsed, dec_ms, store_ms, fused_ms = times.tolist()
+    elapsed, e2e_elapsed, dec_ms, two_ms, store_ms, two_dec_ms = times.tolist()
 
     # ---- N > 1: the step plus the all-gather of the head-sharded outputs ----
     allgather = None
     if world > 1 and not args.no_allgather:
         allgather = allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq,
-                                   lens, bt_np, kc, vc, q)
+                                   lens, bt_np, kc, vc, normed_q)
 
     # CPU baseline (rank 0, one GPU): the oracle's ggml-chain decode on the
     # host cores over the workload's first sequences, with this run's K/V.
@@ -1431,10 +1475,14 @@ def main():
         hbm_peak, _, peak_kind = peaks()
         n_tok = B * args.steps
         kv_bytes = int(lens.sum()) * hkv * D * 2 * 2
-        # cache rows read, q read + out written, block-table entries, lengths
-        alg_bytes = (kv_bytes + B * hq * D * 4 * 2 + int(((lens + BS - 1) // BS).sum()) * 4
+        # decode: cache rows read, q read + out written, block-table entries,
+        # lengths; the store of the new token: its k and v read (f32), its
+        # RoPE row read, its K/V rows written (bf16), position and slot
+        dec_bytes = (kv_bytes + B * hq * D * 4 * 2 + int(((lens + BS - 1) // BS).sum()) * 4
                      + B * 4)
+        alg_bytes = dec_bytes + B * (2 * hkv * D * 4 + D * 4 + 2 * hkv * D * 2 + 8)
         achieved = alg_bytes / (dec_ms / 1e3) / 1e9
+        two_dec_gbs = dec_bytes / (two_dec_ms / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": n_tok / elapsed, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
@@ -1443,7 +1491,12 @@ def main():
             "data": "synthetic (seeded N(0,1) Q/K/V, log-uniform context lengths)",
             "config": headline_config(world, ways, B, lens, allgather is not None),
             "roofline": {"bound": "hbm",
-                         "kernel": "paged_decode (split-KV, merged in-kernel by the last split)",
+                         "kernel": ("paged_decode_step: q/k norm + RoPE and K/V row store, "
+                                    "split-KV decode merged in-kernel by the last split "
+                                    + ("(one fused launch)" if step_launches == 1 else
+                                       "(store launch + decode launch; the step's device "
+                                       "time)")),
+                         "step_launches": step_launches,
                          "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_kind,
                          "traffic": NCU_TRAFFIC_BYTES_N1 if world == 1 else None,
@@ -1451,7 +1504,7 @@ def main():
                          "frac_of_8tbs": achieved / 8000.0},
             "e2e": {"value": n_tok / e2e_elapsed, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * 2,  # fused store + decode per step
+            "gpu_launches": args.steps * step_launches,  # nvattn_paged_decode_step's
             "clocks": clk,
             "decode_long": decode_long,
             "decode_small": decode_small,
@@ -1459,9 +1512,10 @@ def main():
             "sample": sample,
             "prefill_chunked": prefill_chunked,
             "kv_store": kv_store_roofline(B, hq, hkv, store_ms, q_out_bytes=4),
-            "fused_step": {"ms_per_step": fused_ms,
-                           "note": "the same step as one nvattn_paged_decode_step launch "
-                                   "(store + decode), device time"},
+            "two_call_step": {"ms_per_step": two_ms, "decode_ms": two_dec_ms,
+                              "decode_gbs": two_dec_gbs, "store_ms": store_ms,
+                              "note": "the same step as two launches (nvattn_kv_store_qk_"
+                                      "norm_rope, then nvattn_paged_decode), device time"},
         }
         for res in prefill_results:
             line["prefill_" + res["kind"]] = res

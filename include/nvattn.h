@@ -54,7 +54,7 @@ extern "C" {
 #endif
 
 #define NVATTN_VERSION_MAJOR 0
-#define NVATTN_VERSION_MINOR 3
+#define NVATTN_VERSION_MINOR 4
 
 typedef enum nvattn_status {
   NVATTN_OK = 0,
@@ -281,7 +281,7 @@ NVATTN_API nvattn_status nvattn_paged_decode(
     const int32_t* context_lens_dev, int max_context_len, float* out_dev,
     nvattn_stream_t stream);
 
-/* One decode step in one launch: nvattn_kv_store_qk_norm_rope of the step's
+/* One decode step: nvattn_kv_store_qk_norm_rope of the step's
  * new token (one per sequence) followed by nvattn_paged_decode -- the
  * reference's q/k RMSNorm + NEOX RoPE of the decode graph (qwen3.cpp:619-641),
  * AppendDecodeKV (model_runner.cpp:380-415) and the decode attention -- with
@@ -296,8 +296,16 @@ NVATTN_API nvattn_status nvattn_paged_decode(
  *                NVATTN_ERR_INVALID_ARG, since the attention reads position
  *                context_lens[s] - 1 through the block table
  *   the rest as nvattn_paged_decode.
- * The CTA whose key range holds the new token stores its K/V row and reads
- * the tile that holds it only afterwards; no other CTA reads that position. */
+ * Batches whose decode grid (n_seqs x n_kv_heads x the splits of
+ * max_context_len) stays within 32 CTAs per SM run as ONE launch: every CTA
+ * norms and rotates its own query rows, and the CTA whose key range holds the
+ * new token stores its K/V row and reads the tile that holds it only
+ * afterwards (no other CTA reads that position).  Larger grids run as two
+ * launches -- the KV store writing the normed q once per head into the
+ * handle's workspace, then the decode -- because there the CTAs' own query
+ * paths cost more than the store launch; the results are the same bits and
+ * the same errors are reported either way (the decode launch checks the
+ * slot).  nvattn_paged_decode_step_launches tells which form a batch takes. */
 NVATTN_API nvattn_status nvattn_paged_decode_step(
     nvattn_handle* h, int layer, int n_seqs, const float* q_dev,
     const float* k_dev, const float* v_dev, const uint16_t* q_norm_w_dev,
@@ -305,6 +313,13 @@ NVATTN_API nvattn_status nvattn_paged_decode_step(
     const int32_t* slot_mapping_dev, uint16_t* k_cache_dev, uint16_t* v_cache_dev,
     const int32_t* block_tables_dev, int max_blocks, const int32_t* context_lens_dev,
     int max_context_len, float* out_dev, nvattn_stream_t stream);
+
+/* The number of kernel launches nvattn_paged_decode_step makes for a batch
+ * of n_seqs sequences and this max_context_len: 1 (the fused kernel), 2 (the
+ * KV store, then the decode) or 0 (n_seqs == 0).  Host-only; launches
+ * nothing. */
+NVATTN_API nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* h, int n_seqs,
+                                                           int max_context_len, int* launches);
 
 /* Causal paged prefill, prefix aware (also serves chunked prefill): sequence
  * s owns query rows [cu_q_lens[s], cu_q_lens[s+1]) at positions

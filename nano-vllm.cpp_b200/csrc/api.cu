@@ -206,9 +206,11 @@ nvattn_status nvattn_create(const nvattn_config* cfg, nvattn_handle** out) {
     h->max_splits = (int)(splits < 64 ? splits : 64);
     const size_t rows = (size_t)c.max_seqs * c.n_q_heads * h->max_splits;
     const size_t tickets = (size_t)c.max_seqs * c.n_kv_heads * sizeof(int);
+    const size_t q_rows = (size_t)c.max_seqs * c.n_q_heads;
     if (cudaMalloc(&h->ws_o, rows * c.head_dim * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&h->ws_ml, rows * 2 * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&h->decode_tickets, tickets) != cudaSuccess)
+        cudaMalloc(&h->decode_tickets, tickets) != cudaSuccess ||
+        cudaMalloc(&h->q_step, q_rows * c.head_dim * sizeof(float)) != cudaSuccess)
       st = NVATTN_ERR_NO_MEMORY;
     else if (cudaMemset(h->decode_tickets, 0, tickets) != cudaSuccess)
       st = NVATTN_ERR_CUDA;
@@ -231,6 +233,7 @@ nvattn_status nvattn_destroy(nvattn_handle* h) {
   if (h->ws_o) cudaFree(h->ws_o);
   if (h->ws_ml) cudaFree(h->ws_ml);
   if (h->decode_tickets) cudaFree(h->decode_tickets);
+  if (h->q_step) cudaFree(h->q_step);
   if (h->samp_nib) cudaFree(h->samp_nib);
   if (h->samp_exact) cudaFree(h->samp_exact);
   if (h->samp_part) cudaFree(h->samp_part);
@@ -538,6 +541,15 @@ nvattn_status nvattn_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, 
       h, layer, n_seqs, q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev, positions_dev,
       slot_mapping_dev, k_cache_dev, v_cache_dev, block_tables_dev, max_blocks,
       context_lens_dev, max_context_len, out_dev, reinterpret_cast<cudaStream_t>(stream));
+}
+
+nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* h, int n_seqs,
+                                                int max_context_len, int* launches) {
+  if (h == nullptr || launches == nullptr || n_seqs < 0 || max_context_len < 0 ||
+      max_context_len > h->cfg.max_context)
+    return NVATTN_ERR_INVALID_ARG;
+  *launches = n_seqs == 0 ? 0 : nvattn::decode_step_launches(h, n_seqs, max_context_len);
+  return NVATTN_OK;
 }
 
 nvattn_status nvattn_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int n_tokens,

@@ -298,6 +298,18 @@ __global__ void __launch_bounds__(kThreads, 2)
         tma_load_3d_hint(sm.kv[slot][0], map, &sm.full[slot], 0, kvh, row, policy);
         tma_load_3d_hint(sm.kv[slot][1], map, &sm.full[slot], 64, kvh, row, policy);
       }
+      if constexpr (!kFused) {
+        // The decode launch of a step run as two launches makes the fused
+        // kernel's slot check: the stored row must be the one that position
+        // ctx-1 is read from.  This split's last tile holds ctx-1, and a
+        // 128-token tile never crosses a block, so bid is that block.
+        if (prm.slots != nullptr && kvh == 0 && n_tiles > 0 && t_end == ctx) {
+          const int pos = prm.positions[seq], slot = prm.slots[seq];
+          if (pos >= 0 && pos < prm.max_position && slot >= 0 && (long long)slot < prm.n_slots &&
+              bid * prm.block_size + (ctx - 1) % prm.block_size != slot)
+            record_error(prm.status, NVATTN_ERR_INVALID_ARG, 28, slot);
+        }
+      }
       // Drain: the last load of every slot has landed before the CTA exits.
       for (int idx = max(0, n_loads - kSlots); idx < n_loads; ++idx)
         mbar_wait(&sm.full[ring_slot(idx)], ring_parity(idx), prm.status, 14);
@@ -620,12 +632,14 @@ struct FusedStepInputs {
   uint16_t* v_cache;
 };
 
+// `step_check`: the plain decode of a step run as two launches (only the
+// positions and slots of `fused` are used, for the slot check).
 static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seqs, const float* q,
                                           const uint16_t* k_cache, const uint16_t* v_cache,
                                           const int32_t* block_tables, int max_blocks,
                                           const int32_t* context_lens, int max_context_len,
                                           float* out, const FusedStepInputs* fused,
-                                          cudaStream_t stream) {
+                                          bool step_check, cudaStream_t stream) {
   if (n_seqs == 0) return NVATTN_OK;
   CUtensorMap tk, tv;
   nvattn_status st = get_cache_tensor_map(h, k_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
@@ -653,7 +667,11 @@ static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seq
   prm.ws_ml = h->ws_ml;
   prm.tickets = h->decode_tickets;
   prm.status = h->status_dev;
-  if (fused != nullptr) {
+  if (fused != nullptr && step_check) {
+    prm.positions = fused->positions;
+    prm.slots = fused->slots;
+    prm.max_position = h->cfg.max_position;
+  } else if (fused != nullptr) {
     prm.k_new = fused->k_new;
     prm.v_new = fused->v_new;
     prm.qw = fused->qw;
@@ -688,7 +706,25 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
                                   const int32_t* context_lens, int max_context_len,
                                   float* out, cudaStream_t stream) {
   return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
-                              context_lens, max_context_len, out, nullptr, stream);
+                              context_lens, max_context_len, out, nullptr, false, stream);
+}
+
+// The step as one launch or two.  Each CTA of the fused kernel norms and
+// rotates its own G query rows -- the position, then the RoPE row, then the
+// norm, 0.7-1 us on its critical path -- where the separate KV store does
+// that once per head.  Measured on the 256-sequence, 8-kv-head,
+// 1k-32k-token workload (interleaved runs on one GPU) against the store and
+// decode launches: its full grid (32,768 CTAs) ran the fused step ~1 %
+// slower, its 4-way shard (8,192 CTAs, 55 per SM) 0.6 % slower, its 8-way
+// shard (4,096, 28 per SM) ~1 % faster, and small batches gain the whole
+// store launch.  Grids above 32 CTAs per SM take the two launches.
+constexpr long long kStepFusedMaxGridPerSm = 32;
+
+int decode_step_launches(const nvattn_handle* h, int n_seqs, int max_context_len) {
+  const int split = decode_split_tokens(h, n_seqs, max_context_len);
+  const long long splits = max_context_len > 0 ? (max_context_len + split - 1) / split : 1;
+  const long long grid = (long long)n_seqs * h->cfg.n_kv_heads * splits;
+  return grid <= kStepFusedMaxGridPerSm * h->sm_count ? 1 : 2;
 }
 
 nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, const float* q,
@@ -700,8 +736,16 @@ nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, 
                                        const int32_t* context_lens, int max_context_len,
                                        float* out, cudaStream_t stream) {
   const FusedStepInputs f{k_new, v_new, q_norm_w, k_norm_w, positions, slots, k_cache, v_cache};
+  if (decode_step_launches(h, n_seqs, max_context_len) == 2) {
+    const nvattn_status st =
+        launch_kv_store(h, layer, n_seqs, q, k_new, v_new, q_norm_w, k_norm_w, positions, slots,
+                        h->q_step, NVATTN_DTYPE_F32, k_cache, v_cache, nullptr, nullptr, stream);
+    if (st != NVATTN_OK) return st;
+    return launch_decode_common(h, layer, n_seqs, h->q_step, k_cache, v_cache, block_tables,
+                                max_blocks, context_lens, max_context_len, out, &f, true, stream);
+  }
   return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
-                              context_lens, max_context_len, out, &f, stream);
+                              context_lens, max_context_len, out, &f, false, stream);
 }
 
 // ---------------------------------------------------------------------------

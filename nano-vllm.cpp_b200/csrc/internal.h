@@ -42,6 +42,9 @@ struct nvattn_handle {
   float* ws_ml = nullptr;  // [max_seqs][n_kv_heads][max_splits][G][2]
   int* decode_tickets = nullptr;  // [max_seqs][n_kv_heads], zero between launches
   int max_splits = 0;
+  // the normed, rotated q of a decode step run as two launches (the KV store
+  // writes it, the decode reads it): [max_seqs][n_q_heads][head_dim] f32
+  float* q_step = nullptr;
 
   // TMA descriptor cache: fixed storage, replaced round-robin once full, so
   // an entry never moves while the handle lives.
@@ -91,6 +94,9 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
                                   float* out, cudaStream_t stream);
 // The fused decode step: q/k RMSNorm + RoPE of the raw rows, the store of the
 // new K/V row and the decode in one launch (nvattn_paged_decode_step).
+// Launches nvattn_paged_decode_step makes for this batch shape: 1 (the fused
+// kernel) or 2 (the KV store into q_step, then the plain decode).
+int decode_step_launches(const nvattn_handle* h, int n_seqs, int max_context_len);
 nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, const float* q,
                                        const float* k_new, const float* v_new,
                                        const uint16_t* q_norm_w, const uint16_t* k_norm_w,

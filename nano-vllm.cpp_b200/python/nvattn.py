@@ -32,7 +32,7 @@ EXPORTED = [
     "nvattn_kv_store_qk_norm_rope", "nvattn_paged_decode", "nvattn_paged_prefill",
     "nvattn_paged_decode_noalloc", "nvattn_plan_prefill_device", "nvattn_plan_decode_device",
     "nvattn_sample", "nvattn_schedule_prefill_chunks", "nvattn_kv_store_qk_norm_rope_rows",
-    "nvattn_paged_prefill_rows", "nvattn_paged_decode_step",
+    "nvattn_paged_prefill_rows", "nvattn_paged_decode_step", "nvattn_paged_decode_step_launches",
 ]
 ERR_SCRATCH_LIMIT = 7
 
@@ -109,6 +109,7 @@ def lib():
         L.nvattn_paged_decode_step.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                                _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp]
         L.nvattn_paged_decode_step.restype = _i32
+        L.nvattn_paged_decode_step_launches.argtypes = [_vp, _i32, _i32, ctypes.POINTER(_i32)]
         L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
                                           _vp, _vp]
         L.nvattn_paged_prefill.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32,
@@ -260,8 +261,9 @@ class Handle:
 
     def decode_step(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, k_cache, v_cache,
                     block_tables, context_lens, max_context_len, out, stream=None, check=True):
-        """nvattn_paged_decode_step: the fused store of the new token and the
-        decode in one launch (q, k, v the raw f32 projections)."""
+        """nvattn_paged_decode_step: the store of the new token (q/k norm +
+        RoPE) and the decode, in one launch or two (decode_step_launches);
+        q, k, v are the raw f32 projections."""
         st = lib().nvattn_paged_decode_step(
             self._h, layer, context_lens.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm_w),
             _ptr(k_norm_w), _ptr(positions), _ptr(slots), _ptr(k_cache), _ptr(v_cache),
@@ -270,6 +272,15 @@ class Handle:
         if check:
             _check(st, "nvattn_paged_decode_step")
         return st
+
+    def decode_step_launches(self, n_seqs, max_context_len):
+        """Kernel launches decode_step makes for this batch shape: 1 (fused),
+        2 (the KV store, then the decode) or 0 (no sequences)."""
+        n = _i32()
+        _check(lib().nvattn_paged_decode_step_launches(self._h, n_seqs, max_context_len,
+                                                       ctypes.byref(n)),
+               "nvattn_paged_decode_step_launches")
+        return n.value
 
     def prefill(self, layer, q, cu_q, q_starts, context_lens, block_tables, max_q_len, k_cache,
                 v_cache, out, stream=None, check=True, k_rows=None, v_rows=None):

@@ -1,13 +1,14 @@
-"""GPU tests of the fused decode step (nvattn_paged_decode_step): the q/k
-RMSNorm + NEOX RoPE and the store of each sequence's new token
-(nvattn_kv_store_qk_norm_rope) and the paged decode (nvattn_paged_decode) in
-one launch.
+"""GPU tests of the decode step (nvattn_paged_decode_step): the q/k RMSNorm +
+NEOX RoPE and the store of each sequence's new token
+(nvattn_kv_store_qk_norm_rope) and the paged decode (nvattn_paged_decode),
+as one fused launch for grids up to 32 CTAs per SM and as those two launches
+above.
 
-The step must equal the two calls bit for bit -- every stored K/V cache row
-and every output row -- because both run the same row arithmetic
-(row_math.cuh) and the same attention; the tests also hold it to the oracle
-(the reference's store semantics, exact attention) and check the
-error reporting the fused kernel adds.
+Either form must equal the two calls bit for bit -- every stored K/V cache
+row and every output row -- because the fused kernel runs the store's row
+arithmetic (row_math.cuh) and the same attention; the tests also hold it to
+the oracle (the reference's store semantics, exact attention) and check the
+error reporting the step adds (in both forms).
 """
 import numpy as np
 import pytest
@@ -166,4 +167,63 @@ def test_fused_step_replays_in_a_cuda_graph(cuda):
         assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
     h.check_device()
     del g
+    h.close()
+
+
+def _expected_launches(sm, n_seqs, Hkv, max_ctx):
+    """The step's rule restated: the decode's split (2048 tokens, halved while
+    the grid would not fill the GPU eight times over, at least 256), then one
+    launch while the grid stays within 32 CTAs per SM."""
+    split = 2048
+    while split > 256 and n_seqs * Hkv * -(-max_ctx // split) < 8 * sm:
+        split //= 2
+    return 1 if n_seqs * Hkv * max(1, -(-max_ctx // split)) <= 32 * sm else 2
+
+
+def test_step_form_follows_the_grid(cuda):
+    import torch
+    sm = torch.cuda.get_device_properties(0).multi_processor_count
+    h = handle(32, 8, 64, max_seqs=512)
+    assert h.decode_step_launches(0, 1000) == 0
+    for n, L in ((4, 1000), (64, 32768), (128, 32768), (256, 32768), (512, 2048)):
+        assert h.decode_step_launches(n, L) == _expected_launches(sm, n, 8, L), (n, L)
+    if sm == 148:  # B200: the large-batch workload's full grid and its 8-way shard
+        assert h.decode_step_launches(256, 32768) == 2
+        assert h.decode_step_launches(64, 32768) == 2   # the 4-way shard: 8,192
+        assert h.decode_step_launches(32, 32768) == 1   # the 8-way shard: 4,096
+    h.close()
+
+
+def _two_launch_inputs(seed):
+    """128 sequences, one of 32k tokens: 16,384 grid CTAs (two launches on a
+    148-SM B200)."""
+    lens = [32768] + np.random.default_rng(seed).integers(1, 600, 127).tolist()
+    return _inputs(seed, 32, 8, lens)
+
+
+def test_two_launch_step_equals_store_then_decode_bit_for_bit(cuda):
+    import torch
+    c, q, k, v, qw, kw, ctx, pos, slots = _two_launch_inputs(1500)
+    h = handle(32, 8, c.cache.num_blocks, max_seqs=len(ctx))
+    sm = torch.cuda.get_device_properties(0).multi_processor_count
+    assert h.decode_step_launches(len(ctx), int(ctx.max())) == _expected_launches(
+        sm, len(ctx), 8, int(ctx.max()))
+    ref_out, ref_k, ref_v = _two_calls(h, c, q, k, v, qw, kw, ctx, pos, slots)
+    got_out, got_k, got_v = _fused(h, c, q, k, v, qw, kw, ctx, pos, slots)
+    h.check_device()
+    assert np.array_equal(got_k, ref_k) and np.array_equal(got_v, ref_v)
+    assert np.array_equal(got_out.view(np.uint32), ref_out.view(np.uint32))
+    h.close()
+
+
+def test_two_launch_step_reports_a_slot_off_the_new_position(cuda):
+    c, q, k, v, qw, kw, ctx, pos, slots = _two_launch_inputs(1600)
+    used = set(c.block_tables[c.block_tables >= 0].tolist())
+    free = [b for b in range(c.cache.num_blocks) if b not in used]
+    bad = slots.copy()
+    bad[3] = free[0] * 256 + 7
+    h = handle(32, 8, c.cache.num_blocks, max_seqs=len(ctx))
+    _fused(h, c, q, k, v, qw, kw, ctx, pos, bad)
+    st, detail = h.get_error()
+    assert st == nvattn.ERR_INVALID_ARG and detail == bad[3]
     h.close()
