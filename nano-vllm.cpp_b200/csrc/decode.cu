@@ -32,15 +32,16 @@
 // an atomic ticket per (sequence, kv head), which that CTA re-arms to zero --
 // merges the partials and writes the rows, so a decode is one launch.
 //
-// The fused step (nvattn_paged_decode_step) also does the step's q/k
-// RMSNorm + NEOX RoPE and the store of the new K/V row, so a decode step is
-// one launch instead of the store kernel plus this one: warps 2-5 of every
-// CTA norm and rotate the CTA's G query rows (eight lanes per row, the KV
-// store's bit-exact row arithmetic from row_math.cuh) into shared memory,
-// and the CTA whose split holds position ctx-1 -- the only one that reads
-// it -- also writes the new K and V rows to the cache, fences them to the
-// async proxy and releases its producer, which loads the tile holding that
-// position only afterwards.
+// The fused step (nvattn_paged_decode_step on grids up to 32 CTAs per SM)
+// also does the step's q/k RMSNorm + NEOX RoPE and the store of the new K/V
+// row, so a decode step is one launch instead of the store kernel plus this
+// one: warps 2-5 of every CTA norm and rotate the CTA's G query rows (eight
+// lanes per row, the KV store's bit-exact row arithmetic from row_math.cuh)
+// into shared memory, and the CTA whose split holds position ctx-1 -- the
+// only one that reads it -- also writes the new K and V rows to the cache,
+// fences them to the async proxy and releases its producer, which loads the
+// tile holding that position only afterwards.  Larger grids run the step as
+// the store kernel and the plain kernel (launch_paged_decode_step).
 #include <atomic>
 #include <functional>
 #include <mutex>
