@@ -146,26 +146,38 @@ __device__ __forceinline__ void fused_rows(DecodeSmem<G>& sm, const DecodeParams
 #pragma unroll
     for (int e = 0; e < 2 * kPer; ++e) x[e] = 0.0f;
   }
-  const int pos = prm.positions[seq];
-  const bool pos_ok = pos >= 0 && pos < prm.max_position;
-  bool finite;
-  const float scale = rms_scale(x, kind == 0 || kind == 1, prm.eps, finite);
-  bool nan_rule = !finite;
-  if ((kind == 0 || kind == 1) && pos_ok) {
-    LaneWeights lw;
-    load_weights(kind == 0 ? prm.qw : prm.kw, l8, lw);
-    float w[2 * kPer], c[kPer], sn[kPer];
-#pragma unroll
-    for (int e = 0; e < kPer; ++e) {
-      w[2 * e] = bf16lo_to_f32(lw.w[e]);
-      w[2 * e + 1] = bf16hi_to_f32(lw.w[e]);
-    }
-    const float4* cs = reinterpret_cast<const float4*>(prm.rope + (long long)pos * kD + kPer * l8);
+  const bool normed = kind == 0 || kind == 1;
+  // The RoPE row of position ctx-1 -- the new token's position in a decode
+  // step -- and the norm weights load beside the row, not after the
+  // position arrives; a step whose position differs reloads the RoPE row.
+  const int pos_guess = min(max(ctx - 1, 0), prm.max_position - 1);
+  float c[kPer], sn[kPer];
+  auto load_rope = [&](int p) {
+    const float4* cs = reinterpret_cast<const float4*>(prm.rope + (long long)p * kD + kPer * l8);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const float4 a = __ldg(cs + j), b = __ldg(cs + kHalf / 4 + j);
       c[4 * j] = a.x; c[4 * j + 1] = a.y; c[4 * j + 2] = a.z; c[4 * j + 3] = a.w;
       sn[4 * j] = b.x; sn[4 * j + 1] = b.y; sn[4 * j + 2] = b.z; sn[4 * j + 3] = b.w;
+    }
+  };
+  LaneWeights lw;
+  if (normed) {
+    load_rope(pos_guess);
+    load_weights(kind == 0 ? prm.qw : prm.kw, l8, lw);
+  }
+  const int pos = prm.positions[seq];
+  const bool pos_ok = pos >= 0 && pos < prm.max_position;
+  bool finite;
+  const float scale = rms_scale(x, normed, prm.eps, finite);
+  bool nan_rule = !finite;
+  if (normed && pos_ok) {
+    if (pos != pos_guess) load_rope(pos);
+    float w[2 * kPer];
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) {
+      w[2 * e] = bf16lo_to_f32(lw.w[e]);
+      w[2 * e + 1] = bf16hi_to_f32(lw.w[e]);
     }
     norm_rope(x, scale, w, c, sn);
     nan_rule = nan_rule || !lw.tame;

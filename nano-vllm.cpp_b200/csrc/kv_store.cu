@@ -170,8 +170,11 @@ __device__ __forceinline__ const float* row_src(const KvStoreParams& p, int t, i
   return p.v + ((long long)t * p.Hkv + (rr - p.Hq - p.Hkv)) * kD;
 }
 
-template <int kQOut>
-__global__ void __launch_bounds__(kThreads, 2) kv_store_rows_kernel(KvStoreParams p) {
+// kOneRow: every group stores one row (rows_per_group == 1), so nothing is
+// prefetched and three blocks fit on an SM; otherwise the group prefetches
+// its next row while it finishes the current one, two blocks per SM.
+template <int kQOut, bool kOneRow>
+__global__ void __launch_bounds__(kThreads, kOneRow ? 3 : 2) kv_store_rows_kernel(KvStoreParams p) {
   const int l8 = threadIdx.x & 7;  // lane within the row's 8-lane group
   const int rows_per_token = p.Hq + 2 * p.Hkv;
   const int group = blockIdx.x * kGroupsPerBlock + (threadIdx.x >> 3);
@@ -190,14 +193,15 @@ __global__ void __launch_bounds__(kThreads, 2) kv_store_rows_kernel(KvStoreParam
   float c[kPer], sn[kPer];
   LaneWeights lw;
 
-  for (int it = 0; it < p.rows_per_group; ++it) {
+  const int n_rows = kOneRow ? 1 : p.rows_per_group;
+  for (int it = 0; it < n_rows; ++it) {
     const bool valid = row0 + it < p.total_rows;
     const int t_row = t, rr_row = rr;
     float x[2 * kPer];
 #pragma unroll
     for (int e = 0; e < 2 * kPer; ++e) x[e] = xn[e];
     // advance to (and prefetch) the next row
-    if (it + 1 < p.rows_per_group && row0 + it + 1 < p.total_rows) {
+    if (!kOneRow && it + 1 < n_rows && row0 + it + 1 < p.total_rows) {
       if (++rr == rows_per_token) { rr = 0; ++t; }
       load_row(row_src(p, t, rr), l8, xn);
     }
@@ -542,36 +546,46 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
       default: return launch_staged<kQOutF32>(p, plan, h->sm_count, stream);
     }
   }
-  // One wave: as many groups as the resident blocks hold (the kernel's
-  // registers allow two 256-thread blocks per SM; the occupancy is queried
-  // once per device), each group taking as many consecutive rows as that
-  // needs -- a second, partial wave would double the latency of a decode
-  // step's store.
-  static std::atomic<int> rows_blocks_per_sm[64];
+  // One wave: as many groups as the resident blocks hold (the occupancy of
+  // each form is queried once per device), each group taking as many
+  // consecutive rows as that needs -- a second, partial wave would double
+  // the latency of a decode step's store.  Batches that fit one row per
+  // group in the one-row form's wave (three blocks per SM) take it.
+  static std::atomic<int> rows_blocks_per_sm[64][2];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return NVATTN_ERR_CUDA;
-  int per_sm = dev < 64 ? rows_blocks_per_sm[dev].load(std::memory_order_relaxed) : 0;
-  if (per_sm <= 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kv_store_rows_kernel<kQOutF32>,
-                                                      kThreads, 0) != cudaSuccess)
-      return NVATTN_ERR_CUDA;
-    per_sm = std::max(1, per_sm);
-    if (dev < 64) rows_blocks_per_sm[dev].store(per_sm, std::memory_order_relaxed);
+  int per_sm[2] = {0, 0};
+  for (int one = 0; one < 2; ++one) {
+    per_sm[one] = dev < 64 ? rows_blocks_per_sm[dev][one].load(std::memory_order_relaxed) : 0;
+    if (per_sm[one] <= 0) {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+              &per_sm[one],
+              one ? kv_store_rows_kernel<kQOutF32, true> : kv_store_rows_kernel<kQOutF32, false>,
+              kThreads, 0) != cudaSuccess)
+        return NVATTN_ERR_CUDA;
+      per_sm[one] = std::max(1, per_sm[one]);
+      if (dev < 64) rows_blocks_per_sm[dev][one].store(per_sm[one], std::memory_order_relaxed);
+    }
   }
-  const long long per_wave = (long long)h->sm_count * per_sm * kGroupsPerBlock;
+  const bool one_row = rows <= (long long)h->sm_count * per_sm[1] * kGroupsPerBlock;
+  const long long per_wave = (long long)h->sm_count * per_sm[one_row ? 1 : 0] * kGroupsPerBlock;
   p.rows_per_group =
       (int)std::max(1LL, std::min<long long>(kMaxRowsPerGroup, (rows + per_wave - 1) / per_wave));
   const long long groups = (rows + p.rows_per_group - 1) / p.rows_per_group;
-  const long long blocks = (groups + kGroupsPerBlock - 1) / kGroupsPerBlock;
+  const unsigned blocks = (unsigned)((groups + kGroupsPerBlock - 1) / kGroupsPerBlock);
+  auto launch = [&](auto kernel) { kernel<<<blocks, kThreads, 0, stream>>>(p); };
   switch (q_kind) {
     case kQOutBf16:
-      kv_store_rows_kernel<kQOutBf16><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+      one_row ? launch(kv_store_rows_kernel<kQOutBf16, true>)
+              : launch(kv_store_rows_kernel<kQOutBf16, false>);
       break;
     case kQOutF16:
-      kv_store_rows_kernel<kQOutF16><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+      one_row ? launch(kv_store_rows_kernel<kQOutF16, true>)
+              : launch(kv_store_rows_kernel<kQOutF16, false>);
       break;
     default:
-      kv_store_rows_kernel<kQOutF32><<<(unsigned)blocks, kThreads, 0, stream>>>(p);
+      one_row ? launch(kv_store_rows_kernel<kQOutF32, true>)
+              : launch(kv_store_rows_kernel<kQOutF32, false>);
   }
   return cudaGetLastError() == cudaSuccess ? NVATTN_OK : NVATTN_ERR_CUDA;
 }

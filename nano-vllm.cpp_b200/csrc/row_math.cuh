@@ -56,21 +56,33 @@ __device__ __forceinline__ float rms_scale(const float (&x)[2 * kPer], bool norm
     finite = m < 0x7f800000u;
     return 1.0f;
   }
-  double d[2 * kPer];
+  // The lane's 16 squares summed in double into four accumulators.  A
+  // positive normal float widens to double by its bits (exponent re-biased
+  // from 127 to 1023, mantissa shifted up 29 places), which spares the slow
+  // conversion instruction; a warp with a zero, subnormal or non-finite
+  // square redoes the sums with the conversion.
+  float sq[2 * kPer];
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const uint64_t x2 = pack2(x[2 * k], x[2 * k + 1]);
-    float s0, s1;
-    unpack2(fmul2(x2, x2), s0, s1);
-    d[2 * k] = (double)s0;
-    d[2 * k + 1] = (double)s1;
+    unpack2(fmul2(x2, x2), sq[2 * k], sq[2 * k + 1]);
   }
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  uint32_t odd = 0;
 #pragma unroll
-  for (int w = 1; w < 2 * kPer; w *= 2) {
-#pragma unroll
-    for (int e = 0; e < 2 * kPer; e += 2 * w) d[e] = __dadd_rn(d[e], d[e + w]);
+  for (int e = 0; e < 2 * kPer; ++e) {
+    const uint32_t u = __float_as_uint(sq[e]);
+    odd |= (u >> 23) - 1u >= 254u;  // exponent field 0 or 255, or the sign set
+    acc[e & 3] = __dadd_rn(acc[e & 3],
+                           __hiloint2double((int)((u >> 3) + 0x38000000u), (int)(u << 29)));
   }
-  double s = d[0];
+  if (__any_sync(0xffffffffu, odd != 0)) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = 0.0;
+#pragma unroll
+    for (int e = 0; e < 2 * kPer; ++e) acc[e & 3] = __dadd_rn(acc[e & 3], (double)sq[e]);
+  }
+  double s = __dadd_rn(__dadd_rn(acc[0], acc[1]), __dadd_rn(acc[2], acc[3]));
 #pragma unroll
   for (int o = kLanesPerRow / 2; o >= 1; o >>= 1)
     s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o, kLanesPerRow));
@@ -81,9 +93,11 @@ __device__ __forceinline__ float rms_scale(const float (&x)[2 * kPer], bool norm
   static_assert(kD == 128, "1/kD must be a power of two");
   // Rounding d = sum/128 to float drops the low 29 of its 52 mantissa bits;
   // d sits near a float rounding boundary when those bits are within 512
-  // double ulps (> 2^-44 relative, three times the largest tree-vs-sequential
-  // difference) of one half.  Outside the normal float range the exact sum
-  // is always redone.
+  // double ulps (> 2^-44 relative) of one half.  Any order of summing 128
+  // non-negative terms in double is within 127 u S of the exact sum S (u =
+  // 2^-53), so this order and ggml's sequential one differ by at most
+  // 2^-45 S: outside the margin both round to the same float.  Outside the
+  // normal float range the exact sum is always redone.
   const double dm = s * kInvD;
   const int hi = __double2hiint(dm);
   const int ex = (hi >> 20) & 0x7ff;

@@ -100,6 +100,21 @@ def test_fused_step_skips_slot_minus_one(cuda):
     h.close()
 
 
+def test_fused_step_with_positions_other_than_the_last_token(cuda):
+    """The fused kernel loads the RoPE row of position ctx-1 beside the query
+    row; a step whose positions differ (an offset position scheme) reloads it
+    and still equals the two calls bit for bit."""
+    c, q, k, v, qw, kw, ctx, pos, slots = _inputs(1150, 32, 8, [40, 300, 2100, 5000])
+    pos = (pos + np.array([7, 0, 1000, 30000], pos.dtype)).astype(pos.dtype)
+    h = handle(32, 8, c.cache.num_blocks, max_seqs=4)
+    ref_out, ref_k, ref_v = _two_calls(h, c, q, k, v, qw, kw, ctx, pos, slots)
+    got_out, got_k, got_v = _fused(h, c, q, k, v, qw, kw, ctx, pos, slots)
+    h.check_device()
+    assert np.array_equal(got_k, ref_k) and np.array_equal(got_v, ref_v)
+    assert np.array_equal(got_out.view(np.uint32), ref_out.view(np.uint32))
+    h.close()
+
+
 def test_fused_step_reports_a_slot_off_the_new_position(cuda):
     """A slot that is not the block table's slot of position ctx-1 is written
     (as the KV store would) but reported: the attention reads position ctx-1
