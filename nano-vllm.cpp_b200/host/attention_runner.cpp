@@ -173,7 +173,7 @@ bool AttentionRunner::PrepareInputs(const std::vector<SequenceView*>& seqs, bool
          up(d_cu_q_, cu_q_) && up(d_q_starts_, q_starts_);
 }
 
-bool AttentionRunner::RunAttentionLayer(int layer, float* q, const float* k, const float* v,
+bool AttentionRunner::RunAttentionLayer(int layer, const float* q, const float* k, const float* v,
                                         const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                                         uint16_t* k_cache, uint16_t* v_cache, float* out,
                                         cudaStream_t stream) {
@@ -187,12 +187,12 @@ bool AttentionRunner::RunAttentionLayer(int layer, float* q, const float* k, con
                                 d_q_starts_, d_context_lens_, d_block_tables_, max_blocks_,
                                 max_q_len_, k_cache, v_cache, out, s) == NVATTN_OK;
   }
-  if (nvattn_kv_store_qk_norm_rope(handle_, layer, n_tokens_, q, k, v, q_norm_w, k_norm_w,
-                                   d_positions_, d_slots_, q, NVATTN_DTYPE_F32, k_cache, v_cache,
-                                   s) != NVATTN_OK)
-    return false;
-  return nvattn_paged_decode(handle_, layer, n_seqs_, q, k_cache, v_cache, d_block_tables_,
-                             max_blocks_, d_context_lens_, max_context_, out, s) == NVATTN_OK;
+  // one token per sequence: the store of the new token and the decode in one
+  // call (one fused launch, or the two launches for large grids)
+  return nvattn_paged_decode_step(handle_, layer, n_seqs_, q, k, v, q_norm_w, k_norm_w,
+                                  d_positions_, d_slots_, k_cache, v_cache, d_block_tables_,
+                                  max_blocks_, d_context_lens_, max_context_, out,
+                                  s) == NVATTN_OK;
 }
 
 }  // namespace nvattn_host

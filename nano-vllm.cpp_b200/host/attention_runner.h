@@ -52,13 +52,13 @@ class AttentionRunner {
   bool PrepareInputs(const std::vector<SequenceView*>& seqs, bool is_prefill,
                      cudaStream_t stream);
 
-  // One layer of the cut graph: q [n_tokens][Hq][d] f32 (a decode step
-  // overwrites it with the normed, rotated q; a prefill step writes that q as
-  // bf16 to the runner's own buffer), k/v [n_tokens][Hkv][d] f32 (graph
-  // projections), the
-  // layer's q/k norm weights (bf16 [d]), and the BF16 caches (all layers).
-  // Writes attention output [n_tokens][Hq][d] f32.
-  bool RunAttentionLayer(int layer, float* q, const float* k, const float* v,
+  // One layer of the cut graph: q [n_tokens][Hq][d] f32 (read only: a
+  // prefill step writes the normed, rotated q as f16 to the runner's own
+  // buffer; a decode step is one nvattn_paged_decode_step call), k/v
+  // [n_tokens][Hkv][d] f32 (graph projections), the layer's q/k norm weights
+  // (bf16 [d]), and the BF16 caches (all layers).  Writes attention output
+  // [n_tokens][Hq][d] f32.
+  bool RunAttentionLayer(int layer, const float* q, const float* k, const float* v,
                          const uint16_t* q_norm_w, const uint16_t* k_norm_w,
                          uint16_t* k_cache, uint16_t* v_cache, float* out,
                          cudaStream_t stream);
