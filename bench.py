@@ -54,11 +54,12 @@ SEED = 0
 NCU_TRAFFIC_BYTES_N1 = 11.113e9
 
 # sm__pipe_tensor_cycles_active of paged_prefill_kernel, fraction of elapsed
-# cycles, from full ncu captures of the CTA-pair kernel with f16 Q/K/V: the
-# chunk shape (2 x 2048 new tokens at [30720, 32768), 32B heads) and the
-# prefix-hit workload itself (None until captured).
+# cycles, from ncu captures of the CTA-pair kernel with f16 Q/K/V: the chunk
+# shape (2 x 2048 new tokens at [30720, 32768), 32B heads; full capture) and
+# the prefix-hit workload itself (one launch; 42.2 % of the SMs' active
+# cycles, the SMs active 88.6 % of the launch).
 NCU_PREFILL_TENSOR_ACTIVE = 0.556
-NCU_PREFIX_HIT_TENSOR_ACTIVE = None
+NCU_PREFIX_HIT_TENSOR_ACTIVE = 0.374
 
 
 def log(*a):
