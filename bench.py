@@ -517,9 +517,8 @@ def bench_decode_small(args, world, rank, device):
         dist.all_reduce(gt, op=dist.ReduceOp.MAX)
     graph_us, planned_us, fgraph_us, fplanned_us, fused_us, dec20_us, host_us, step_us = (
         gt[i].item() if isinstance(v, float) else v for i, v in enumerate(vals))
-    if not isinstance(dec20_us, float):
-        raise RuntimeError(f"decode_small: {dec20_us}")
-    dec_ms = dec20_us / 20 / 1e3
+    # a failed capture is reported in its field; the decode time is then NaN
+    dec_ms = dec20_us / 20 / 1e3 if isinstance(dec20_us, float) else float("nan")
     hbm_peak, _, kind = peaks()
     alg = int(lens.sum()) * hkv * D * 2 * 2 + B * hq * D * 4 * 2 + int(need.sum()) * 4 + B * 4
     gbs = alg / (dec_ms / 1e3) / 1e9
