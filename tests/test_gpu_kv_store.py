@@ -38,9 +38,12 @@ def test_golden_fixture_bit_exact(cuda):
 
 
 # (8, 1, 20000): ten rows per token, so an 8-lane group's run of rows crosses
-# token boundaries and the (cos, sin) reload path is exercised.
+# token boundaries and the (cos, sin) reload path is exercised.  The
+# register-row kernel's forms: one row per group up to three blocks' worth
+# of groups per SM ((64, 8, 129), (8, 1, 513)), two rows per group above
+# that ((64, 8, 256): 20,480 rows); larger batches take the staged kernel.
 @pytest.mark.parametrize("Hq,Hkv,T", [(16, 8, 3000), (32, 8, 777), (8, 1, 513), (64, 8, 129),
-                                      (8, 1, 20000)])
+                                      (64, 8, 256), (8, 1, 20000)])
 @pytest.mark.parametrize("q_dtype", ["f32", "bf16", "f16"])
 def test_random_tokens_bit_exact(cuda, Hq, Hkv, T, q_dtype):
     rng = np.random.default_rng(Hq * 1000 + T)
