@@ -317,7 +317,9 @@ NVATTN_API nvattn_status nvattn_paged_decode_step(
 /* The number of kernel launches nvattn_paged_decode_step makes for a batch
  * of n_seqs sequences and this max_context_len: 1 (the fused kernel), 2 (the
  * KV store, then the decode) or 0 (n_seqs == 0).  Host-only; launches
- * nothing. */
+ * nothing.  NVATTN_ERR_INVALID_ARG for the arguments nvattn_paged_decode_step
+ * would reject (n_seqs above the handle's max_seqs, max_context_len outside
+ * [0, max_context]). */
 NVATTN_API nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* h, int n_seqs,
                                                            int max_context_len, int* launches);
 

@@ -545,8 +545,8 @@ nvattn_status nvattn_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, 
 
 nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* h, int n_seqs,
                                                 int max_context_len, int* launches) {
-  if (h == nullptr || launches == nullptr || n_seqs < 0 || max_context_len < 0 ||
-      max_context_len > h->cfg.max_context)
+  if (h == nullptr || launches == nullptr || n_seqs < 0 || n_seqs > h->cfg.max_seqs ||
+      max_context_len < 0 || max_context_len > h->cfg.max_context)
     return NVATTN_ERR_INVALID_ARG;
   *launches = n_seqs == 0 ? 0 : nvattn::decode_step_launches(h, n_seqs, max_context_len);
   return NVATTN_OK;

@@ -202,6 +202,9 @@ def test_step_form_follows_the_grid(cuda):
     assert h.decode_step_launches(0, 1000) == 0
     for n, L in ((4, 1000), (64, 32768), (128, 32768), (256, 32768), (512, 2048)):
         assert h.decode_step_launches(n, L) == _expected_launches(sm, n, 8, L), (n, L)
+    for n, L in ((-1, 1000), (513, 1000), (4, 40961), (4, -1)):  # handle: 512 seqs, 40960
+        with pytest.raises(nvattn.NvattnError):
+            h.decode_step_launches(n, L)
     if sm == 148:  # B200: the large-batch workload's full grid and its 8-way shard
         assert h.decode_step_launches(256, 32768) == 2
         assert h.decode_step_launches(64, 32768) == 2   # the 4-way shard: 8,192
