@@ -4,9 +4,10 @@
 // inverse CDF with a caller-supplied uniform draw.
 //
 // Three launches:
-//  1. count  -- one 1024-thread CTA per penalised sequence builds the
-//     history's id histogram in shared memory (16-bit counters, plain atomic
-//     adds; 98304 ids per pass) and writes it out densely as 4-bit counts
+//  1. count  -- one 512-thread CTA per penalised sequence and 49,152-id
+//     segment of the vocabulary (two per SM) builds the segment's histogram
+//     of the history in shared memory (16-bit counters, plain atomic adds)
+//     and writes it out densely as 4-bit counts
 //     min(c, 15) per id, plus the exact count of every id seen 15 or more
 //     times into a [n_seqs][vocab] u32 table (sparse writes, read only
 //     where the 4-bit count is 15).  No state survives between calls: every
@@ -53,8 +54,8 @@ constexpr int kChunk = 4096;             // logits per work item (8 pieces of 51
 constexpr int kMaxChunks = 512;          // n_vocab <= 2,097,152
 constexpr int kStages = 3;
 constexpr int kNibBytes = kChunk / 2;    // 4-bit counts of one chunk
-constexpr int kCountThreads = 1024;
-constexpr int kSegment = 24 * kChunk;    // ids counted per shared-memory pass (16-bit counts)
+constexpr int kCountThreads = 512;
+constexpr int kSegment = 12 * kChunk;    // ids one CTA counts (16-bit counts in shared memory)
 constexpr int kOvSlots = 1024;           // ids seen more than 65535 times, per segment
 constexpr int kPassSmem = kStages * (kChunk * 4 + kNibBytes);
 constexpr int kPassCtasPerSm = 3;
@@ -190,7 +191,7 @@ __device__ __forceinline__ uint32_t sat_pair_bytes(uint32_t w) {
   return (t | (t >> 8)) & 0x0F0Fu;
 }
 
-__global__ void __launch_bounds__(kCountThreads, 1) sample_count_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(kCountThreads, 2) sample_count_kernel(SampleArgs a) {
   extern __shared__ __align__(16) uint8_t csm[];
   __shared__ int ov_full;
   const int s = blockIdx.x;
@@ -209,7 +210,9 @@ __global__ void __launch_bounds__(kCountThreads, 1) sample_count_kernel(SampleAr
   // atomic adds.  Longer ones saturate at 65535 and keep the excess in a
   // small hash table.
   const bool short_hist = he - hb <= 65535;
-  for (long long v0 = 0; v0 < a.cap; v0 += kSegment) {
+  {
+    const long long v0 = (long long)blockIdx.y * kSegment;
+    if (v0 >= a.cap) return;
     const int seg = (int)min((long long)kSegment, a.cap - v0);
     for (int i = threadIdx.x; i < seg / 8; i += kCountThreads)
       reinterpret_cast<uint4*>(c16)[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -962,7 +965,9 @@ nvattn_status launch_sample(nvattn_handle* h, int n_seqs, int n_vocab, const flo
   a.cap = h->samp_cap;
   a.part = reinterpret_cast<PiecePartial*>(h->samp_part);
   a.status = h->status_dev;
-  if (hist != nullptr) sample_count_kernel<<<n_seqs, kCountThreads, kCountSmem, stream>>>(a);
+  if (hist != nullptr)
+    sample_count_kernel<<<dim3((unsigned)n_seqs, (unsigned)((a.cap + kSegment - 1) / kSegment)),
+                          kCountThreads, kCountSmem, stream>>>(a);
   const bool bulk = (reinterpret_cast<uintptr_t>(logits) & 15u) == 0 && row_stride % 4 == 0;
   const long long items = (long long)n_seqs * a.n_chunks;
   const int grid = (int)std::min<long long>(items, (long long)kPassCtasPerSm * h->sm_count);
