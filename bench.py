@@ -1504,7 +1504,8 @@ def main():
                          "frac_of_8tbs": achieved / 8000.0},
             "e2e": {"value": n_tok / e2e_elapsed, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * step_launches,  # nvattn_paged_decode_step's
+            # the kernel launches nvattn_paged_decode_step makes per step (1 or 2)
+            "gpu_launches": args.steps * step_launches,
             "clocks": clk,
             "decode_long": decode_long,
             "decode_small": decode_small,
