@@ -773,6 +773,47 @@ def bench_model_step(args, world, rank, device):
             "attention_gbs": kv_bytes / (attn_ms / 1e3) / 1e9}
 
 
+def bench_kv_store(args, world, rank, device):
+    """The decode step's KV store alone (for profiling): the headline
+    workload's 256 new tokens (this rank's shard of 32 q / 8 kv heads),
+    random positions and slots in a 64-block cache, 50 launches queued behind
+    a spin kernel and timed with CUDA events (device time per launch)."""
+    import torch
+    import nvattn
+    T, ways = N_SEQS, (world if world > 1 else max(1, args.shard_of))
+    hq, hkv = HQ // ways, HKV // ways
+    cfg = nvattn.qwen3_config(n_layer=1, n_q_heads=hq, n_kv_heads=hkv, num_blocks=64,
+                              max_seqs=T, max_context=8192, max_position=40960,
+                              device=device.index)
+    h = nvattn.Handle(cfg)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5000 + rank)
+    kc = torch.zeros((64 * BS, hkv, D), dtype=torch.int16, device=device)
+    vc = torch.zeros_like(kc)
+    q = torch.randn((T, hq, D), generator=gen, device=device)
+    k = torch.randn((T, hkv, D), generator=gen, device=device)
+    v = torch.randn((T, hkv, D), generator=gen, device=device)
+    w = (1 + 0.02 * torch.randn(D, generator=gen, device=device)).to(torch.bfloat16).view(
+        torch.int16)
+    pos = torch.randint(0, 32768, (T,), generator=gen, dtype=torch.int32, device=device)
+    slots = torch.randperm(64 * BS, generator=gen, device=device)[:T].to(torch.int32)
+    qo = torch.empty_like(q)
+    for _ in range(10):
+        h.kv_store(0, q, k, v, w, w, pos, slots, qo, kc, vc)
+    torch.cuda.synchronize(device)
+    h.check_device("kv_store warmup")
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(20_000_000)
+    a.record()
+    for _ in range(50):
+        h.kv_store(0, q, k, v, w, w, pos, slots, qo, kc, vc)
+    b.record()
+    torch.cuda.synchronize(device)
+    h.check_device("kv_store")
+    h.close()
+    return kv_store_roofline(T, hq, hkv, a.elapsed_time(b) / 50, q_out_bytes=4)
+
+
 def bench_sample(args, world, rank, device):
     """Token sampling over the headline batch: 256 rows of Qwen3's 151936
     logits (f32, N(0, 4^2)), temperature 0.8 and repetition penalty 1.2 (the
@@ -1196,6 +1237,8 @@ def main():
                     help="skip the token-sampling workload")
     ap.add_argument("--only-sample", action="store_true",
                     help="run only the token-sampling workload (one JSON line)")
+    ap.add_argument("--only-kv-store", action="store_true",
+                    help="run only the decode step's KV store, back to back (one JSON line)")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="profiling on one GPU: time rank 0's kv-head shard of an N-way split "
                          "(the per-GPU work of an N-GPU run)")
@@ -1229,6 +1272,14 @@ def main():
             print(json.dumps({"metric": METRIC, "value": first.get("tokens_per_s"),
                               "unit": "tokens/s", "n_gpus": world, "prefill": res,
                               "prefill_chunked": chunked}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
+    if args.only_kv_store:
+        res = bench_kv_store(args, world, rank, device)
+        if rank == 0:
+            print(json.dumps({"n_gpus": world, "kv_store": res}), flush=True)
         if world > 1:
             dist.destroy_process_group()
         return 0
