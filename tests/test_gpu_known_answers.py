@@ -1,6 +1,6 @@
 """Known-answer tests of the CUDA attention kernels, independent of the oracle.
 
-Closed forms that hold for any queries (the survey's own known-answer list):
+Closed forms that hold for any queries:
   * a context of one key: the softmax is 1, so the output row is that key's
     V row (to f32 rounding: the kernels form x = s*scale - max with one
     fused multiply-add, so p = 2^x is 1 within an ulp, and O = p*V / p);
