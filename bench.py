@@ -11,7 +11,9 @@ the decode grid is large (the full workload on one GPU); the explicit two
 calls (nvattn_kv_store_qk_norm_rope, nvattn_paged_decode) are timed beside
 it.  With --gpus N the 8 kv heads are sharded N ways (rank r owns kv
 heads [r*8/N, (r+1)*8/N) and their q heads) -- strong scaling, no collective
-on the data path (--allgather adds the optional all-gather of head outputs).
+on the data path; a second timed loop adds the optional all-gather of the
+head outputs and checks the gathered rows against the oracle
+(--no-allgather skips it).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
