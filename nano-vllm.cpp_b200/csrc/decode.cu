@@ -88,6 +88,10 @@ struct DecodeParams {
   float eps;
   uint16_t* k_cache;
   uint16_t* v_cache;
+  // all-gather over peer memory: every final output row is also stored at
+  // the same offset from each g_dst[p] (g_n ranks; 0 = no gather)
+  float* g_dst[nvattn_handle::kMaxGatherRanks];
+  int g_n;
 };
 
 template <int G>
@@ -525,8 +529,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float o = __uint_as_float(ov[g]) + __uint_as_float(ov[G + g]);
-        prm.out[((long long)seq * prm.Hq + kvh * G + g) * kD + r] =
-            l_tot[g] > 0.0f ? o / l_tot[g] : 0.0f;
+        const long long oi = ((long long)seq * prm.Hq + kvh * G + g) * kD + r;
+        const float y = l_tot[g] > 0.0f ? o / l_tot[g] : 0.0f;
+        prm.out[oi] = y;
+        for (int p = 0; p < prm.g_n; ++p) prm.g_dst[p][oi] = y;
       }
     } else {
       const long long base = (long long)(seq * prm.Hkv + kvh) * prm.max_splits;
@@ -565,10 +571,15 @@ __global__ void __launch_bounds__(kThreads, 2)
             L = fmaf(__ldcg(prm.ws_ml + pidx * 2 + 1), w, L);
             O = fmaf(__ldcg(prm.ws_o + pidx * kD + r), w, O);
           }
-          prm.out[((long long)seq * prm.Hq + kvh * G + g) * kD + r] = L > 0.0f ? O / L : 0.0f;
+          const long long oi = ((long long)seq * prm.Hq + kvh * G + g) * kD + r;
+          const float y = L > 0.0f ? O / L : 0.0f;
+          prm.out[oi] = y;
+          for (int p = 0; p < prm.g_n; ++p) prm.g_dst[p][oi] = y;
         }
       }
     }
+    // rows stored to peers are visible system-wide before the CTA ends
+    if (prm.g_n > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -652,7 +663,8 @@ static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seq
                                           const int32_t* block_tables, int max_blocks,
                                           const int32_t* context_lens, int max_context_len,
                                           float* out, const FusedStepInputs* fused,
-                                          bool step_check, cudaStream_t stream) {
+                                          bool step_check, const DecodeParams* gather,
+                                          cudaStream_t stream) {
   if (n_seqs == 0) return NVATTN_OK;
   CUtensorMap tk, tv;
   nvattn_status st = get_cache_tensor_map(h, k_cache, 64, kTile, CU_TENSOR_MAP_SWIZZLE_128B, &tk);
@@ -680,6 +692,10 @@ static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seq
   prm.ws_ml = h->ws_ml;
   prm.tickets = h->decode_tickets;
   prm.status = h->status_dev;
+  if (gather != nullptr) {
+    for (int p = 0; p < gather->g_n; ++p) prm.g_dst[p] = gather->g_dst[p];
+    prm.g_n = gather->g_n;
+  }
   if (fused != nullptr && step_check) {
     prm.positions = fused->positions;
     prm.slots = fused->slots;
@@ -719,7 +735,7 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
                                   const int32_t* context_lens, int max_context_len,
                                   float* out, cudaStream_t stream) {
   return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
-                              context_lens, max_context_len, out, nullptr, false, stream);
+                              context_lens, max_context_len, out, nullptr, false, nullptr, stream);
 }
 
 // The step as one launch or two.  Each CTA of the fused kernel norms and
@@ -740,6 +756,28 @@ int decode_step_launches(const nvattn_handle* h, int n_seqs, int max_context_len
   return grid <= kStepFusedMaxGridPerSm * h->sm_count ? 1 : 2;
 }
 
+static nvattn_status decode_step_impl(nvattn_handle* h, int layer, int n_seqs, const float* q,
+                                      const float* k_new, const float* v_new,
+                                      const uint16_t* q_norm_w, const uint16_t* k_norm_w,
+                                      const int32_t* positions, const int32_t* slots,
+                                      uint16_t* k_cache, uint16_t* v_cache,
+                                      const int32_t* block_tables, int max_blocks,
+                                      const int32_t* context_lens, int max_context_len, float* out,
+                                      const DecodeParams* gather, cudaStream_t stream) {
+  const FusedStepInputs f{k_new, v_new, q_norm_w, k_norm_w, positions, slots, k_cache, v_cache};
+  if (decode_step_launches(h, n_seqs, max_context_len) == 2) {
+    const nvattn_status st =
+        launch_kv_store(h, layer, n_seqs, q, k_new, v_new, q_norm_w, k_norm_w, positions, slots,
+                        h->q_step, NVATTN_DTYPE_F32, k_cache, v_cache, nullptr, nullptr, stream);
+    if (st != NVATTN_OK) return st;
+    return launch_decode_common(h, layer, n_seqs, h->q_step, k_cache, v_cache, block_tables,
+                                max_blocks, context_lens, max_context_len, out, &f, true, gather,
+                                stream);
+  }
+  return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
+                              context_lens, max_context_len, out, &f, false, gather, stream);
+}
+
 nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, const float* q,
                                        const float* k_new, const float* v_new,
                                        const uint16_t* q_norm_w, const uint16_t* k_norm_w,
@@ -748,17 +786,76 @@ nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, 
                                        const int32_t* block_tables, int max_blocks,
                                        const int32_t* context_lens, int max_context_len,
                                        float* out, cudaStream_t stream) {
-  const FusedStepInputs f{k_new, v_new, q_norm_w, k_norm_w, positions, slots, k_cache, v_cache};
-  if (decode_step_launches(h, n_seqs, max_context_len) == 2) {
-    const nvattn_status st =
-        launch_kv_store(h, layer, n_seqs, q, k_new, v_new, q_norm_w, k_norm_w, positions, slots,
-                        h->q_step, NVATTN_DTYPE_F32, k_cache, v_cache, nullptr, nullptr, stream);
-    if (st != NVATTN_OK) return st;
-    return launch_decode_common(h, layer, n_seqs, h->q_step, k_cache, v_cache, block_tables,
-                                max_blocks, context_lens, max_context_len, out, &f, true, stream);
+  return decode_step_impl(h, layer, n_seqs, q, k_new, v_new, q_norm_w, k_norm_w, positions, slots,
+                          k_cache, v_cache, block_tables, max_blocks, context_lens,
+                          max_context_len, out, nullptr, stream);
+}
+
+namespace {
+struct GatherSync {
+  uint32_t* flag[nvattn_handle::kMaxGatherRanks];  // every rank's counter, mapped here
+  uint32_t* own;
+  int n;
+  uint32_t target;
+  DeviceStatus* status;
+};
+
+// One thread, after the decode launch in stream order: adds one to every
+// rank's counter with a system-scope release (this rank's rows, fenced by
+// every CTA of that launch, are then visible to each rank that acquires the
+// count), then waits until this rank's counter shows every rank's rows of
+// this step.  Bounded: after kWaitLimitNs it records NVATTN_ERR_TIMEOUT
+// (detail = the count reached) and returns.
+__global__ void gather_sync_kernel(GatherSync g) {
+  if (threadIdx.x != 0) return;
+  asm volatile("fence.sc.sys;" ::: "memory");
+  for (int p = 0; p < g.n; ++p)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(g.flag[p]) : "memory");
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.own) : "memory");
+    if ((int)(v - g.target) >= 0) return;
+    if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+      record_error(g.status, NVATTN_ERR_TIMEOUT, 80, (long long)v);
+      return;
+    }
+    __nanosleep(64);
   }
-  return launch_decode_common(h, layer, n_seqs, q, k_cache, v_cache, block_tables, max_blocks,
-                              context_lens, max_context_len, out, &f, false, stream);
+}
+}  // namespace
+
+nvattn_status launch_paged_decode_step_gather(nvattn_handle* h, int layer, int n_seqs,
+                                              const float* q, const float* k_new,
+                                              const float* v_new, const uint16_t* q_norm_w,
+                                              const uint16_t* k_norm_w, const int32_t* positions,
+                                              const int32_t* slots, uint16_t* k_cache,
+                                              uint16_t* v_cache, const int32_t* block_tables,
+                                              int max_blocks, const int32_t* context_lens,
+                                              int max_context_len, float* out,
+                                              cudaStream_t stream) {
+  if (!h->g_connected) return NVATTN_ERR_INVALID_ARG;
+  const long long parity_off = (long long)(h->g_steps & 1u) * h->g_ranks * h->g_slice;
+  DecodeParams gd = {};
+  gd.g_n = h->g_ranks;
+  for (int p = 0; p < h->g_ranks; ++p)
+    gd.g_dst[p] = reinterpret_cast<float*>(h->g_peer[p]) + parity_off +
+                  (long long)h->g_rank * h->g_slice;
+  nvattn_status st = decode_step_impl(h, layer, n_seqs, q, k_new, v_new, q_norm_w, k_norm_w,
+                                      positions, slots, k_cache, v_cache, block_tables,
+                                      max_blocks, context_lens, max_context_len, out, &gd, stream);
+  if (st != NVATTN_OK) return st;
+  GatherSync gs = {};
+  for (int p = 0; p < h->g_ranks; ++p)
+    gs.flag[p] = reinterpret_cast<uint32_t*>(h->g_peer[p] + h->g_flag_off);
+  gs.own = reinterpret_cast<uint32_t*>(h->g_own + h->g_flag_off);
+  gs.n = h->g_ranks;
+  gs.target = (uint32_t)h->g_ranks * (h->g_steps + 1u);
+  gs.status = h->status_dev;
+  gather_sync_kernel<<<1, 32, 0, stream>>>(gs);
+  if (cudaGetLastError() != cudaSuccess) return NVATTN_ERR_CUDA;
+  ++h->g_steps;
+  return NVATTN_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -876,7 +973,7 @@ extern "C" NVATTN_API nvattn_status nvattn_paged_decode_noalloc(
   // (possibly one cut short by a timeout) left there.
   if (ticket_bytes > 0 && cudaMemsetAsync(tickets, 0, ticket_bytes, s) != cudaSuccess)
     return NVATTN_ERR_CUDA;
-  DecodeParams prm;
+  DecodeParams prm = {};  // fused-step, slot-check and gather fields stay null
   prm.Hq = c.n_q_heads;
   prm.Hkv = c.n_kv_heads;
   prm.layer = layer;

@@ -46,6 +46,19 @@ struct nvattn_handle {
   // writes it, the decode reads it): [max_seqs][n_q_heads][head_dim] f32
   float* q_step = nullptr;
 
+  // all-gather of decode outputs over peer memory (nvattn_gather_*): this
+  // rank's allocation holds [2 step parities][g_ranks][g_slice] f32 and, at
+  // g_flag_off, the completion counter; g_peer[p] is rank p's allocation
+  // mapped on this device (g_peer[g_rank] == g_own)
+  static constexpr int kMaxGatherRanks = 8;
+  int g_ranks = 0, g_rank = 0;
+  long long g_slice = 0;  // floats per rank: max_seqs * n_q_heads * head_dim
+  size_t g_flag_off = 0;
+  char* g_own = nullptr;
+  char* g_peer[kMaxGatherRanks] = {};
+  bool g_connected = false;
+  unsigned g_steps = 0;   // gather steps issued on this handle
+
   // TMA descriptor cache: fixed storage, replaced round-robin once full, so
   // an entry never moves while the handle lives.
   static constexpr int kMapCacheSize = 16;
@@ -97,6 +110,17 @@ nvattn_status launch_paged_decode(nvattn_handle* h, int layer, int n_seqs, const
 // Launches nvattn_paged_decode_step makes for this batch shape: 1 (the fused
 // kernel) or 2 (the KV store into q_step, then the plain decode).
 int decode_step_launches(const nvattn_handle* h, int n_seqs, int max_context_len);
+// The decode step with every output row also stored into every rank's
+// gathered buffer, then the release/wait launch (nvattn_paged_decode_step_gather).
+nvattn_status launch_paged_decode_step_gather(nvattn_handle* h, int layer, int n_seqs,
+                                              const float* q, const float* k_new,
+                                              const float* v_new, const uint16_t* q_norm_w,
+                                              const uint16_t* k_norm_w, const int32_t* positions,
+                                              const int32_t* slots, uint16_t* k_cache,
+                                              uint16_t* v_cache, const int32_t* block_tables,
+                                              int max_blocks, const int32_t* context_lens,
+                                              int max_context_len, float* out,
+                                              cudaStream_t stream);
 nvattn_status launch_paged_decode_step(nvattn_handle* h, int layer, int n_seqs, const float* q,
                                        const float* k_new, const float* v_new,
                                        const uint16_t* q_norm_w, const uint16_t* k_norm_w,

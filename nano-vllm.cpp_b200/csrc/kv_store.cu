@@ -509,7 +509,7 @@ nvattn_status launch_kv_store(nvattn_handle* h, int layer, int n_tokens, const f
                               uint16_t* k_cache, uint16_t* v_cache, uint16_t* k_rows,
                               uint16_t* v_rows, cudaStream_t stream) {
   if (n_tokens == 0) return NVATTN_OK;
-  KvStoreParams p;
+  KvStoreParams p = {};
   p.n_tokens = n_tokens;
   p.Hq = h->cfg.n_q_heads;
   p.Hkv = h->cfg.n_kv_heads;

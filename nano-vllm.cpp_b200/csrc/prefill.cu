@@ -898,7 +898,7 @@ nvattn_status launch_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int 
     if (st != NVATTN_OK) return st;
   }
 
-  PrefillParams prm;
+  PrefillParams prm = {};
   prm.Hq = Hq;
   prm.Hkv = Hkv;
   prm.G = Hq / Hkv;

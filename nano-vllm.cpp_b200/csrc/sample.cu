@@ -948,7 +948,7 @@ nvattn_status launch_sample(nvattn_handle* h, int n_seqs, int n_vocab, const flo
                             long long row_stride, const float* temps, const float* pens,
                             const int32_t* hist, const int64_t* hist_off, const float* uniforms,
                             int32_t* tokens, cudaStream_t stream) {
-  SampleArgs a;
+  SampleArgs a = {};
   a.n_seqs = n_seqs;
   a.n_vocab = n_vocab;
   a.n_chunks = (n_vocab + kChunk - 1) / kChunk;
