@@ -1011,7 +1011,7 @@ def allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq, lens
     dist.all_gather_into_tensor(q_all, qs)
     res = {"allgather_ms": ag_ms, "steps": args.steps, "ms_per_step": 1e3 * elapsed / args.steps,
            "e2e_with_gather": {"value": B * args.steps / elapsed, "unit": "tokens/s"},
-           "bytes_per_rank": B * hq * D * 4}
+           "bytes_per_rank": B * hq * D * 4, "_gathered": gathered}
     if rank == 0:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
@@ -1027,6 +1027,50 @@ def allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq, lens
                                  "ok": bool(mx <= 2e-2 and mr <= 1e-3),
                                  "against": "oracle TRUTH over all heads"}
     return res
+
+
+def peer_gather_loop(args, world, rank, local_rank, h, peer_step, stream, B, hq, nccl_gathered):
+    """Third timed loop at N > 1: the decode step with the gather fused over
+    peer memory (nvattn_paged_decode_step_gather): each rank's decode stores
+    its output rows into every rank's gathered buffer as it finishes them,
+    then a one-thread launch releases them and waits for the other ranks'.
+    The rows of the last step are compared with the NCCL all-gather's (the
+    same step's outputs: equal bit for bit).  The 64-byte IPC handles travel
+    by an NCCL all-gather; every rank runs the same collectives in order."""
+    import torch
+    import torch.distributed as dist
+    device = device_of(nccl_gathered)
+    mine = torch.tensor(list(h.gather_init(world, rank)), dtype=torch.uint8, device=device)
+    handles = torch.empty((world, mine.numel()), dtype=torch.uint8, device=device)
+    dist.all_gather_into_tensor(handles, mine)
+    hb = handles.cpu().numpy()
+    h.gather_connect([hb[p].tobytes() for p in range(world)])
+    dist.barrier(device_ids=[local_rank])
+    for _ in range(3):
+        peer_step()
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[local_rank])
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        peer_step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    h.check_device("peer gather")
+    dist.barrier(device_ids=[local_rank])
+    tv = torch.tensor([t0.elapsed_time(t1) / 1e3], dtype=torch.float64, device=device)
+    dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+    elapsed = tv.item()
+    got = torch.empty((world, B, hq, D), device=device)
+    h.gather_read(3 + args.steps - 1, B, got, stream=stream)
+    torch.cuda.synchronize()
+    same = torch.tensor([int(torch.equal(got.view(-1), nccl_gathered.view(-1)))], device=device)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    return {"ms_per_step": 1e3 * elapsed / args.steps,
+            "e2e_with_gather": {"value": B * args.steps / elapsed, "unit": "tokens/s"},
+            "identical_to_nccl_gather": bool(same.item()),
+            "note": "decode step whose output rows are stored into every rank's gathered "
+                    "buffer over NVLink, plus one release/wait launch; no NCCL on the data path"}
 
 
 def reassemble_shards(kv_ranks, q_ranks, need):
@@ -1489,6 +1533,13 @@ def main():
     if world > 1 and not args.no_allgather:
         allgather = allgather_loop(args, world, rank, local_rank, step, out, stream, B, hq,
                                    lens, bt_np, kc, vc, normed_q)
+
+        def peer_step():
+            h.decode_step_gather(0, q0, k_new, v_new, w16, w16, pos, slots, kc16, vc16, bt, ctx,
+                                 max_ctx, out, stream=stream)
+
+        allgather["peer_gather"] = peer_gather_loop(args, world, rank, local_rank, h, peer_step,
+                                                    stream, B, hq, allgather.pop("_gathered"))
 
     # CPU baseline (rank 0, one GPU): the oracle's ggml-chain decode on the
     # host cores over the workload's first sequences, with this run's K/V.

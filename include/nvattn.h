@@ -54,7 +54,7 @@ extern "C" {
 #endif
 
 #define NVATTN_VERSION_MAJOR 0
-#define NVATTN_VERSION_MINOR 4
+#define NVATTN_VERSION_MINOR 5
 
 typedef enum nvattn_status {
   NVATTN_OK = 0,
@@ -322,6 +322,47 @@ NVATTN_API nvattn_status nvattn_paged_decode_step(
  * [0, max_context]). */
 NVATTN_API nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* h, int n_seqs,
                                                            int max_context_len, int* launches);
+
+/* ---- The decode step with the all-gather of head outputs over peer memory ----
+ * KV-head sharding across n_ranks GPUs of one node (one process and one
+ * handle per GPU, every handle created with the same max_seqs): rank r's
+ * output rows [n_seqs][n_q_heads][head_dim] are the heads of its kv-head
+ * share, and o_proj needs every rank's rows.  Instead of a separate
+ * all-gather, the decode launch stores each output row into every rank's
+ * gathered buffer directly (plain peer-to-peer stores over NVLink, as each
+ * row is finished), and a one-thread launch after it releases this rank's
+ * rows to all ranks and waits -- bounded, NVATTN_ERR_TIMEOUT after ~2 s --
+ * until every rank's rows of the step have arrived.
+ *   nvattn_gather_init: allocates this rank's gathered buffer
+ *     [2][n_ranks][max_seqs][n_q_heads][head_dim] f32 (two step parities)
+ *     and a completion counter, and writes their CUDA IPC handle
+ *     (NVATTN_IPC_HANDLE_BYTES bytes) to ipc_handle_out.
+ *   nvattn_gather_connect: ipc_handles = every rank's handle, rank order
+ *     (n_ranks x NVATTN_IPC_HANDLE_BYTES bytes, exchanged by the caller);
+ *     maps every peer's buffer on this device.  NVATTN_ERR_INVALID_ARG if a
+ *     handle's rank count, rank or buffer shape differs from this rank's.  All ranks connect before any
+ *     rank takes a gather step, and no rank destroys its handle while
+ *     another may still store to it.
+ *   nvattn_paged_decode_step_gather: nvattn_paged_decode_step (same
+ *     arguments and results) plus the gather of its output rows; a
+ *     collective -- every rank calls it the same number of times, with the
+ *     same n_seqs.  Step s (counted per handle from 0) fills parity s & 1.
+ *   nvattn_gather_read: copies step `step`'s gathered rows (one of the last
+ *     two steps) into out_dev [n_ranks][n_seqs][n_q_heads][head_dim] on the
+ *     stream -- rank-major, as an all-gather of the ranks' outputs. */
+#define NVATTN_IPC_HANDLE_BYTES 128
+NVATTN_API nvattn_status nvattn_gather_init(nvattn_handle* h, int n_ranks, int rank,
+                                            void* ipc_handle_out);
+NVATTN_API nvattn_status nvattn_gather_connect(nvattn_handle* h, const void* ipc_handles);
+NVATTN_API nvattn_status nvattn_paged_decode_step_gather(
+    nvattn_handle* h, int layer, int n_seqs, const float* q_dev,
+    const float* k_dev, const float* v_dev, const uint16_t* q_norm_w_dev,
+    const uint16_t* k_norm_w_dev, const int32_t* positions_dev,
+    const int32_t* slot_mapping_dev, uint16_t* k_cache_dev, uint16_t* v_cache_dev,
+    const int32_t* block_tables_dev, int max_blocks, const int32_t* context_lens_dev,
+    int max_context_len, float* out_dev, nvattn_stream_t stream);
+NVATTN_API nvattn_status nvattn_gather_read(nvattn_handle* h, unsigned step, int n_seqs,
+                                            float* out_dev, nvattn_stream_t stream);
 
 /* Causal paged prefill, prefix aware (also serves chunked prefill): sequence
  * s owns query rows [cu_q_lens[s], cu_q_lens[s+1]) at positions

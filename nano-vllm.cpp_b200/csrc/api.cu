@@ -234,6 +234,9 @@ nvattn_status nvattn_destroy(nvattn_handle* h) {
   if (h->ws_ml) cudaFree(h->ws_ml);
   if (h->decode_tickets) cudaFree(h->decode_tickets);
   if (h->q_step) cudaFree(h->q_step);
+  for (int p = 0; p < h->g_ranks; ++p)
+    if (p != h->g_rank && h->g_peer[p] != nullptr) cudaIpcCloseMemHandle(h->g_peer[p]);
+  if (h->g_own) cudaFree(h->g_own);
   if (h->samp_nib) cudaFree(h->samp_nib);
   if (h->samp_exact) cudaFree(h->samp_exact);
   if (h->samp_part) cudaFree(h->samp_part);
@@ -550,6 +553,134 @@ nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* h, int n_se
     return NVATTN_ERR_INVALID_ARG;
   *launches = n_seqs == 0 ? 0 : nvattn::decode_step_launches(h, n_seqs, max_context_len);
   return NVATTN_OK;
+}
+
+namespace {
+// What a rank's exported handle carries after the CUDA IPC handle: the shape
+// every rank's buffer must share (peer stores land at offsets computed from
+// this rank's own shape).
+struct GatherMeta {
+  long long slice;
+  long long flag_off;
+  int n_ranks;
+  int rank;
+};
+static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(GatherMeta) <= NVATTN_IPC_HANDLE_BYTES,
+              "IPC handle size");
+}  // namespace
+
+nvattn_status nvattn_gather_init(nvattn_handle* h, int n_ranks, int rank, void* ipc_handle_out) {
+  if (h == nullptr || ipc_handle_out == nullptr || n_ranks < 1 ||
+      n_ranks > nvattn_handle::kMaxGatherRanks || rank < 0 || rank >= n_ranks ||
+      h->g_own != nullptr)
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  const long long slice = (long long)h->cfg.max_seqs * h->cfg.n_q_heads * h->cfg.head_dim;
+  const size_t flag_off = ((size_t)2 * n_ranks * slice * sizeof(float) + 255) / 256 * 256;
+  char* own = nullptr;
+  if (cudaMalloc(&own, flag_off + 256) != cudaSuccess) {
+    cudaGetLastError();
+    return NVATTN_ERR_NO_MEMORY;
+  }
+  cudaIpcMemHandle_t ipc;
+  if (cudaMemset(own + flag_off, 0, 256) != cudaSuccess ||
+      cudaIpcGetMemHandle(&ipc, own) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(own);
+    return NVATTN_ERR_CUDA;
+  }
+  std::memset(ipc_handle_out, 0, NVATTN_IPC_HANDLE_BYTES);
+  std::memcpy(ipc_handle_out, &ipc, sizeof(ipc));
+  const GatherMeta meta{slice, (long long)flag_off, n_ranks, rank};
+  std::memcpy(static_cast<char*>(ipc_handle_out) + sizeof(ipc), &meta, sizeof(meta));
+  h->g_own = own;
+  h->g_ranks = n_ranks;
+  h->g_rank = rank;
+  h->g_slice = slice;
+  h->g_flag_off = flag_off;
+  h->g_peer[rank] = own;
+  h->g_steps = 0;
+  return NVATTN_OK;
+}
+
+nvattn_status nvattn_gather_connect(nvattn_handle* h, const void* ipc_handles) {
+  if (h == nullptr || ipc_handles == nullptr || h->g_own == nullptr || h->g_connected)
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  const char* all = static_cast<const char*>(ipc_handles);
+  for (int p = 0; p < h->g_ranks; ++p) {
+    GatherMeta meta;
+    std::memcpy(&meta, all + (size_t)p * NVATTN_IPC_HANDLE_BYTES + sizeof(cudaIpcMemHandle_t),
+                sizeof(meta));
+    if (meta.slice != h->g_slice || meta.flag_off != (long long)h->g_flag_off ||
+        meta.n_ranks != h->g_ranks || meta.rank != p)
+      return NVATTN_ERR_INVALID_ARG;
+  }
+  for (int p = 0; p < h->g_ranks; ++p) {
+    if (p == h->g_rank) continue;
+    cudaIpcMemHandle_t ipc;
+    std::memcpy(&ipc, all + (size_t)p * NVATTN_IPC_HANDLE_BYTES, sizeof(ipc));
+    void* ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, ipc, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      for (int q = 0; q < p; ++q)
+        if (q != h->g_rank && h->g_peer[q] != nullptr) {
+          cudaIpcCloseMemHandle(h->g_peer[q]);
+          h->g_peer[q] = nullptr;
+        }
+      return NVATTN_ERR_CUDA;
+    }
+    h->g_peer[p] = static_cast<char*>(ptr);
+  }
+  h->g_connected = true;
+  return NVATTN_OK;
+}
+
+nvattn_status nvattn_paged_decode_step_gather(
+    nvattn_handle* h, int layer, int n_seqs, const float* q_dev, const float* k_dev,
+    const float* v_dev, const uint16_t* q_norm_w_dev, const uint16_t* k_norm_w_dev,
+    const int32_t* positions_dev, const int32_t* slot_mapping_dev, uint16_t* k_cache_dev,
+    uint16_t* v_cache_dev, const int32_t* block_tables_dev, int max_blocks,
+    const int32_t* context_lens_dev, int max_context_len, float* out_dev,
+    nvattn_stream_t stream) {
+  if (h == nullptr || !h->g_connected || layer < 0 || layer >= h->cfg.n_layer || n_seqs < 0 ||
+      n_seqs > h->cfg.max_seqs || n_seqs > nvattn::kMaxDecodeSeqs || max_blocks <= 0 ||
+      max_context_len < 0 || max_context_len > h->cfg.max_context ||
+      (long long)max_context_len > (long long)max_blocks * h->cfg.block_size)
+    return NVATTN_ERR_INVALID_ARG;
+  const void* ptrs[] = {q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev, k_cache_dev,
+                        v_cache_dev, out_dev};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return NVATTN_ERR_INVALID_ARG;
+  if (positions_dev == nullptr || slot_mapping_dev == nullptr || block_tables_dev == nullptr ||
+      context_lens_dev == nullptr)
+    return NVATTN_ERR_INVALID_ARG;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  return nvattn::launch_paged_decode_step_gather(
+      h, layer, n_seqs, q_dev, k_dev, v_dev, q_norm_w_dev, k_norm_w_dev, positions_dev,
+      slot_mapping_dev, k_cache_dev, v_cache_dev, block_tables_dev, max_blocks, context_lens_dev,
+      max_context_len, out_dev, reinterpret_cast<cudaStream_t>(stream));
+}
+
+nvattn_status nvattn_gather_read(nvattn_handle* h, unsigned step, int n_seqs, float* out_dev,
+                                 nvattn_stream_t stream) {
+  if (h == nullptr || !h->g_connected || out_dev == nullptr || n_seqs < 0 ||
+      n_seqs > h->cfg.max_seqs || step >= h->g_steps || h->g_steps - step > 2u)
+    return NVATTN_ERR_INVALID_ARG;
+  if (n_seqs == 0) return NVATTN_OK;
+  DeviceGuard guard(h->cfg.device);
+  if (!guard.ok()) return NVATTN_ERR_CUDA;
+  const size_t row_bytes = (size_t)n_seqs * h->cfg.n_q_heads * h->cfg.head_dim * sizeof(float);
+  const float* src = reinterpret_cast<const float*>(h->g_own) +
+                     (long long)(step & 1u) * h->g_ranks * h->g_slice;
+  return cudaMemcpy2DAsync(out_dev, row_bytes, src, (size_t)h->g_slice * sizeof(float), row_bytes,
+                           (size_t)h->g_ranks, cudaMemcpyDeviceToDevice,
+                           reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? NVATTN_OK
+             : NVATTN_ERR_CUDA;
 }
 
 nvattn_status nvattn_paged_prefill(nvattn_handle* h, int layer, int n_seqs, int n_tokens,

@@ -33,7 +33,10 @@ EXPORTED = [
     "nvattn_paged_decode_noalloc", "nvattn_plan_prefill_device", "nvattn_plan_decode_device",
     "nvattn_sample", "nvattn_schedule_prefill_chunks", "nvattn_kv_store_qk_norm_rope_rows",
     "nvattn_paged_prefill_rows", "nvattn_paged_decode_step", "nvattn_paged_decode_step_launches",
+    "nvattn_gather_init", "nvattn_gather_connect", "nvattn_paged_decode_step_gather",
+    "nvattn_gather_read",
 ]
+IPC_HANDLE_BYTES = 128
 ERR_SCRATCH_LIMIT = 7
 
 
@@ -110,6 +113,10 @@ def lib():
                                                _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp]
         L.nvattn_paged_decode_step.restype = _i32
         L.nvattn_paged_decode_step_launches.argtypes = [_vp, _i32, _i32, ctypes.POINTER(_i32)]
+        L.nvattn_gather_init.argtypes = [_vp, _i32, _i32, ctypes.c_char_p]
+        L.nvattn_gather_connect.argtypes = [_vp, ctypes.c_char_p]
+        L.nvattn_paged_decode_step_gather.argtypes = L.nvattn_paged_decode_step.argtypes
+        L.nvattn_gather_read.argtypes = [_vp, ctypes.c_uint, _i32, _vp, _vp]
         L.nvattn_paged_decode.argtypes = [_vp, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
                                           _vp, _vp]
         L.nvattn_paged_prefill.argtypes = [_vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i32,
@@ -272,6 +279,38 @@ class Handle:
         if check:
             _check(st, "nvattn_paged_decode_step")
         return st
+
+    # ---- the decode step with the all-gather over peer memory ----
+    def gather_init(self, n_ranks, rank):
+        """This rank's gathered buffer; returns its IPC handle (bytes) for the
+        other ranks."""
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        _check(lib().nvattn_gather_init(self._h, n_ranks, rank, buf), "nvattn_gather_init")
+        return buf.raw
+
+    def gather_connect(self, handles):
+        """handles: every rank's gather_init bytes, in rank order."""
+        blob = b"".join(handles)
+        _check(lib().nvattn_gather_connect(self._h, blob), "nvattn_gather_connect")
+
+    def decode_step_gather(self, layer, q, k, v, q_norm_w, k_norm_w, positions, slots, k_cache,
+                           v_cache, block_tables, context_lens, max_context_len, out,
+                           stream=None, check=True):
+        """decode_step whose output rows also land in every rank's gathered
+        buffer (a collective; see nvattn_paged_decode_step_gather)."""
+        st = lib().nvattn_paged_decode_step_gather(
+            self._h, layer, context_lens.shape[0], _ptr(q), _ptr(k), _ptr(v), _ptr(q_norm_w),
+            _ptr(k_norm_w), _ptr(positions), _ptr(slots), _ptr(k_cache), _ptr(v_cache),
+            _ptr(block_tables), block_tables.shape[1], _ptr(context_lens), int(max_context_len),
+            _ptr(out), _stream_ptr(stream))
+        if check:
+            _check(st, "nvattn_paged_decode_step_gather")
+        return st
+
+    def gather_read(self, step, n_seqs, out, stream=None):
+        """Copies gather step `step`'s rows into out [n_ranks][n_seqs][Hq][128] f32."""
+        _check(lib().nvattn_gather_read(self._h, step, n_seqs, _ptr(out), _stream_ptr(stream)),
+               "nvattn_gather_read")
 
     def decode_step_launches(self, n_seqs, max_context_len):
         """Kernel launches decode_step makes for this batch shape: 1 (fused),

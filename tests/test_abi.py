@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_version_and_status_strings():
-    assert nvattn.version() == (0, 4)
+    assert nvattn.version() == (0, 5)
     for s in range(7):
         assert nvattn.status_string(s)
     assert nvattn.status_string(99) == "unknown status"
