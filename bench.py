@@ -1035,29 +1035,59 @@ def peer_gather_loop(args, world, rank, local_rank, h, peer_step, stream, B, hq,
     its output rows into every rank's gathered buffer as it finishes them,
     then a one-thread launch releases them and waits for the other ranks'.
     The rows of the last step are compared with the NCCL all-gather's (the
-    same step's outputs: equal bit for bit).  The 64-byte IPC handles travel
-    by an NCCL all-gather; every rank runs the same collectives in order."""
+    same step's outputs: equal bit for bit).  The IPC handles travel by an
+    NCCL all-gather.  Every rank runs the same collectives in the same order
+    whether or not its own part failed: a failure (no IPC mapping between the
+    ranks, a release/wait that ran out of time) is reported in the returned
+    dict as "error" instead of ending the run."""
+    import nvattn
     import torch
     import torch.distributed as dist
     device = device_of(nccl_gathered)
-    mine = torch.tensor(list(h.gather_init(world, rank)), dtype=torch.uint8, device=device)
+    err = None
+
+    def agree(ok):
+        flag = torch.tensor([int(ok)], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        return bool(flag.item())
+
+    try:
+        blob = h.gather_init(world, rank)
+    except Exception as e:  # reported; the other ranks learn of it below
+        err, blob = f"gather_init: {e}", bytes(nvattn.IPC_HANDLE_BYTES)
+    mine = torch.tensor(list(blob), dtype=torch.uint8, device=device)
     handles = torch.empty((world, mine.numel()), dtype=torch.uint8, device=device)
     dist.all_gather_into_tensor(handles, mine)
-    hb = handles.cpu().numpy()
-    h.gather_connect([hb[p].tobytes() for p in range(world)])
-    dist.barrier(device_ids=[local_rank])
-    for _ in range(3):
-        peer_step()
-    torch.cuda.synchronize()
+    if err is None:
+        hb = handles.cpu().numpy()
+        try:
+            h.gather_connect([hb[p].tobytes() for p in range(world)])
+        except Exception as e:
+            err = f"gather_connect: {e}"
+    if not agree(err is None):
+        return {"error": err or "another rank could not map the gathered buffers"}
     dist.barrier(device_ids=[local_rank])
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.steps):
-        peer_step()
-    t1.record(stream)
-    torch.cuda.synchronize()
-    h.check_device("peer gather")
-    dist.barrier(device_ids=[local_rank])
+    try:
+        for _ in range(3):
+            peer_step()
+        torch.cuda.synchronize()
+        h.check_device("peer gather warm-up")
+    except Exception as e:
+        err = str(e)
+    if agree(err is None):
+        dist.barrier(device_ids=[local_rank])
+        try:
+            t0.record(stream)
+            for _ in range(args.steps):
+                peer_step()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            h.check_device("peer gather")
+        except Exception as e:
+            err = str(e)
+    if not agree(err is None):
+        return {"error": err or "the release/wait failed on another rank"}
     tv = torch.tensor([t0.elapsed_time(t1) / 1e3], dtype=torch.float64, device=device)
     dist.all_reduce(tv, op=dist.ReduceOp.MAX)
     elapsed = tv.item()

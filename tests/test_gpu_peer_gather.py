@@ -29,5 +29,6 @@ def test_peer_gather_equals_nccl_all_gather():
     ag = d["allgather"]
     assert ag["sharded_parity"]["ok"]
     pg = ag["peer_gather"]
+    assert "error" not in pg, pg["error"]
     assert pg["identical_to_nccl_gather"] is True
     assert pg["ms_per_step"] > 0
