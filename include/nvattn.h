@@ -347,9 +347,16 @@ NVATTN_API nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* 
  *     arguments and results) plus the gather of its output rows; a
  *     collective -- every rank calls it the same number of times, with the
  *     same n_seqs.  Step s (counted per handle from 0) fills parity s & 1.
- *   nvattn_gather_read: copies step `step`'s gathered rows (one of the last
- *     two steps) into out_dev [n_ranks][n_seqs][n_q_heads][head_dim] on the
- *     stream -- rank-major, as an all-gather of the ranks' outputs. */
+ *   nvattn_gather_read: copies step `step`'s gathered rows into out_dev
+ *     [n_ranks][n_seqs][n_q_heads][head_dim] on the stream -- rank-major, as
+ *     an all-gather of the ranks' outputs.  Only the latest step this handle
+ *     took can be read, and only before its next gather step: once every
+ *     rank has released step s, a peer may already run step s + 1 and store
+ *     into the other parity, so step s - 1's rows are no longer stable;
+ *     step s's parity is not written again until this rank has released
+ *     step s + 1, which stream order puts after the read.  Consumers that
+ *     read the gathered buffer directly follow the same rule.
+ *     NVATTN_ERR_INVALID_ARG for any other step. */
 #define NVATTN_IPC_HANDLE_BYTES 128
 NVATTN_API nvattn_status nvattn_gather_init(nvattn_handle* h, int n_ranks, int rank,
                                             void* ipc_handle_out);

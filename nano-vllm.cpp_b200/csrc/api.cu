@@ -668,7 +668,7 @@ nvattn_status nvattn_paged_decode_step_gather(
 nvattn_status nvattn_gather_read(nvattn_handle* h, unsigned step, int n_seqs, float* out_dev,
                                  nvattn_stream_t stream) {
   if (h == nullptr || !h->g_connected || out_dev == nullptr || n_seqs < 0 ||
-      n_seqs > h->cfg.max_seqs || step >= h->g_steps || h->g_steps - step > 2u)
+      n_seqs > h->cfg.max_seqs || h->g_steps == 0u || step != h->g_steps - 1u)
     return NVATTN_ERR_INVALID_ARG;
   if (n_seqs == 0) return NVATTN_OK;
   DeviceGuard guard(h->cfg.device);

@@ -308,7 +308,9 @@ class Handle:
         return st
 
     def gather_read(self, step, n_seqs, out, stream=None):
-        """Copies gather step `step`'s rows into out [n_ranks][n_seqs][Hq][128] f32."""
+        """Copies gather step `step`'s rows into out [n_ranks][n_seqs][Hq][128] f32;
+        `step` must be the latest gather step this handle took, read before
+        its next one."""
         _check(lib().nvattn_gather_read(self._h, step, n_seqs, _ptr(out), _stream_ptr(stream)),
                "nvattn_gather_read")
 
