@@ -578,8 +578,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
-    // rows stored to peers are visible system-wide before the CTA ends
-    if (prm.g_n > 0) __threadfence_system();
+    // rows stored to peers are visible system-wide before the CTA ends; only
+    // the CTAs that wrote final rows (the one split, or the merging one) pay
+    // for the system-scope fence -- the other splits stored nothing off-GPU
+    if (prm.g_n > 0 && (n_splits == 1 || sm.last_split)) __threadfence_system();
   }
 
   tc_fence_before();
