@@ -1033,7 +1033,9 @@ def peer_gather_loop(args, world, rank, local_rank, h, peer_step, stream, B, hq,
     """Third timed loop at N > 1: the decode step with the gather fused over
     peer memory (nvattn_paged_decode_step_gather): each rank's decode stores
     its output rows into every rank's gathered buffer as it finishes them,
-    then a one-thread launch releases them and waits for the other ranks'.
+    and the launch's last CTA to write final rows releases them to every
+    rank and waits for the other ranks' -- one launch for the step and its
+    gather (two where the step's grid takes the store launch first).
     The rows of the last step are compared with the NCCL all-gather's (the
     same step's outputs: equal bit for bit).  The IPC handles travel by an
     NCCL all-gather.  Every rank runs the same collectives in the same order
@@ -1100,7 +1102,8 @@ def peer_gather_loop(args, world, rank, local_rank, h, peer_step, stream, B, hq,
             "e2e_with_gather": {"value": B * args.steps / elapsed, "unit": "tokens/s"},
             "identical_to_nccl_gather": bool(same.item()),
             "note": "decode step whose output rows are stored into every rank's gathered "
-                    "buffer over NVLink, plus one release/wait launch; no NCCL on the data path"}
+                    "buffer over NVLink; its last final-row CTA releases them and waits for "
+                    "the other ranks' (bounded); no NCCL on the data path"}
 
 
 def reassemble_shards(kv_ranks, q_ranks, need):

@@ -325,14 +325,18 @@ NVATTN_API nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* 
 
 /* ---- The decode step with the all-gather of head outputs over peer memory ----
  * KV-head sharding across n_ranks GPUs of one node (one process and one
- * handle per GPU, every handle created with the same max_seqs): rank r's
+ * handle per GPU, every handle created with the same max_seqs; the ranks'
+ * launches wait on one another, so no two ranks share a GPU): rank r's
  * output rows [n_seqs][n_q_heads][head_dim] are the heads of its kv-head
  * share, and o_proj needs every rank's rows.  Instead of a separate
  * all-gather, the decode launch stores each output row into every rank's
  * gathered buffer directly (plain peer-to-peer stores over NVLink, as each
- * row is finished), and a one-thread launch after it releases this rank's
- * rows to all ranks and waits -- bounded, NVATTN_ERR_TIMEOUT after ~2 s --
- * until every rank's rows of the step have arrived.
+ * row is finished); the last CTA of that launch to write final rows then
+ * releases this rank's rows to all ranks and waits -- bounded,
+ * NVATTN_ERR_TIMEOUT after ~2 s -- until every rank's rows of the step have
+ * arrived, so the launch ends with the whole step gathered.  After a
+ * recorded timeout the handle's later launches skip their work and release
+ * nothing, so the other ranks time out as well.
  *   nvattn_gather_init: allocates this rank's gathered buffer
  *     [2][n_ranks][max_seqs][n_q_heads][head_dim] f32 (two step parities)
  *     and a completion counter, and writes their CUDA IPC handle
@@ -347,6 +351,8 @@ NVATTN_API nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* 
  *     arguments and results) plus the gather of its output rows; a
  *     collective -- every rank calls it the same number of times, with the
  *     same n_seqs.  Step s (counted per handle from 0) fills parity s & 1.
+ *     A step with n_seqs = 0 has no decode launch; a one-thread launch
+ *     releases and waits in its place.
  *   nvattn_gather_read: copies step `step`'s gathered rows into out_dev
  *     [n_ranks][n_seqs][n_q_heads][head_dim] on the stream -- rank-major, as
  *     an all-gather of the ranks' outputs.  Only the latest step this handle

@@ -601,6 +601,7 @@ nvattn_status nvattn_gather_init(nvattn_handle* h, int n_ranks, int rank, void* 
   h->g_flag_off = flag_off;
   h->g_peer[rank] = own;
   h->g_steps = 0;
+  h->g_done_total = 0;
   return NVATTN_OK;
 }
 

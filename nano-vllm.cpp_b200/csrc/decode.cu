@@ -92,7 +92,39 @@ struct DecodeParams {
   // the same offset from each g_dst[p] (g_n ranks; 0 = no gather)
   float* g_dst[nvattn_handle::kMaxGatherRanks];
   int g_n;
+  // ...and the step's release/wait (g_done != null): the CTA whose add takes
+  // this rank's final-row count g_done to g_done_target (the last CTA of the
+  // launch to write final rows) adds one to every rank's counter g_flag[p]
+  // and waits until its own counter g_own_flag reaches g_flag_target
+  uint32_t* g_flag[nvattn_handle::kMaxGatherRanks];
+  const uint32_t* g_own_flag;
+  unsigned* g_done;
+  unsigned g_done_target;
+  uint32_t g_flag_target;
 };
+
+// Releases this rank's rows of a gather step to every rank (a sequentially
+// consistent system fence, then a system-scope release add on each rank's
+// counter) and waits until this rank's counter shows every rank's rows of
+// the step.  Bounded: after kWaitLimitNs it records NVATTN_ERR_TIMEOUT
+// (detail = the count reached) and returns.
+__device__ void gather_release_wait(uint32_t* const* flag, int n, const uint32_t* own,
+                                    uint32_t target, DeviceStatus* status) {
+  asm volatile("fence.sc.sys;" ::: "memory");
+  for (int p = 0; p < n; ++p)
+    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag[p]) : "memory");
+  const unsigned long long t0 = global_timer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(own) : "memory");
+    if ((int)(v - target) >= 0) return;
+    if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
+      record_error(status, NVATTN_ERR_TIMEOUT, 80, (long long)v);
+      return;
+    }
+    __nanosleep(64);
+  }
+}
 
 template <int G>
 struct __align__(1024) DecodeSmem {
@@ -580,8 +612,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     // rows stored to peers are visible system-wide before the CTA ends; only
     // the CTAs that wrote final rows (the one split, or the merging one) pay
-    // for the system-scope fence -- the other splits stored nothing off-GPU
-    if (prm.g_n > 0 && (n_splits == 1 || sm.last_split)) __threadfence_system();
+    // for the system-scope fence -- the other splits stored nothing off-GPU.
+    // With the release in the launch, each such CTA then counts itself, and
+    // the last one releases the step's rows to every rank and waits for
+    // theirs: every other CTA of the grid has finished its work by then.
+    if (prm.g_n > 0 && (n_splits == 1 || sm.last_split)) {
+      __threadfence_system();
+      if (prm.g_done != nullptr) {
+        named_barrier_sync(1, 128);
+        if (r == 0 && atomicAdd(prm.g_done, 1u) == prm.g_done_target - 1u)
+          gather_release_wait(prm.g_flag, prm.g_n, prm.g_own_flag, prm.g_flag_target,
+                              prm.status);
+      }
+    }
   }
 
   tc_fence_before();
@@ -695,8 +738,15 @@ static nvattn_status launch_decode_common(nvattn_handle* h, int layer, int n_seq
   prm.tickets = h->decode_tickets;
   prm.status = h->status_dev;
   if (gather != nullptr) {
-    for (int p = 0; p < gather->g_n; ++p) prm.g_dst[p] = gather->g_dst[p];
+    for (int p = 0; p < gather->g_n; ++p) {
+      prm.g_dst[p] = gather->g_dst[p];
+      prm.g_flag[p] = gather->g_flag[p];
+    }
     prm.g_n = gather->g_n;
+    prm.g_own_flag = gather->g_own_flag;
+    prm.g_done = gather->g_done;
+    prm.g_done_target = gather->g_done_target;
+    prm.g_flag_target = gather->g_flag_target;
   }
   if (fused != nullptr && step_check) {
     prm.positions = fused->positions;
@@ -802,28 +852,10 @@ struct GatherSync {
   DeviceStatus* status;
 };
 
-// One thread, after the decode launch in stream order: adds one to every
-// rank's counter with a system-scope release (this rank's rows, fenced by
-// every CTA of that launch, are then visible to each rank that acquires the
-// count), then waits until this rank's counter shows every rank's rows of
-// this step.  Bounded: after kWaitLimitNs it records NVATTN_ERR_TIMEOUT
-// (detail = the count reached) and returns.
+// A step with no sequences has no decode launch to release from: one thread
+// releases and waits instead (gather_release_wait).
 __global__ void gather_sync_kernel(GatherSync g) {
-  if (threadIdx.x != 0) return;
-  asm volatile("fence.sc.sys;" ::: "memory");
-  for (int p = 0; p < g.n; ++p)
-    asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(g.flag[p]) : "memory");
-  const unsigned long long t0 = global_timer_ns();
-  for (uint32_t it = 0;; ++it) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(g.own) : "memory");
-    if ((int)(v - g.target) >= 0) return;
-    if ((it & 63u) == 63u && global_timer_ns() - t0 > kWaitLimitNs) {
-      record_error(g.status, NVATTN_ERR_TIMEOUT, 80, (long long)v);
-      return;
-    }
-    __nanosleep(64);
-  }
+  if (threadIdx.x == 0) gather_release_wait(g.flag, g.n, g.own, g.target, g.status);
 }
 }  // namespace
 
@@ -838,24 +870,40 @@ nvattn_status launch_paged_decode_step_gather(nvattn_handle* h, int layer, int n
                                               cudaStream_t stream) {
   if (!h->g_connected) return NVATTN_ERR_INVALID_ARG;
   const long long parity_off = (long long)(h->g_steps & 1u) * h->g_ranks * h->g_slice;
+  const uint32_t flag_target = (uint32_t)h->g_ranks * (h->g_steps + 1u);
+  uint32_t* own_flag = reinterpret_cast<uint32_t*>(h->g_own + h->g_flag_off);
+  if (n_seqs == 0) {
+    GatherSync gs = {};
+    for (int p = 0; p < h->g_ranks; ++p)
+      gs.flag[p] = reinterpret_cast<uint32_t*>(h->g_peer[p] + h->g_flag_off);
+    gs.own = own_flag;
+    gs.n = h->g_ranks;
+    gs.target = flag_target;
+    gs.status = h->status_dev;
+    gather_sync_kernel<<<1, 32, 0, stream>>>(gs);
+    if (cudaGetLastError() != cudaSuccess) return NVATTN_ERR_CUDA;
+    ++h->g_steps;
+    return NVATTN_OK;
+  }
+  // One CTA per (sequence, kv head) writes that pair's final rows; the
+  // count runs on across steps (compared modulo 2^32), so nothing re-arms it.
+  const unsigned done_target = h->g_done_total + (unsigned)n_seqs * (unsigned)h->cfg.n_kv_heads;
   DecodeParams gd = {};
   gd.g_n = h->g_ranks;
-  for (int p = 0; p < h->g_ranks; ++p)
+  for (int p = 0; p < h->g_ranks; ++p) {
     gd.g_dst[p] = reinterpret_cast<float*>(h->g_peer[p]) + parity_off +
                   (long long)h->g_rank * h->g_slice;
+    gd.g_flag[p] = reinterpret_cast<uint32_t*>(h->g_peer[p] + h->g_flag_off);
+  }
+  gd.g_own_flag = own_flag;
+  gd.g_done = reinterpret_cast<unsigned*>(h->g_own + h->g_flag_off + nvattn_handle::kGatherDoneOffset);
+  gd.g_done_target = done_target;
+  gd.g_flag_target = flag_target;
   nvattn_status st = decode_step_impl(h, layer, n_seqs, q, k_new, v_new, q_norm_w, k_norm_w,
                                       positions, slots, k_cache, v_cache, block_tables,
                                       max_blocks, context_lens, max_context_len, out, &gd, stream);
   if (st != NVATTN_OK) return st;
-  GatherSync gs = {};
-  for (int p = 0; p < h->g_ranks; ++p)
-    gs.flag[p] = reinterpret_cast<uint32_t*>(h->g_peer[p] + h->g_flag_off);
-  gs.own = reinterpret_cast<uint32_t*>(h->g_own + h->g_flag_off);
-  gs.n = h->g_ranks;
-  gs.target = (uint32_t)h->g_ranks * (h->g_steps + 1u);
-  gs.status = h->status_dev;
-  gather_sync_kernel<<<1, 32, 0, stream>>>(gs);
-  if (cudaGetLastError() != cudaSuccess) return NVATTN_ERR_CUDA;
+  h->g_done_total = done_target;
   ++h->g_steps;
   return NVATTN_OK;
 }

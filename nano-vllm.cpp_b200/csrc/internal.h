@@ -51,6 +51,9 @@ struct nvattn_handle {
   // g_flag_off, the completion counter; g_peer[p] is rank p's allocation
   // mapped on this device (g_peer[g_rank] == g_own)
   static constexpr int kMaxGatherRanks = 8;
+  // byte offset, from the completion counter, of this rank's count of the
+  // decode CTAs that have written final rows (zeroed with the counter)
+  static constexpr size_t kGatherDoneOffset = 64;
   int g_ranks = 0, g_rank = 0;
   long long g_slice = 0;  // floats per rank: max_seqs * n_q_heads * head_dim
   size_t g_flag_off = 0;
@@ -58,6 +61,9 @@ struct nvattn_handle {
   char* g_peer[kMaxGatherRanks] = {};
   bool g_connected = false;
   unsigned g_steps = 0;   // gather steps issued on this handle
+  // final-row CTAs counted so far at g_flag_off + kGatherDoneOffset (the
+  // decode launch's last one releases the step's rows)
+  unsigned g_done_total = 0;
 
   // TMA descriptor cache: fixed storage, replaced round-robin once full, so
   // an entry never moves while the handle lives.
