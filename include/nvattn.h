@@ -344,9 +344,9 @@ NVATTN_API nvattn_status nvattn_paged_decode_step_launches(const nvattn_handle* 
  *   nvattn_gather_connect: ipc_handles = every rank's handle, rank order
  *     (n_ranks x NVATTN_IPC_HANDLE_BYTES bytes, exchanged by the caller);
  *     maps every peer's buffer on this device.  NVATTN_ERR_INVALID_ARG if a
- *     handle's rank count, rank or buffer shape differs from this rank's.  All ranks connect before any
- *     rank takes a gather step, and no rank destroys its handle while
- *     another may still store to it.
+ *     handle's rank count, rank or buffer shape differs from this rank's.
+ *     All ranks connect before any rank takes a gather step, and no rank
+ *     destroys its handle while another may still store to it.
  *   nvattn_paged_decode_step_gather: nvattn_paged_decode_step (same
  *     arguments and results) plus the gather of its output rows; a
  *     collective -- every rank calls it the same number of times, with the

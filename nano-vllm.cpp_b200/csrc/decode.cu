@@ -896,7 +896,8 @@ nvattn_status launch_paged_decode_step_gather(nvattn_handle* h, int layer, int n
     gd.g_flag[p] = reinterpret_cast<uint32_t*>(h->g_peer[p] + h->g_flag_off);
   }
   gd.g_own_flag = own_flag;
-  gd.g_done = reinterpret_cast<unsigned*>(h->g_own + h->g_flag_off + nvattn_handle::kGatherDoneOffset);
+  gd.g_done =
+      reinterpret_cast<unsigned*>(h->g_own + h->g_flag_off + nvattn_handle::kGatherDoneOffset);
   gd.g_done_target = done_target;
   gd.g_flag_target = flag_target;
   nvattn_status st = decode_step_impl(h, layer, n_seqs, q, k_new, v_new, q_norm_w, k_norm_w,
