@@ -70,6 +70,18 @@ def test_null_handle_is_rejected():
     assert L.nvattn_destroy(None) == nvattn.OK
 
 
+def test_gather_entry_points_reject_a_null_handle():
+    """The peer-memory gather's entry points check their handle before any
+    device work: a null handle is an argument error."""
+    L = nvattn.lib()
+    buf = ctypes.create_string_buffer(nvattn.IPC_HANDLE_BYTES * 2)
+    assert L.nvattn_gather_init(None, 2, 0, buf) == nvattn.ERR_INVALID_ARG
+    assert L.nvattn_gather_connect(None, buf) == nvattn.ERR_INVALID_ARG
+    assert L.nvattn_paged_decode_step_gather(None, 0, 1, *([None] * 10), 1, None, 1, None,
+                                             None) == nvattn.ERR_INVALID_ARG
+    assert L.nvattn_gather_read(None, 0, 1, None, None) == nvattn.ERR_INVALID_ARG
+
+
 def reference_prepare_inputs(seq_lens, num_cached, block_tables, bs=256):
     """ModelRunner::PrepareInputs + the StorePrefillKV slot formula, in Python."""
     positions, slots, cu = [], [], [0]
