@@ -119,7 +119,11 @@ NVATTN_API void nvattn_version(int* major, int* minor);
 
 /* Synchronises the handle's device, returns the first error recorded by a
  * kernel since the last call (NVATTN_OK if none) and clears it.  *detail
- * (nullable) receives the offending value (block id, slot or wait site). */
+ * (nullable) receives the offending value (block id, slot or wait site).
+ * Reporting NVATTN_ERR_TIMEOUT also re-arms the handle's split tickets and
+ * prefill work counter, and ends its peer-memory gather (later
+ * nvattn_paged_decode_step_gather / nvattn_gather_read calls return
+ * NVATTN_ERR_INVALID_ARG; every rank destroys its handle and starts over). */
 NVATTN_API nvattn_status nvattn_get_error(nvattn_handle* h, int64_t* detail);
 
 /* ---- host-side planning (no device work) ------------------------------- */

@@ -262,6 +262,10 @@ nvattn_status nvattn_get_error(nvattn_handle* h, int64_t* detail) {
                   (size_t)h->cfg.max_seqs * h->cfg.n_kv_heads * sizeof(int)) != cudaSuccess ||
        cudaMemset(h->prefill_sched_dev, 0, 2 * sizeof(int)) != cudaSuccess))
     return NVATTN_ERR_CUDA;
+  // ...and ends the peer-memory gather: the ranks' step counters and this
+  // rank's count of final-row CTAs no longer agree, so a later step could
+  // not tell when every rank's rows have arrived.
+  if (st.code == NVATTN_ERR_TIMEOUT) h->g_connected = false;
   if (detail) *detail = st.detail;
   return (nvattn_status)st.code;
 }
